@@ -1,0 +1,490 @@
+"""Benchmark of the B200 xtile backend (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl b200|reference]
+
+Workloads are the BASELINE configurations (synthetic, seeded inputs):
+
+  add             fp32 [2048,2048] + [2048,2048], 32x64 Block tiles, grid (64,32)
+  softmax         fp32 [8192,1024] row softmax, 1x1024 Block tiles, grid (8192,)
+  matmul          bf16 4096^3, fp32 out, 128x128 Block tiles, K-step 64, grid (32,32)
+  conv2d          NHWC bf16 [32,56,56,64] * [3,3,64,64], pad 1, fp32 out
+  sharded_matmul  bf16 [32768,8192] x [8192,8192], fp32 out, 256x128 Block tiles,
+                  grid (128,64) split along bid0 across ranks, output rows
+                  gathered to rank 0 over NCCL (the default workload)
+
+A step is one launch of the workload's Block program over its whole Grid
+(for sharded_matmul: every rank's share plus the gather).  ``value`` is the
+whole-job throughput with inputs resident in HBM; ``e2e`` repeats the step
+through the public ``xtile.launch`` API with pinned host inputs copied in and
+the result copied out inside the timed region.  ``--impl reference`` times the
+reference path on the host CPU instead: the reference (sjjeong94/xtile)
+executes nothing, so its arm is the CPU oracle restating its semantics
+(``oracle/xt_oracle.py``) on a bounded sample of the workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "TFLOP/s (matmul/conv) & HBM GB/s (add/softmax) vs B200 peak, 1–8 GPUs"
+L2_BYTES = 126 * 2 ** 20
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+# DRAM bytes per launch of the dominant kernel from one ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum), summarised in profiles/.
+NCU_TRAFFIC_BYTES: dict[str, float] = {}
+
+
+# ---------------------------------------------------------------- workloads
+def build_workload(name: str, xt, torch, world: int, rank: int):
+    """Returns (module, host input tensors, output index, ...) for ``name``."""
+    g = torch.Generator().manual_seed
+    A = xt.Array
+    if name == "add":
+        @xt.kernel
+        def add_tiles(lhs, rhs, out, th, tw):
+            i, j = xt.bid(0), xt.bid(1)
+            a = xt.load(lhs, index=(i, j), shape=(th, tw))
+            b = xt.load(rhs, index=(i, j), shape=(th, tw))
+            xt.store(out, index=(i, j), tile=a + b)
+
+        gen = g(0)
+        a = torch.rand(2048, 2048, generator=gen) * 2 - 1
+        b = torch.rand(2048, 2048, generator=gen) * 2 - 1
+        args = (A((2048, 2048), xt.float32),) * 3
+        mod = xt.convert(add_tiles, args=(*args, 32, 64), grid=(64, 32, 1), double_buffering=True)
+        return dict(module=mod, inputs=[a, b], out_shape=(2048, 2048), out_dtype=torch.float32,
+                    unit="GB/s", bound="hbm", dtype="f32",
+                    config={"workload": "add", "shape": [2048, 2048], "block_tile": [32, 64],
+                            "grid": [64, 32, 1]})
+    if name == "softmax":
+        @xt.kernel
+        def softmax_rows(inp, out, trow, col):
+            i = xt.bid(0)
+            x = xt.load(inp, index=(i, 0), shape=(trow, col))
+            x = x - xt.max(x, axis=-1)
+            x = xt.exp(x)
+            xt.store(out, index=(i, 0), tile=x / xt.sum(x, axis=-1))
+
+        x = torch.randn(8192, 1024, generator=g(1)) * 4
+        mod = xt.convert(softmax_rows, args=(A((8192, 1024), xt.float32), A((8192, 1024), xt.float32),
+                                             1, 1024), grid=(8192, 1, 1), double_buffering=True)
+        return dict(module=mod, inputs=[x], out_shape=(8192, 1024), out_dtype=torch.float32,
+                    unit="GB/s", bound="hbm", dtype="f32",
+                    config={"workload": "softmax", "shape": [8192, 1024], "block_tile": [1, 1024],
+                            "grid": [8192, 1, 1]})
+    if name in ("matmul", "sharded_matmul"):
+        if name == "matmul":
+            M = N = K = 4096
+            tm, tn, tk, seed = 128, 128, 64, 2
+        else:
+            M, N, K = 32768, 8192, 8192
+            tm, tn, tk, seed = 256, 128, K, 4
+
+        @xt.kernel
+        def matmul_kloop(lhs, rhs, out, tm, tn, tk, ksteps):
+            i, j = xt.bid(0), xt.bid(1)
+            acc = None
+            for k in range(ksteps):
+                p = xt.matmul(xt.load(lhs, index=(i, k), shape=(tm, tk)),
+                              xt.load(rhs, index=(k, j), shape=(tk, tn), shared=1))
+                acc = p if acc is None else acc + p
+            xt.store(out, index=(i, j), tile=acc)
+
+        gen = g(seed)
+        s = 1.0 / (K ** 0.5)
+        a = (torch.randn(M, K, generator=gen) * s).to(torch.bfloat16)
+        b = (torch.randn(K, N, generator=gen) * s).to(torch.bfloat16)
+        grid = (M // tm, N // tn, 1)
+        mod = xt.convert(matmul_kloop, args=(A((M, K), xt.bfloat16), A((K, N), xt.bfloat16),
+                                             A((M, N), xt.float32), tm, tn, tk, K // tk),
+                         grid=grid, double_buffering=True)
+        cfg = {"workload": name, "M": M, "N": N, "K": K, "block_tile": [tm, tn], "k_step": tk,
+               "grid": list(grid)}
+        if name == "sharded_matmul":
+            cfg["parallelism"] = f"bid0 split over {world} GPU(s), NCCL gather of C rows to rank 0"
+        return dict(module=mod, inputs=[a, b], out_shape=(M, N), out_dtype=torch.float32,
+                    unit="TFLOP/s", bound="tensor", dtype="bf16", config=cfg, sharded=name == "sharded_matmul")
+    if name == "conv2d":
+        @xt.kernel
+        def conv2d_bf16(inp, filt, out, tile_h, tile_w, cin, cout, kh, kw):
+            n, h, w = xt.bid(0), xt.bid(1), xt.bid(2)
+            f = xt.load(filt, index=(0, 0, 0, 0), shape=(kh, kw, cin, cout), shared=2)
+            y = xt.load_conv2d(inp, f, index=(n, h, w, 0), shape=(1, tile_h, tile_w, cout), group=1,
+                               pad=(kh // 2, kw // 2, kh // 2, kw // 2), stride=(1, 1), dilation=(1, 1))
+            xt.store(out, index=(n, h, w, 0), tile=y)
+
+        gen = g(3)
+        x = (torch.randn(32, 56, 56, 64, generator=gen) * 0.1).to(torch.bfloat16)
+        f = (torch.randn(3, 3, 64, 64, generator=gen) * 0.1).to(torch.bfloat16)
+        mod = xt.convert(conv2d_bf16, args=(A((32, 56, 56, 64), xt.bfloat16), A((3, 3, 64, 64), xt.bfloat16),
+                                            A((32, 56, 56, 64), xt.float32), 8, 56, 64, 64, 3, 3),
+                         grid=(32, 7, 1), double_buffering=True)
+        return dict(module=mod, inputs=[x, f], out_shape=(32, 56, 56, 64), out_dtype=torch.float32,
+                    unit="TFLOP/s", bound="tensor", dtype="bf16",
+                    config={"workload": "conv2d", "input": [32, 56, 56, 64], "filter": [3, 3, 64, 64],
+                            "pad": 1, "block_tile": [1, 8, 56, 64], "grid": [32, 7, 1]})
+    raise SystemExit(f"unknown workload {name}")
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu = gpu_id
+        self.proc = None
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.25)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        sm = [float(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3][0].isdigit())}
+
+
+# ---------------------------------------------------------------- helpers
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except ValueError:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def cpu_baseline(w: dict, xt, torch, budget_s: float = 12.0) -> dict:
+    """Times the CPU oracle on a bounded sample of the workload's Blocks."""
+    import numpy as np
+    from oracle import xt_oracle
+
+    module = w["module"]
+    text = xt._module_asm(module)
+    func = xt_oracle.parse_module(text)[0]
+    order = xt_oracle.serialize_order(func.grid)
+    arrays = []
+    for t in w["inputs"]:
+        arrays.append(t.view(torch.uint16).numpy() if t.dtype == torch.bfloat16 else t.numpy())
+    out = np.zeros(w["out_shape"], dtype=np.float32)
+    arrays.append(out)
+    plan = module.plan()
+    work = plan["flops"] if w["unit"] == "TFLOP/s" else plan["bytes"]
+    interp = xt_oracle.Interpreter(func)
+    done = 0
+    t0 = time.perf_counter()
+    rng = np.random.default_rng(0)
+    picks = rng.permutation(len(order))
+    interp.run(arrays, blocks=[])  # binds arrays
+    while done < len(order) and time.perf_counter() - t0 < budget_s:
+        interp.run_block(order[picks[done]])
+        done += 1
+    dt = time.perf_counter() - t0
+    per_block = work / len(order)
+    value = per_block * done / dt / (1e12 if w["unit"] == "TFLOP/s" else 1e9)
+    threads = torch.get_num_threads()
+    return {"value": value, "unit": w["unit"], "cores": threads, "kind": "port",
+            "sample": f"{done} of {len(order)} Blocks in {dt:.1f} s (numpy oracle, BLAS threads={threads})"}
+
+
+def nccl_gather(out, rows_per_rank, world, rank, dist):
+    if world == 1:
+        return
+    mine = out[rank * rows_per_rank:(rank + 1) * rows_per_rank]
+    if rank == 0:
+        dist.gather(mine, gather_list=[out[r * rows_per_rank:(r + 1) * rows_per_rank] for r in range(world)], dst=0)
+    else:
+        dist.gather(mine, dst=0)
+
+
+# ---------------------------------------------------------------- main
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="sharded_matmul",
+                    choices=["add", "softmax", "matmul", "conv2d", "sharded_matmul"])
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    import torch
+
+    if args.impl == "reference":
+        run_reference(args, world, rank, torch)
+        return
+
+    import xtile as xt
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    w = build_workload(args.workload, xt, torch, world, rank)
+    mod = w["module"]
+    plan = mod.plan()
+    grid0 = plan["grid"][0]
+    sharded = w.get("sharded", False)
+    if world > 1 and not sharded:
+        # not a sharded configuration: every rank runs an independent replica
+        w["config"]["parallelism"] = f"{world} independent replicas"
+    lo, hi = (rank * grid0 // world, (rank + 1) * grid0 // world) if sharded else (0, grid0)
+    rows_per_rank = w["out_shape"][0] // world if sharded else 0
+
+    # device-resident inputs; rotate enough sets to defeat the 126 MB L2
+    inputs_dev = [t.to(dev) for t in w["inputs"]]
+    out = torch.empty(w["out_shape"], dtype=w["out_dtype"], device=dev)
+    ws_bytes = sum(t.numel() * t.element_size() for t in inputs_dev) + out.numel() * out.element_size()
+    n_sets = 1 if ws_bytes > 3 * L2_BYTES else int(-(-3 * L2_BYTES // ws_bytes)) + 1
+    sets = [(inputs_dev, out)] + [([t.clone() for t in inputs_dev], torch.empty_like(out))
+                                  for _ in range(n_sets - 1)]
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        ins, o = sets[i % n_sets]
+        xt.launch(mod, *ins, o, bid0_range=(lo, hi))
+
+    for i in range(args.warmup):
+        step(i)
+        if sharded:
+            nccl_gather(sets[i % n_sets][1], rows_per_rank, world, rank, dist)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+
+    # ---- timed region: K steps, per-launch events for the kernel roofline
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    t_begin = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    uuid = str(getattr(torch.cuda.get_device_properties(dev), "uuid", local))
+    gpu_id = uuid if uuid.startswith("GPU-") or uuid.isdigit() else f"GPU-{uuid}"
+    with ClockSampler(gpu_id) as clocks:
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        t_begin.record(stream)
+        for i in range(args.steps):
+            starts[i].record(stream)
+            step(i)
+            ends[i].record(stream)
+            if sharded:
+                nccl_gather(sets[i % n_sets][1], rows_per_rank, world, rank, dist)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+    total_ms = t_begin.elapsed_time(t_end)
+    kernel_ms = statistics.fmean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    if dist:
+        t = torch.tensor([total_ms, kernel_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, kernel_ms = t.tolist()
+    clock = clocks.summary()
+    err = xt.device_error()
+
+    # ---- compute-only timing (sharded: no gather), for the scaling report
+    compute = None
+    if sharded and world > 1:
+        c0 = torch.cuda.Event(enable_timing=True)
+        c1 = torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        c0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        c1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([c0.elapsed_time(c1) / args.steps], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        compute = t.item()
+
+    # ---- end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        host_in = [t.pin_memory() for t in w["inputs"]]
+        if sharded:
+            rows = w["inputs"][0].shape[0] // world
+            host_in[0] = host_in[0][rank * rows:(rank + 1) * rows]
+        host_out = torch.empty(w["out_shape"] if (rank == 0 or not sharded) else (0,), dtype=w["out_dtype"]).pin_memory()
+        ins, o = sets[0]
+        h2d = sum(t.numel() * t.element_size() for t in host_in)
+        d2h = host_out.numel() * host_out.element_size()
+        e_steps = max(3, min(args.steps, 10))
+
+        def e2e_step():
+            if sharded:
+                ins[0][lo * (w["out_shape"][0] // grid0):hi * (w["out_shape"][0] // grid0)].copy_(
+                    host_in[0], non_blocking=True)
+                ins[1].copy_(host_in[1], non_blocking=True)
+            else:
+                for d, h in zip(ins, host_in):
+                    d.copy_(h, non_blocking=True)
+            xt.launch(mod, *ins, o, bid0_range=(lo, hi))
+            if sharded:
+                nccl_gather(o, rows_per_rank, world, rank, dist)
+            if host_out.numel():
+                host_out.copy_(o, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = e0.elapsed_time(e1) / e_steps
+        if dist:
+            t = torch.tensor([e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = t.item()
+        e2e = (e_ms, h2d, d2h)
+
+    if dist:
+        dist.barrier()
+    if rank != 0:
+        dist.destroy_process_group()
+        return
+
+    # ---- report
+    peaks, peak_kind = load_peaks()
+    work = plan["flops"] if w["unit"] == "TFLOP/s" else plan["bytes"]
+    scale = 1e12 if w["unit"] == "TFLOP/s" else 1e9
+    job_units = work if (sharded or world == 1) else work * world
+    ms_per_step = total_ms / args.steps
+    value = job_units / (ms_per_step * 1e-3) / scale
+    # one launch processes this rank's share of the Grid
+    launch_work = work * (hi - lo) / grid0
+    achieved = launch_work / (kernel_ms * 1e-3) / scale
+    if w["bound"] == "hbm":
+        peak = peaks["hbm_gbs"]
+        achieved_r = launch_work / (kernel_ms * 1e-3) / 1e9
+        roof_unit = "GB/s"
+    else:
+        peak = peaks["bf16_tflops"]
+        achieved_r = achieved
+        roof_unit = "TFLOP/s"
+    line = {
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": w["unit"],
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True,
+        "scaling": "strong" if sharded else "weak",
+        "vs_baseline": None,
+        "dtype": w["dtype"],
+        "data": "synthetic (seeded torch.Generator inputs of the BASELINE shapes)",
+        "config": {**w["config"], "l2": f"{n_sets} rotating input/output sets" if n_sets > 1
+                   else "working set larger than L2"},
+        "roofline": {"bound": w["bound"], "achieved": round(achieved_r, 2), "peak": peak, "unit": roof_unit,
+                     "frac": round(achieved_r / peak, 4), "peak_kind": f"{peak_kind} (burst)",
+                     "traffic": NCU_TRAFFIC_BYTES.get(args.workload),
+                     "kernel_ms": round(kernel_ms, 4)},
+        "clocks": clock,
+        "gpu_launches": args.steps,
+        "device_error": err,
+    }
+    if compute is not None:
+        line["compute_only"] = {"ms_per_step": round(compute, 4),
+                                "value": round(work / (compute * 1e-3) / scale, 3)}
+        line["gather"] = {"ms_per_step": round(ms_per_step - compute, 4),
+                          "bytes": (world - 1) * rows_per_rank * w["out_shape"][1] * 4}
+    if e2e is not None:
+        e_ms, h2d, d2h = e2e
+        line["e2e"] = {"value": round(job_units / (e_ms * 1e-3) / scale, 3), "unit": w["unit"],
+                       "ms_per_step": round(e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+    if not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(w, xt, torch)
+    print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+
+
+def run_reference(args, world: int, rank: int, torch) -> None:
+    """Reference arm: the CPU oracle (the reference executes nothing itself)."""
+    if rank != 0:
+        return
+    import xtile as xt
+
+    w = build_workload(args.workload, xt, torch, 1, 0)
+    samples = []
+    for i in range(args.warmup + args.steps):
+        b = cpu_baseline(w, xt, torch, budget_s=max(1.0, 60.0 / (args.warmup + args.steps)))
+        if i >= args.warmup:
+            samples.append(b)
+    value = statistics.fmean(s["value"] for s in samples)
+    base = samples[-1]
+    line = {
+        "metric": METRIC, "impl": "reference", "value": round(value, 6), "unit": w["unit"], "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "scaling": "strong" if w.get("sharded") else "weak", "vs_baseline": None, "dtype": w["dtype"],
+        "data": "synthetic (seeded torch.Generator inputs of the BASELINE shapes)", "config": w["config"],
+        "cpu_baseline": {"value": round(value, 6), "unit": w["unit"], "cores": base["cores"],
+                         "kind": "port", "sample": base["sample"]},
+        "e2e": {"value": round(value, 6), "unit": w["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference (sjjeong94/xtile) compiles to NPU command IR and executes nothing; this arm "
+                "times the CPU oracle that restates its semantics on a bounded sample of Blocks",
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

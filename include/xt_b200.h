@@ -1,0 +1,125 @@
+/* C ABI of the B200 xtile backend (libxt_b200.so).
+ *
+ * The reference exposes its compiler to Python through one nanobind module,
+ * ``_xtile`` (python/XTModule.cpp:210-231): parse, seven pass thunks,
+ * _parse_module and _module_asm, with MLIR modules owned by PyCapsules.  This
+ * header is the same surface as plain C: an opaque module handle, the same
+ * pass names, and -- new, since the reference cannot execute anything --
+ * planning and launching a module's Block program on a B200.
+ *
+ * Conventions
+ *  - Every call returns an int status: XT_OK (0) or one of the XT_E* codes.
+ *    The message of the last failure on the calling thread is returned by
+ *    xt_last_error() (replaces the exceptions raised at
+ *    python/XTModule.cpp:119 (parse), :41,50 (type) and :135-148 (passes)).
+ *  - Device buffers are borrowed: the caller allocates them (any allocator),
+ *    keeps them alive until the launch's stream has finished, and owns the
+ *    results, which are written in place (xt.store into a mutable Array).
+ *  - Arrays are dense row-major with the exact shape and element type of the
+ *    kernel's memref arguments; device pointers must be 16-byte aligned.
+ *  - Launches are asynchronous on the given CUDA stream (NULL: legacy default
+ *    stream) on the device current on the calling thread.  xt_launch may be
+ *    called from several threads, one device per thread.
+ */
+#ifndef XT_B200_H
+#define XT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct xt_module xt_module;
+
+enum {
+  XT_OK = 0,
+  XT_EPARSE = 1,       /* text is not valid xt (reference: ValueError) */
+  XT_EVERIFY = 2,      /* an op verifier failed (reference: parse fails) */
+  XT_EPASS = 3,        /* a stage failed (reference: RuntimeError) */
+  XT_EUNSUPPORTED = 4, /* no B200 kernel family implements the program */
+  XT_EARGUMENT = 5,    /* bad argument to a call (count, null, range) */
+  XT_ECUDA = 6,        /* a CUDA runtime / driver call failed */
+  XT_ETYPE = 7,        /* wrong handle type (reference: TypeError) */
+  XT_EDEVICE = 8       /* a kernel reported an error word (bounded wait ran out) */
+};
+
+/* Kernel families a Block program maps onto. */
+enum { XT_FAMILY_EW = 1, XT_FAMILY_ROWS = 2, XT_FAMILY_GEMM = 3, XT_FAMILY_CONV = 4 };
+
+typedef struct xt_plan_info {
+  int family;           /* XT_FAMILY_* */
+  int n_args;           /* memref arguments of the function, in signature order */
+  int64_t grid[3];      /* xt.grid */
+  int64_t bid0_extent;  /* grid[0]: the range xt_launch's bid0 bounds select from */
+  int64_t m, n, k;      /* gemm/conv: covered GEMM extents; ew: elements; rows: rows, cols */
+  double flops;         /* algorithmic FLOPs of one full launch (0 for ew/rows) */
+  double bytes;         /* algorithmic bytes moved by one full launch */
+} xt_plan_info;
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* xt_last_error(void);
+
+/* Parses and verifies xt text (a ``module { ... }`` or bare func.func ops).
+ * Replaces parseModule, python/XTModule.cpp:112-126. */
+int xt_parse(const char* text, xt_module** out);
+
+/* Frees a module (the capsule destructor, python/XTModule.cpp:88-100). */
+void xt_module_free(xt_module* module);
+
+/* Prints the module at its current stage into a malloc'ed string the caller
+ * frees with xt_string_free.  Replaces _module_asm, python/XTModule.cpp:228-230. */
+int xt_module_asm(const xt_module* module, char** out_text);
+void xt_string_free(char* text);
+
+/* Runs one stage in place.  ``pass`` is one of the reference's names:
+ * "xt_serialize", "xt_to_nova", "nova_optimize", "nova_threading",
+ * "nova_barrier", "nova_allocate", "nova_to_x1" (python/XTModule.cpp:153-206,
+ * pipeline order xtile/__init__.py:160-168).  xt_serialize unrolls the grid
+ * for the dump (lib/xt/XTSerialize.cpp semantics); the later stages annotate
+ * the B200 kernel plan.  Launching never depends on the stage. */
+int xt_run_pass(xt_module* module, const char* pass);
+
+/* Number of functions and the name of function ``index``. */
+int xt_num_funcs(const xt_module* module, int* out_count);
+int xt_func_name(const xt_module* module, int index, const char** out_name);
+
+/* Element types of memref arguments. */
+enum { XT_ELEM_F32 = 0, XT_ELEM_BF16 = 1, XT_ELEM_I8 = 2, XT_ELEM_OTHER = 3 };
+
+typedef struct xt_arg_info {
+  const char* name;     /* argument name without '%' (valid while the module lives) */
+  int is_memref;        /* 0 for tensor / scalar arguments (not launchable) */
+  int elem;             /* XT_ELEM_* */
+  int rank;
+  int64_t shape[8];
+} xt_arg_info;
+
+/* Arguments of ``func`` (NULL: the first function), in signature order: the
+ * arrays xt_launch expects.  Mirrors the memref signature the DSL prints
+ * (reference xtile/dsl.py:491-495). */
+int xt_func_num_args(const xt_module* module, const char* func, int* out_count);
+int xt_func_arg(const xt_module* module, const char* func, int index, xt_arg_info* out);
+
+/* Maps function ``func`` (NULL: the first one) onto a kernel family. */
+int xt_plan(const xt_module* module, const char* func, xt_plan_info* out);
+
+/* Runs the Block program of ``func`` (NULL: the first) for the Blocks with
+ * bid0 in [bid0_begin, bid0_end) -- all Blocks when bid0_end <= 0 -- on
+ * ``stream``.  ``args`` holds one device pointer per memref argument in
+ * signature order, ``n_args`` of them.  Used by one process per GPU to split
+ * a Grid along bid0.  Allocates a small per-device workspace (error word,
+ * scheduler counters) with cudaMalloc on the first launch on each device. */
+int xt_launch(const xt_module* module, const char* func, void* const* args, int n_args,
+              int64_t bid0_begin, int64_t bid0_end, void* stream);
+
+/* Reads and clears the error word the kernels on the current device set when
+ * a bounded wait runs out (0: none).  Synchronizes the device. */
+int xt_device_error(uint32_t* out_code);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* XT_B200_H */

@@ -1,0 +1,311 @@
+"""GPU parity: every kernel family against the CPU oracle, through the public
+API (xtile.launch -> _xtile -> libxt_b200.so C ABI -> sm_100a kernels).
+
+Tolerances (fixed up front):
+* f32 add/sub/mul, int8 matmul with its f32 epilogue: bit-exact;
+* row softmax: max elementwise |gpu - ref| / ref <= 1e-5;
+* bf16 matmul / conv (f32 accumulation): max|gpu - ref| / max|ref| <= 1e-2
+  and |gpu - ref| <= 1e-2 |ref| + 1e-2 rms(ref) per element.
+Full-size configurations are checked on a seeded sample of Blocks.
+"""
+import numpy as np
+import pytest
+import torch
+
+import xtile as xt
+from oracle import xt_oracle
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0") if torch.cuda.is_available() else None
+
+
+def gen(seed):
+    return torch.Generator().manual_seed(seed)
+
+
+def host(t):
+    t = t.detach().cpu()
+    return t.view(torch.uint16).numpy() if t.dtype == torch.bfloat16 else t.numpy()
+
+
+def oracle(module, arrays, blocks=None):
+    outs = [host(a).copy() for a in arrays]
+    xt_oracle.run(xt._module_asm(module), outs, blocks=blocks)
+    return outs
+
+
+def bf16_close(got, ref):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    scale = np.max(np.abs(ref))
+    rms = np.sqrt(np.mean(ref ** 2))
+    assert np.max(np.abs(got - ref)) / scale <= 1e-2
+    assert np.all(np.abs(got - ref) <= 1e-2 * np.abs(ref) + 1e-2 * rms)
+
+
+@pytest.fixture(autouse=True)
+def no_device_errors():
+    yield
+    assert xt.device_error() == 0
+
+
+# ------------------------------------------------------------------- add
+@xt.kernel
+def add_tiles(lhs, rhs, out, th, tw):
+    i, j = xt.bid(0), xt.bid(1)
+    a = xt.load(lhs, index=(i, j), shape=(th, tw))
+    b = xt.load(rhs, index=(i, j), shape=(th, tw))
+    xt.store(out, index=(i, j), tile=a + b)
+
+
+@xt.kernel
+def add_rows(lhs, rhs, out, trow, col):
+    i = xt.bid(0)
+    a = xt.load(lhs, index=(i, 0), shape=(trow, col))
+    b = xt.load(rhs, index=(i, 0), shape=(trow, col))
+    xt.store(out, index=(i, 0), tile=a + b)
+
+
+def test_add_config1_bit_exact():
+    g = gen(0)
+    a = torch.rand(2048, 2048, generator=g) * 2 - 1
+    b = torch.rand(2048, 2048, generator=g) * 2 - 1
+    c = torch.empty(2048, 2048, device=DEV)
+    m = xt.run(add_tiles, args=(a.to(DEV), b.to(DEV), c, 32, 64), grid=(64, 32, 1))
+    ref = oracle(m, [a, b, torch.zeros(2048, 2048)])[2]
+    assert np.array_equal(host(c).view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("shape,trow", [((128, 128), 64), ((101, 37), 64), ((7, 3), 4)])
+def test_add_rows_ragged(shape, trow):
+    g = gen(1)
+    a = torch.randn(*shape, generator=g)
+    b = torch.randn(*shape, generator=g)
+    c = torch.full(shape, float("nan"), device=DEV)
+    grid = ((shape[0] + trow - 1) // trow, 1, 1)
+    m = xt.run(add_rows, args=(a.to(DEV), b.to(DEV), c, trow, shape[1]), grid=grid)
+    ref = oracle(m, [a, b, torch.zeros(shape)])[2]
+    assert np.array_equal(host(c).view(np.uint32), ref.view(np.uint32))
+
+
+def test_add_subnormals_and_specials_bit_exact():
+    vals = torch.tensor([1e-45, -1e-45, 1e-38, float("inf"), -float("inf"), 0.0, -0.0, 3.0e38])
+    a = vals.repeat(16, 1)
+    b = vals.flip(0).repeat(16, 1)
+    c = torch.empty(16, 8, device=DEV)
+    m = xt.run(add_rows, args=(a.to(DEV), b.to(DEV), c, 16, 8), grid=(1, 1, 1))
+    ref = oracle(m, [a, b, torch.zeros(16, 8)])[2]
+    got = host(c)
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    mask = ~np.isnan(ref)
+    assert np.array_equal(got[mask].view(np.uint32), ref[mask].view(np.uint32))
+
+
+@xt.kernel
+def ew_mixed(x, y, out, out2, trow, col):
+    i = xt.bid(0)
+    a = xt.load(x, index=(i, 0), shape=(trow, col))
+    b = xt.load(y, index=(i, 0), shape=(trow, col))
+    t = xt.exp(a) * b - a
+    xt.store(out, index=(i, 0), tile=t)
+    xt.store(out2, index=(i, 0), tile=xt.sigmoid(t) + xt.tanh(b))
+
+
+def test_ew_interpreter_program():
+    g = gen(2)
+    a = torch.randn(300, 50, generator=g)
+    b = torch.randn(300, 50, generator=g)
+    c = torch.empty(300, 50, device=DEV)
+    d = torch.empty(300, 50, device=DEV)
+    m = xt.run(ew_mixed, args=(a.to(DEV), b.to(DEV), c, d, 100, 50), grid=(3, 1, 1))
+    assert m.plan()["family"] == "ew"
+    ref = oracle(m, [a, b, torch.zeros(300, 50), torch.zeros(300, 50)])
+    np.testing.assert_allclose(host(c), ref[2], rtol=2e-6, atol=1e-6)
+    np.testing.assert_allclose(host(d), ref[3], rtol=2e-6, atol=1e-6)
+
+
+# --------------------------------------------------------------- softmax
+@xt.kernel
+def softmax_rows(inp, out, trow, col):
+    i = xt.bid(0)
+    x = xt.load(inp, index=(i, 0), shape=(trow, col))
+    x = x - xt.max(x, axis=-1)
+    x = xt.exp(x)
+    xt.store(out, index=(i, 0), tile=x / xt.sum(x, axis=-1))
+
+
+def softmax_case(rows, cols, trow, seed, blocks=None):
+    x = torch.randn(rows, cols, generator=gen(seed)) * 4
+    y = torch.empty(rows, cols, device=DEV)
+    grid = ((rows + trow - 1) // trow, 1, 1)
+    m = xt.run(softmax_rows, args=(x.to(DEV), y, trow, cols), grid=grid)
+    ref = oracle(m, [x, torch.zeros(rows, cols)], blocks=blocks)[1]
+    return host(y), ref
+
+
+def test_softmax_config2():
+    blocks = [(b, 0, 0) for b in np.random.default_rng(1).choice(8192, 512, replace=False)]
+    got, ref = softmax_case(8192, 1024, 1, 1, blocks)
+    rows = [b[0] for b in blocks]
+    assert np.max(np.abs(got[rows] - ref[rows]) / ref[rows]) <= 1e-5
+    np.testing.assert_allclose(got.sum(axis=1), 1.0, rtol=1e-5)
+
+
+@pytest.mark.parametrize("rows,cols,trow", [(128, 128, 64), (100, 37, 64), (9, 2048, 4), (33, 100, 8)])
+def test_softmax_shapes(rows, cols, trow):
+    got, ref = softmax_case(rows, cols, trow, 3)
+    assert np.max(np.abs(got - ref) / ref) <= 1e-5
+
+
+@xt.kernel
+def row_stats(x, y, mx, trow, col):
+    i = xt.bid(0)
+    t = xt.load(x, index=(i, 0), shape=(trow, col))
+    m = xt.max(t, axis=1)
+    xt.store(y, index=(i, 0), tile=(t - m) * (t - m))
+    xt.store(mx, index=(i, 0), tile=xt.reciprocal(xt.sum(t, axis=1)))
+
+
+def test_row_program_interpreter():
+    x = torch.randn(96, 200, generator=gen(4)) + 3
+    y = torch.empty(96, 200, device=DEV)
+    mx = torch.empty(96, 1, device=DEV)
+    m = xt.run(row_stats, args=(x.to(DEV), y, mx, 32, 200), grid=(3, 1, 1))
+    assert m.plan()["family"] == "rows"
+    ref = oracle(m, [x, torch.zeros(96, 200), torch.zeros(96, 1)])
+    np.testing.assert_array_equal(host(y), ref[1])
+    np.testing.assert_allclose(host(mx), ref[2], rtol=1e-5)
+
+
+# ---------------------------------------------------------------- matmul
+@xt.kernel
+def matmul_kloop(lhs, rhs, out, tm, tn, tk, ksteps):
+    i, j = xt.bid(0), xt.bid(1)
+    acc = None
+    for k in range(ksteps):
+        p = xt.matmul(xt.load(lhs, index=(i, k), shape=(tm, tk)),
+                      xt.load(rhs, index=(k, j), shape=(tk, tn), shared=1))
+        acc = p if acc is None else acc + p
+    xt.store(out, index=(i, j), tile=acc)
+
+
+@xt.kernel
+def matmul_single(lhs, rhs, out, tm, tn, tk):
+    i, j = xt.bid(0), xt.bid(1)
+    a = xt.load(lhs, index=(i, 0), shape=(tm, tk))
+    b = xt.load(rhs, index=(0, j), shape=(tk, tn), shared=1)
+    xt.store(out, index=(i, j), tile=xt.matmul(a, b))
+
+
+def bf16_inputs(m, n, k, seed, scale=None):
+    g = gen(seed)
+    s = scale if scale is not None else 1.0 / np.sqrt(k)
+    a = (torch.randn(m, k, generator=g) * s).to(torch.bfloat16)
+    b = (torch.randn(k, n, generator=g) * s).to(torch.bfloat16)
+    return a, b
+
+
+def test_matmul_bf16_kloop_small():
+    a, b = bf16_inputs(256, 256, 512, 5)
+    c = torch.empty(256, 256, device=DEV)
+    m = xt.run(matmul_kloop, args=(a.to(DEV), b.to(DEV), c, 128, 128, 64, 8), grid=(2, 2, 1))
+    assert m.plan()["family"] == "gemm"
+    ref = oracle(m, [a, b, torch.zeros(256, 256)])[2]
+    bf16_close(host(c), ref)
+
+
+@pytest.mark.parametrize("mnk,tile", [((300, 200, 96), (128, 128, 96)), ((128, 520, 64), (128, 256, 64)),
+                                      ((64, 64, 8), (64, 64, 8))])
+def test_matmul_bf16_ragged(mnk, tile):
+    M, N, K = mnk
+    tm, tn, tk = tile
+    a, b = bf16_inputs(M, N, K, 6)
+    c = torch.full((M, N), float("nan"), device=DEV)
+    grid = ((M + tm - 1) // tm, (N + tn - 1) // tn, 1)
+    m = xt.run(matmul_single, args=(a.to(DEV), b.to(DEV), c, tm, tn, tk), grid=grid)
+    ref = oracle(m, [a, b, torch.zeros(M, N)])[2]
+    bf16_close(host(c), ref)
+
+
+def test_matmul_config3_sampled():
+    a, b = bf16_inputs(4096, 4096, 4096, 2, scale=1.0 / 64)
+    c = torch.empty(4096, 4096, device=DEV)
+    m = xt.run(matmul_kloop, args=(a.to(DEV), b.to(DEV), c, 128, 128, 64, 64), grid=(32, 32, 1))
+    rng = np.random.default_rng(2)
+    blocks = [(int(x), int(y), 0) for x, y in zip(rng.integers(0, 32, 12), rng.integers(0, 32, 12))]
+    blocks += [(0, 0, 0), (31, 31, 0), (0, 31, 0), (31, 0, 0)]
+    ref = oracle(m, [a, b, torch.zeros(4096, 4096)], blocks=blocks)[2]
+    got = host(c)
+    for x, y, _ in blocks:
+        sl = (slice(x * 128, x * 128 + 128), slice(y * 128, y * 128 + 128))
+        bf16_close(got[sl], ref[sl])
+
+
+def test_matmul_bid0_shards_match_full_launch():
+    a, b = bf16_inputs(2048, 1024, 1024, 7)
+    full = torch.empty(2048, 1024, device=DEV)
+    parts = torch.full((2048, 1024), float("nan"), device=DEV)
+    m = xt.run(matmul_single, args=(a.to(DEV), b.to(DEV), full, 256, 128, 1024), grid=(8, 8, 1))
+    for lo, hi in [(0, 3), (3, 4), (4, 8)]:
+        xt.launch(m, a.to(DEV), b.to(DEV), parts, bid0_range=(lo, hi))
+    assert torch.equal(full, parts)
+
+
+@xt.kernel
+def matmul_i8(lhs, rhs, res, scale, bias, tm, tn, tk):
+    i, j = xt.bid(0), xt.bid(1)
+    a = xt.load(lhs, index=(i, 0), shape=(tm, tk))
+    b = xt.load(rhs, index=(0, j), shape=(tk, tn), shared=1)
+    s = xt.load(scale, index=(0, j), shape=(1, tn), shared=1)
+    c = xt.load(bias, index=(0, j), shape=(1, tn), shared=1)
+    t = xt.matmul(a, b)
+    t = t * s + c
+    xt.store(res, index=(i, j), tile=xt.astype(t, dtype=xt.int8))
+
+
+@pytest.mark.parametrize("m_,n_,k_", [(128, 128, 256), (1024, 512, 256), (192, 320, 128)])
+def test_matmul_int8_epilogue_bit_exact(m_, n_, k_):
+    g = gen(8)
+    a = torch.randint(-128, 128, (m_, k_), generator=g, dtype=torch.int8)
+    b = torch.randint(-128, 128, (k_, n_), generator=g, dtype=torch.int8)
+    s = torch.rand(1, n_, generator=g) * 1e-4
+    bias = torch.rand(1, n_, generator=g) * 16 - 8
+    c = torch.zeros(m_, n_, dtype=torch.int8, device=DEV)
+    grid = ((m_ + 63) // 64, (n_ + 63) // 64, 1)
+    m = xt.run(matmul_i8, args=(a.to(DEV), b.to(DEV), c, s.to(DEV), bias.to(DEV), 64, 64, k_), grid=grid)
+    ref = oracle(m, [a, b, torch.zeros(m_, n_, dtype=torch.int8), s, bias])[2]
+    assert np.array_equal(host(c), ref)
+
+
+@xt.kernel
+def mma_chain(a, b, acc_in, acc_out, tm, tn, tk, ksteps):
+    i, j = xt.bid(0), xt.bid(1)
+    acc = xt.load(acc_in, index=(i, j), shape=(tm, tn))
+    for k in range(ksteps):
+        acc = xt.mma(xt.load(a, index=(i, k), shape=(tm, tk)), xt.load(b, index=(k, j), shape=(tk, tn)), acc)
+    xt.store(acc_out, index=(i, j), tile=acc)
+
+
+def test_mma_int8_accumulator_bit_exact():
+    g = gen(9)
+    a = torch.randint(-20, 20, (256, 256), generator=g, dtype=torch.int8)
+    b = torch.randint(-20, 20, (256, 256), generator=g, dtype=torch.int8)
+    acc = torch.randint(-1000, 1000, (256, 256), generator=g).float()
+    out = torch.empty(256, 256, device=DEV)
+    m = xt.run(mma_chain, args=(a.to(DEV), b.to(DEV), acc.to(DEV), out, 128, 128, 128, 2), grid=(2, 2, 1))
+    ref = oracle(m, [a, b, acc, torch.zeros(256, 256)])[3]
+    assert np.array_equal(host(out), ref)
+
+
+def test_launch_rejects_bad_arguments():
+    a, b = bf16_inputs(256, 256, 64, 10)
+    c = torch.empty(256, 256, device=DEV)
+    m = xt.run(matmul_single, args=(a.to(DEV), b.to(DEV), c, 128, 128, 64), grid=(2, 2, 1))
+    with pytest.raises(TypeError, match="must be bf16"):
+        xt.launch(m, a.float().to(DEV), b.to(DEV), c)
+    with pytest.raises(ValueError, match="shape"):
+        xt.launch(m, a[:128].to(DEV), b.to(DEV), c)
+    with pytest.raises(ValueError, match="expects 3 arrays"):
+        xt.launch(m, a.to(DEV), b.to(DEV))
+    with pytest.raises(ValueError, match="outside the grid"):
+        xt.launch(m, a.to(DEV), b.to(DEV), c, bid0_range=(0, 5))

@@ -1,0 +1,386 @@
+// Elementwise and row-program kernels (HBM-bound families).
+//
+// ew:   a flat map over arrays of identical shape.  A single binary
+//       add/sub/mul of two f32 arrays (the kernels/add.py pattern) runs in a
+//       dedicated 128-bit vector kernel; any other register program runs in
+//       an interpreter whose registers stay in registers (operands are picked
+//       by predicated selection, never by dynamic indexing).
+// rows: programs over whole rows (one warp per row, the row held in
+//       registers, warp-shuffle reductions).  The softmax chain
+//       max -> sub -> exp -> sum -> reciprocal -> mul (kernels/softmax.py,
+//       xtile/dsl.py:354-357) has a dedicated kernel; other row programs use
+//       the interpreter.
+//
+// f32 arithmetic is IEEE round-to-nearest with no contraction (the __f*_rn
+// intrinsics), so add/sub/mul/reciprocal/rsqrt match the CPU oracle bit for bit.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "../kernels.h"
+
+namespace xt {
+namespace dev {
+namespace {
+
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ float unary_op(uint8_t op, float x) {
+  switch (op & 0x7f) {
+    case kExp: return expf(x);
+    case kCos: return cosf(x);
+    case kSin: return sinf(x);
+    case kRecip: return __frcp_rn(x);
+    case kRsqrt: return __frcp_rn(__fsqrt_rn(x));
+    case kSigmoid: return __frcp_rn(__fadd_rn(1.0f, expf(-x)));
+    case kTanh: return tanhf(x);
+    case kSilu: return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
+    case kItof: return x;
+    case kFtoi: return x != x ? 0.0f : fminf(fmaxf(rintf(x), -128.0f), 127.0f);
+    default: return x;
+  }
+}
+
+__device__ __forceinline__ float binary_op(uint8_t op, float a, float b) {
+  switch (op & 0x7f) {
+    case kAdd: case kBcastAdd: return __fadd_rn(a, b);
+    case kSub: case kBcastSub: return __fsub_rn(a, b);
+    case kMul: case kBcastMul: return __fmul_rn(a, b);
+    default: return a;
+  }
+}
+
+__device__ __forceinline__ float load_elem(const void* p, uint8_t e, int64_t i) {
+  if (e == kF32) return __ldg(static_cast<const float*>(p) + i);
+  if (e == kBF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+  return static_cast<float>(static_cast<const int8_t*>(p)[i]);
+}
+
+__device__ __forceinline__ void store_elem(void* p, uint8_t e, int64_t i, float v) {
+  if (e == kF32) static_cast<float*>(p)[i] = v;
+  else if (e == kBF16) static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else static_cast<int8_t*>(p)[i] = static_cast<int8_t>(static_cast<int>(v));
+}
+
+// ---------------------------------------------------------------------------
+// ew: dedicated f32 binary kernel
+// ---------------------------------------------------------------------------
+template <int OP>
+__global__ void __launch_bounds__(kThreads) ew_binary_f32(const float* __restrict__ a,
+                                                           const float* __restrict__ b,
+                                                           float* __restrict__ c, int64_t n4,
+                                                           int64_t n) {
+  const float4* a4 = reinterpret_cast<const float4*>(a);
+  const float4* b4 = reinterpret_cast<const float4*>(b);
+  float4* c4 = reinterpret_cast<float4*>(c);
+  int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  // two independent 16-byte loads per operand in flight per thread
+  for (; i + stride < n4; i += 2 * stride) {
+    float4 x0 = __ldcs(a4 + i), y0 = __ldcs(b4 + i);
+    float4 x1 = __ldcs(a4 + i + stride), y1 = __ldcs(b4 + i + stride);
+    float4 r0, r1;
+    r0.x = binary_op(OP, x0.x, y0.x); r0.y = binary_op(OP, x0.y, y0.y);
+    r0.z = binary_op(OP, x0.z, y0.z); r0.w = binary_op(OP, x0.w, y0.w);
+    r1.x = binary_op(OP, x1.x, y1.x); r1.y = binary_op(OP, x1.y, y1.y);
+    r1.z = binary_op(OP, x1.z, y1.z); r1.w = binary_op(OP, x1.w, y1.w);
+    __stcs(c4 + i, r0);
+    __stcs(c4 + i + stride, r1);
+  }
+  for (; i < n4; i += stride) {
+    float4 x = __ldcs(a4 + i), y = __ldcs(b4 + i), r;
+    r.x = binary_op(OP, x.x, y.x); r.y = binary_op(OP, x.y, y.y);
+    r.z = binary_op(OP, x.z, y.z); r.w = binary_op(OP, x.w, y.w);
+    __stcs(c4 + i, r);
+  }
+  // scalar tail (n not a multiple of 4)
+  if (blockIdx.x == 0 && threadIdx.x < n - n4 * 4) {
+    const int64_t t = n4 * 4 + threadIdx.x;
+    c[t] = binary_op(OP, a[t], b[t]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// ew: register-program interpreter
+// ---------------------------------------------------------------------------
+constexpr int kEwRegs = 8;
+
+template <int N>
+__device__ __forceinline__ float pick(const float (&r)[N], int idx) {
+  float v = 0.0f;
+#pragma unroll
+  for (int k = 0; k < N; ++k) v = (k == idx) ? r[k] : v;
+  return v;
+}
+
+template <int N>
+__device__ __forceinline__ void put(float (&r)[N], int idx, float v) {
+#pragma unroll
+  for (int k = 0; k < N; ++k) r[k] = (k == idx) ? v : r[k];
+}
+
+__global__ void __launch_bounds__(kThreads) ew_program(const __grid_constant__ EwArgs p) {
+  int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  for (int64_t i = p.begin + static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < p.end;
+       i += stride) {
+    float r[kEwRegs];
+#pragma unroll
+    for (int k = 0; k < kEwRegs; ++k) r[k] = 0.0f;
+    for (int pc = 0; pc < p.n_code; ++pc) {
+      const Instr ins = p.code[pc];
+      if (ins.op == kLoad) {
+        put(r, ins.dst, load_elem(p.in[ins.a], p.in_elem[ins.a], i));
+      } else if (ins.op == kStore) {
+        store_elem(p.out[ins.dst], p.out_elem[ins.dst], i, pick(r, ins.a));
+      } else if (ins.op == kAdd || ins.op == kSub || ins.op == kMul) {
+        put(r, ins.dst, binary_op(ins.op, pick(r, ins.a), pick(r, ins.b)));
+      } else {
+        put(r, ins.dst, unary_op(ins.op, pick(r, ins.a)));
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// rows: dedicated softmax kernel.  One warp per row; lane l holds float4
+// chunks l, l+32, l+64, ... of the row (coalesced 512-byte warp accesses).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+template <int CHUNKS>  // float4 chunks per lane; row length <= 128 * CHUNKS
+__global__ void __launch_bounds__(kThreads) softmax_rows_vec4(const float* __restrict__ x,
+                                                               float* __restrict__ y, int64_t row_begin,
+                                                               int64_t row_end, int64_t cols) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = row_begin + static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5);
+  if (row >= row_end) return;
+  const int64_t c4 = cols >> 2;
+  const float4* xr = reinterpret_cast<const float4*>(x + row * cols);
+  float4* yr = reinterpret_cast<float4*>(y + row * cols);
+  float4 v[CHUNKS];
+#pragma unroll
+  for (int j = 0; j < CHUNKS; ++j) {
+    int64_t idx = j * 32 + lane;
+    v[j] = idx < c4 ? __ldcs(xr + idx) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+  }
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < CHUNKS; ++j) m = fmaxf(fmaxf(fmaxf(m, v[j].x), fmaxf(v[j].y, v[j].z)), v[j].w);
+  m = warp_max(m);
+  float s = 0.0f;
+#pragma unroll
+  for (int j = 0; j < CHUNKS; ++j) {
+    int64_t idx = j * 32 + lane;
+    if (idx < c4) {
+      v[j].x = expf(__fsub_rn(v[j].x, m));
+      v[j].y = expf(__fsub_rn(v[j].y, m));
+      v[j].z = expf(__fsub_rn(v[j].z, m));
+      v[j].w = expf(__fsub_rn(v[j].w, m));
+      s = __fadd_rn(s, __fadd_rn(__fadd_rn(v[j].x, v[j].y), __fadd_rn(v[j].z, v[j].w)));
+    }
+  }
+  s = warp_sum(s);
+  const float inv = __frcp_rn(s);
+#pragma unroll
+  for (int j = 0; j < CHUNKS; ++j) {
+    int64_t idx = j * 32 + lane;
+    if (idx < c4) {
+      float4 o;
+      o.x = __fmul_rn(v[j].x, inv);
+      o.y = __fmul_rn(v[j].y, inv);
+      o.z = __fmul_rn(v[j].z, inv);
+      o.w = __fmul_rn(v[j].w, inv);
+      __stcs(yr + idx, o);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// rows: register-program interpreter.  Row registers hold PER_LANE values per
+// lane (element j*32 + lane); scalar registers hold one value per row.
+// ---------------------------------------------------------------------------
+constexpr int kRowV = 3;
+constexpr int kRowS = 8;
+
+template <int PL>
+__device__ __forceinline__ void get_row(const float (&v)[kRowV][PL], int idx, float (&out)[PL]) {
+#pragma unroll
+  for (int k = 0; k < kRowV; ++k) {
+    const bool hit = k == idx;
+#pragma unroll
+    for (int j = 0; j < PL; ++j) out[j] = hit ? v[k][j] : out[j];
+  }
+}
+
+template <int PL>
+__device__ __forceinline__ void set_row(float (&v)[kRowV][PL], int idx, const float (&in)[PL]) {
+#pragma unroll
+  for (int k = 0; k < kRowV; ++k) {
+    const bool hit = k == idx;
+#pragma unroll
+    for (int j = 0; j < PL; ++j) v[k][j] = hit ? in[j] : v[k][j];
+  }
+}
+
+template <int PL>
+__global__ void __launch_bounds__(kThreads) rows_program(const __grid_constant__ RowArgs p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = p.row_begin + static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5);
+  if (row >= p.row_end) return;
+  float v[kRowV][PL];
+  float s[kRowS];
+#pragma unroll
+  for (int k = 0; k < kRowV; ++k)
+#pragma unroll
+    for (int j = 0; j < PL; ++j) v[k][j] = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kRowS; ++k) s[k] = 0.0f;
+
+  for (int pc = 0; pc < p.n_code; ++pc) {
+    const Instr ins = p.code[pc];
+    const uint8_t op = ins.op & 0x7f;
+    const bool scalar = ins.op & 0x80;
+    float t[PL], u[PL];
+#pragma unroll
+    for (int j = 0; j < PL; ++j) t[j] = u[j] = 0.0f;
+    if (op == kLoad) {
+      const float* src = p.in[ins.a] + row * p.cols;
+#pragma unroll
+      for (int j = 0; j < PL; ++j) {
+        int64_t c = static_cast<int64_t>(j) * 32 + lane;
+        t[j] = c < p.cols ? __ldg(src + c) : 0.0f;
+      }
+      set_row(v, ins.dst, t);
+    } else if (op == kLoadScalar) {
+      put(s, ins.dst, __ldg(p.in[ins.a] + row));
+    } else if (op == kStore) {
+      float* dst = p.out[ins.dst] + row * p.cols;
+      get_row(v, ins.a, t);
+#pragma unroll
+      for (int j = 0; j < PL; ++j) {
+        int64_t c = static_cast<int64_t>(j) * 32 + lane;
+        if (c < p.cols) dst[c] = t[j];
+      }
+    } else if (op == kStoreScalar) {
+      if (lane == 0) p.out[ins.dst][row] = pick(s, ins.a);
+    } else if (op == kRowMax || op == kRowSum) {
+      get_row(v, ins.a, t);
+      float acc = op == kRowMax ? -INFINITY : 0.0f;
+#pragma unroll
+      for (int j = 0; j < PL; ++j) {
+        int64_t c = static_cast<int64_t>(j) * 32 + lane;
+        if (c < p.cols) acc = op == kRowMax ? fmaxf(acc, t[j]) : __fadd_rn(acc, t[j]);
+      }
+      put(s, ins.dst, op == kRowMax ? warp_max(acc) : warp_sum(acc));
+    } else if (scalar) {
+      const float a = pick(s, ins.a);
+      put(s, ins.dst, (op == kAdd || op == kSub || op == kMul) ? binary_op(op, a, pick(s, ins.b))
+                                                               : unary_op(op, a));
+    } else if (op == kBcastAdd || op == kBcastSub || op == kBcastMul) {
+      get_row(v, ins.a, t);
+      const float b = pick(s, ins.b);
+#pragma unroll
+      for (int j = 0; j < PL; ++j) t[j] = binary_op(op, t[j], b);
+      set_row(v, ins.dst, t);
+    } else if (op == kAdd || op == kSub || op == kMul) {
+      get_row(v, ins.a, t);
+      get_row(v, ins.b, u);
+#pragma unroll
+      for (int j = 0; j < PL; ++j) t[j] = binary_op(op, t[j], u[j]);
+      set_row(v, ins.dst, t);
+    } else {
+      get_row(v, ins.a, t);
+#pragma unroll
+      for (int j = 0; j < PL; ++j) t[j] = unary_op(op, t[j]);
+      set_row(v, ins.dst, t);
+    }
+  }
+}
+
+int grid_for(int64_t work_items, int per_block, int max_blocks) {
+  int64_t b = (work_items + per_block - 1) / per_block;
+  if (b < 1) b = 1;
+  return static_cast<int>(b < max_blocks ? b : max_blocks);
+}
+
+int sm_count() {
+  static int n = [] {
+    int dev = 0, v = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    return v;
+  }();
+  return n;
+}
+
+}  // namespace
+
+cudaError_t launch_ew(const EwArgs& a, cudaStream_t stream) {
+  const int64_t n = a.end - a.begin;
+  if (n <= 0) return cudaSuccess;
+  const int max_blocks = sm_count() * 8;
+  // dedicated path: out = in0 (op) in1, all f32, 16-byte aligned
+  if (a.n_code == 4 && a.n_in == 2 && a.n_out == 1 && a.code[0].op == kLoad && a.code[1].op == kLoad &&
+      a.code[3].op == kStore && a.code[3].a == a.code[2].dst && a.in_elem[0] == kF32 &&
+      a.in_elem[1] == kF32 && a.out_elem[0] == kF32 &&
+      (a.code[2].op == kAdd || a.code[2].op == kSub || a.code[2].op == kMul) && a.begin % 4 == 0) {
+    const bool swap = a.code[2].a == a.code[1].dst;  // operand order of the op
+    const float* x = static_cast<const float*>(a.in[swap ? 1 : 0]) + a.begin;
+    const float* y = static_cast<const float*>(a.in[swap ? 0 : 1]) + a.begin;
+    float* z = static_cast<float*>(a.out[0]) + a.begin;
+    if (((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(z)) &
+         15) == 0) {
+      const int64_t n4 = n / 4;
+      const int blocks = grid_for(n4 > 0 ? n4 : 1, kThreads, max_blocks);
+      switch (a.code[2].op) {
+        case kAdd: ew_binary_f32<kAdd><<<blocks, kThreads, 0, stream>>>(x, y, z, n4, n); break;
+        case kSub: ew_binary_f32<kSub><<<blocks, kThreads, 0, stream>>>(x, y, z, n4, n); break;
+        default: ew_binary_f32<kMul><<<blocks, kThreads, 0, stream>>>(x, y, z, n4, n); break;
+      }
+      return cudaGetLastError();
+    }
+  }
+  ew_program<<<grid_for(n, kThreads, max_blocks), kThreads, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rows(const RowArgs& a, cudaStream_t stream) {
+  const int64_t rows = a.row_end - a.row_begin;
+  if (rows <= 0) return cudaSuccess;
+  const int rows_per_block = kThreads / 32;
+  const int blocks = static_cast<int>((rows + rows_per_block - 1) / rows_per_block);
+  bool aligned = a.cols % 4 == 0 && ((reinterpret_cast<uintptr_t>(a.in[0]) |
+                                      reinterpret_cast<uintptr_t>(a.out[0])) & 15) == 0;
+  if (a.softmax && aligned) {
+    const int64_t chunks = (a.cols / 4 + 31) / 32;
+    const float* x = a.in[0];
+    float* y = a.out[0];
+    if (chunks <= 1) softmax_rows_vec4<1><<<blocks, kThreads, 0, stream>>>(x, y, a.row_begin, a.row_end, a.cols);
+    else if (chunks <= 2) softmax_rows_vec4<2><<<blocks, kThreads, 0, stream>>>(x, y, a.row_begin, a.row_end, a.cols);
+    else if (chunks <= 4) softmax_rows_vec4<4><<<blocks, kThreads, 0, stream>>>(x, y, a.row_begin, a.row_end, a.cols);
+    else if (chunks <= 8) softmax_rows_vec4<8><<<blocks, kThreads, 0, stream>>>(x, y, a.row_begin, a.row_end, a.cols);
+    else softmax_rows_vec4<16><<<blocks, kThreads, 0, stream>>>(x, y, a.row_begin, a.row_end, a.cols);
+    return cudaGetLastError();
+  }
+  const int64_t pl = (a.cols + 31) / 32;
+  if (pl <= 1) rows_program<1><<<blocks, kThreads, 0, stream>>>(a);
+  else if (pl <= 2) rows_program<2><<<blocks, kThreads, 0, stream>>>(a);
+  else if (pl <= 4) rows_program<4><<<blocks, kThreads, 0, stream>>>(a);
+  else if (pl <= 8) rows_program<8><<<blocks, kThreads, 0, stream>>>(a);
+  else if (pl <= 16) rows_program<16><<<blocks, kThreads, 0, stream>>>(a);
+  else if (pl <= 32) rows_program<32><<<blocks, kThreads, 0, stream>>>(a);
+  else return cudaErrorInvalidValue;  // the planner admits rows up to 1024
+  return cudaGetLastError();
+}
+
+}  // namespace dev
+}  // namespace xt

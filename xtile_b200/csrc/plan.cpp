@@ -1,0 +1,737 @@
+// Classification of xt Block programs into B200 kernel families.
+//
+// Semantics restated from the reference:
+//  * tile coordinate -> element start = index * tile dim (lib/xt/XTToNova.cpp:82-101);
+//  * the grid enumerates every (x, y, z) Block (lib/xt/XTSerialize.cpp:68-84);
+//  * matmul epilogue C = (A.B) * scale + bias [-> int8] is what
+//    lib/nova/NovaOptimize.cpp:126-296 folds t*s+b and ftoi into;
+//  * load_conv2d: zero-padded convolution of the halo slice
+//    (lib/xt/XTToNova.cpp:103-142,353-437).
+#include <algorithm>
+#include <functional>
+#include <map>
+#include <set>
+#include <sstream>
+
+#include "plan.h"
+
+namespace xt {
+
+const char* family_name(Family f) {
+  switch (f) {
+    case Family::Ew: return "ew";
+    case Family::Rows: return "rows";
+    case Family::Gemm: return "gemm";
+    case Family::Conv: return "conv";
+  }
+  return "?";
+}
+
+namespace {
+
+struct Coord {
+  bool bid = false;
+  int dim = -1;
+  int64_t value = 0;
+  bool operator==(const Coord& o) const { return bid == o.bid && dim == o.dim && value == o.value; }
+};
+
+struct Access {
+  int op = -1;                 // op index
+  int arg = -1;                // memref argument position
+  Type array;
+  std::vector<int64_t> tile;
+  std::vector<Coord> idx;
+  int shared = 0;
+};
+
+class Classifier {
+ public:
+  Classifier(const Module& m, const Func& f) : m_(m), f_(f) {
+    grid_ = func_grid(f);
+    for (size_t k = 0; k < f.args.size(); ++k) arg_pos_[f.args[k]] = static_cast<int>(k);
+  }
+
+  Plan run() {
+    if (f_.num_blocks != 1) unsupported("the function must have a single block");
+    if (!f_.result_types.empty()) unsupported("the function must not return values");
+    for (int a : f_.args)
+      if (m_.value(a).type.kind != Type::MemRef) unsupported("every function argument must be a memref");
+    Plan p;
+    p.func = f_.name;
+    p.grid = grid_;
+    for (int a : f_.args) {
+      p.arg_types.push_back(m_.value(a).type);
+      p.arg_names.push_back(m_.value(a).name);
+    }
+    bool has_mm = false, has_conv = false;
+    for (const Op& op : f_.ops) {
+      has_mm |= op.name == "xt.matmul" || op.name == "xt.mma";
+      has_conv |= op.name == "xt.load_conv2d";
+    }
+    collect_accesses();
+    if (has_mm) {
+      p.family = Family::Gemm;
+      p.gemm = plan_gemm(p.notes);
+    } else if (has_conv) {
+      p.family = Family::Conv;
+      p.conv = plan_conv();
+    } else {
+      std::string ew_why, rows_why;
+      try {
+        p.ew = plan_ew();
+        p.family = Family::Ew;
+        return p;
+      } catch (const Error& e) {
+        ew_why = e.what();
+      }
+      try {
+        p.rows = plan_rows();
+        p.family = Family::Rows;
+        return p;
+      } catch (const Error& e) {
+        rows_why = e.what();
+      }
+      throw Error(kUnsupported, "no B200 kernel family matches @" + f_.name + ": as an elementwise map: " +
+                                    ew_why + "; as a row program: " + rows_why);
+    }
+    return p;
+  }
+
+ private:
+  const Module& m_;
+  const Func& f_;
+  std::vector<int64_t> grid_;
+  std::map<int, int> arg_pos_;
+  std::map<int, Access> loads_;     // result value id -> access
+  std::vector<Access> stores_;
+  std::map<int, int> uses_;         // value id -> use count
+
+  [[noreturn]] void unsupported(const std::string& why) const { throw Error(kUnsupported, why); }
+
+  const Op* def(int vid) const {
+    int d = m_.value(vid).def_op;
+    return d < 0 ? nullptr : &f_.ops[d];
+  }
+
+  Coord coord(int vid) const {
+    const Op* op = def(vid);
+    if (op && op->name == "xt.get_tile_block_id") {
+      for (int k = 0; k < 3; ++k)
+        if (op->results[k] == vid) return Coord{true, k, 0};
+    }
+    if (op && op->name == "arith.constant" && !op->is_dense && op->result_types[0].kind == Type::Scalar)
+      return Coord{false, -1, op->ivalue};
+    unsupported("tile coordinates must be xt.get_tile_block_id results or integer constants");
+  }
+
+  void collect_accesses() {
+    for (size_t i = 0; i < f_.ops.size(); ++i) {
+      const Op& op = f_.ops[i];
+      for (int v : op.operands) uses_[v]++;
+      if (op.name == "xt.load" || op.name == "xt.store") {
+        Access a;
+        a.op = static_cast<int>(i);
+        bool is_store = op.name == "xt.store";
+        int mem = op.operands[is_store ? 1 : 0];
+        auto it = arg_pos_.find(mem);
+        if (it == arg_pos_.end()) unsupported("loads and stores must address function arguments");
+        a.arg = it->second;
+        a.array = m_.value(mem).type;
+        a.tile = is_store ? op.operand_types[0].shape : op.result_types[0].shape;
+        for (size_t k = is_store ? 2 : 1; k < op.operands.size(); ++k) a.idx.push_back(coord(op.operands[k]));
+        if (const Attr* s = find_attr(op.attrs, "shared")) a.shared = static_cast<int>(s->i);
+        if (is_store) stores_.push_back(a);
+        else loads_[op.results[0]] = a;
+      }
+    }
+    if (stores_.empty()) unsupported("the program stores nothing");
+  }
+
+  // Elements [lo, hi) of one dim that the grid covers through coordinate c.
+  std::pair<int64_t, int64_t> covered(const Coord& c, int64_t tile, int64_t dim) const {
+    if (c.bid) return {0, std::min(grid_[c.dim] * tile, dim)};
+    return {std::min(c.value * tile, dim), std::min((c.value + 1) * tile, dim)};
+  }
+
+  // ------------------------------------------------------------------ ew
+  EwPlan plan_ew() {
+    EwPlan p;
+    const Access* ref = stores_.empty() ? nullptr : &stores_[0];
+    auto same_map = [&](const Access& a) {
+      if (a.tile != ref->tile || a.idx != ref->idx || a.array.shape != ref->array.shape)
+        unsupported("loads and stores must use the same tile shape, index and array shape");
+    };
+    for (auto& kv : loads_) same_map(kv.second);
+    for (auto& s : stores_) same_map(s);
+    // the grid must cover every element exactly once
+    std::set<int> axes;
+    for (size_t d = 0; d < ref->idx.size(); ++d) {
+      const Coord& c = ref->idx[d];
+      auto r = covered(c, ref->tile[d], ref->array.shape[d]);
+      if (r.first != 0 || r.second != ref->array.shape[d])
+        unsupported("the grid's tiles must cover the whole array");
+      if (c.bid) {
+        if (axes.count(c.dim)) unsupported("a block axis may index only one tile dimension");
+        axes.insert(c.dim);
+      }
+    }
+    p.shape = ref->array.shape;
+    p.numel = ref->array.numel();
+    if (!ref->idx.empty() && ref->idx[0].bid && ref->idx[0].dim == 0)
+      p.bid0_span = ref->tile[0] * (p.numel / ref->array.shape[0]);
+
+    std::map<int, int> reg_of;        // value id -> register
+    std::map<int, int> last_use;      // value id -> op index of last use
+    for (size_t i = 0; i < f_.ops.size(); ++i)
+      for (int v : f_.ops[i].operands) last_use[v] = static_cast<int>(i);
+    std::vector<bool> busy(8, false);
+    auto alloc = [&](int vid) {
+      for (int r = 0; r < 8; ++r)
+        if (!busy[r]) {
+          busy[r] = true;
+          reg_of[vid] = r;
+          p.n_regs = std::max(p.n_regs, r + 1);
+          return r;
+        }
+      unsupported("the program needs more than 8 live tiles");
+    };
+    auto release_dead = [&](int i) {
+      for (auto& kv : reg_of)
+        if (busy[kv.second] && last_use[kv.first] <= i) busy[kv.second] = false;
+    };
+    std::map<int, int> in_slot;
+    for (size_t i = 0; i < f_.ops.size(); ++i) {
+      const Op& op = f_.ops[i];
+      const std::string& n = op.name;
+      if (n == "xt.get_tile_block_id" || n == "arith.constant" || n == "func.return" || n == "return") {
+        if (n == "arith.constant" && op.is_dense) unsupported("tensor constants are not supported");
+        continue;
+      }
+      auto reg = [&](int v) { return static_cast<uint8_t>(reg_of.at(v)); };
+      if (n == "xt.load") {
+        const Access& a = loads_.at(op.results[0]);
+        Elem e = a.array.elem;
+        if (e != Elem::F32 && e != Elem::I8 && e != Elem::BF16) unsupported("unsupported element type");
+        auto it = in_slot.find(a.arg);
+        int slot;
+        if (it == in_slot.end()) {
+          if (p.n_in == kMaxSlots) unsupported("too many input arrays");
+          slot = p.n_in++;
+          p.in_arg[slot] = a.arg;
+          p.in_elem[slot] = e;
+          in_slot[a.arg] = slot;
+        } else {
+          slot = it->second;
+        }
+        int r = alloc(op.results[0]);
+        p.code.push_back({kLoad, static_cast<uint8_t>(r), static_cast<uint8_t>(slot), 0});
+      } else if (n == "xt.store") {
+        const Access* a = nullptr;
+        for (auto& s : stores_) if (s.op == static_cast<int>(i)) a = &s;
+        Elem e = a->array.elem;
+        if (e != Elem::F32 && e != Elem::I8 && e != Elem::BF16) unsupported("unsupported element type");
+        if (p.n_out == kMaxSlots) unsupported("too many stores");
+        int slot = p.n_out++;
+        p.out_arg[slot] = a->arg;
+        p.out_elem[slot] = e;
+        p.code.push_back({kStore, static_cast<uint8_t>(slot), reg(op.operands[0]), 0});
+      } else {
+        static const std::map<std::string, uint8_t> kOps = {
+            {"xt.add", kAdd}, {"xt.sub", kSub}, {"xt.mul", kMul}, {"xt.exp", kExp},
+            {"xt.cos", kCos}, {"xt.sin", kSin}, {"xt.reciprocal", kRecip}, {"xt.rsqrt", kRsqrt},
+            {"xt.sigmoid", kSigmoid}, {"xt.tanh", kTanh}, {"xt.silu", kSilu},
+            {"xt.itof", kItof}, {"xt.ftoi", kFtoi}};
+        auto it = kOps.find(n);
+        if (it == kOps.end()) unsupported("'" + n + "' is not an elementwise op");
+        for (const Type& t : op.operand_types)
+          if (t.shape != op.result_types[0].shape) unsupported("broadcasting ops are not elementwise");
+        bool binary = op.operands.size() == 2;
+        if (binary && op.result_types[0].elem != Elem::F32)
+          unsupported("elementwise arithmetic is supported on f32 tiles");
+        if (n == "xt.itof" && op.operand_types[0].elem != Elem::I8) unsupported("itof expects i8");
+        if (n == "xt.ftoi" && op.result_types[0].elem != Elem::I8) unsupported("ftoi produces i8");
+        uint8_t a = reg(op.operands[0]);
+        uint8_t b = binary ? reg(op.operands[1]) : 0;
+        release_dead(static_cast<int>(i) - 1);
+        // operands dying at this op may be reused for its result
+        for (int v : op.operands)
+          if (last_use[v] <= static_cast<int>(i)) busy[reg_of[v]] = false;
+        int r = alloc(op.results[0]);
+        p.code.push_back({it->second, static_cast<uint8_t>(r), a, b});
+      }
+      if (p.code.size() > static_cast<size_t>(kMaxInstr)) unsupported("the program is too long");
+    }
+    if (p.n_in == 0) unsupported("the program loads nothing");
+    return p;
+  }
+
+  // ---------------------------------------------------------------- rows
+  RowPlan plan_rows() {
+    RowPlan p;
+    int64_t R = -1, C = -1, tr = -1;
+    int axis = -1;
+    auto check = [&](const Access& a, bool* scalar) {
+      if (a.array.rank() != 2) unsupported("row programs use rank-2 arrays");
+      if (a.array.elem != Elem::F32) unsupported("row programs use f32 arrays");
+      if (!a.idx[0].bid || a.idx[1].bid || a.idx[1].value != 0)
+        unsupported("row tiles must be indexed (xt.bid(k), 0)");
+      bool sc = a.array.shape[1] == 1;
+      if (!sc && a.tile[1] != a.array.shape[1]) unsupported("row tiles must span whole rows");
+      if (sc && a.tile[1] != 1) unsupported("per-row scalars must be (rows, 1) tiles");
+      if (axis < 0) {
+        axis = a.idx[0].dim;
+        tr = a.tile[0];
+        R = a.array.shape[0];
+      }
+      if (a.idx[0].dim != axis || a.tile[0] != tr || a.array.shape[0] != R)
+        unsupported("all row tiles must share the row axis, tile height and row count");
+      if (!sc) {
+        if (C >= 0 && C != a.array.shape[1]) unsupported("all row arrays must have the same width");
+        C = a.array.shape[1];
+      }
+      *scalar = sc;
+    };
+    for (auto& kv : loads_) { bool s; check(kv.second, &s); }
+    for (auto& s : stores_) { bool sc; check(s, &sc); }
+    if (C < 0) unsupported("the program has no full-row tile");
+    if (C > 2048) unsupported("rows longer than 2048 elements are not supported");
+    p.rows = std::min(grid_[axis] * tr, R);
+    p.cols = C;
+    p.tile_rows = tr;
+    p.row_axis = axis;
+
+    // register allocation for row registers (v) and scalar registers (s)
+    std::map<int, int> last_use;
+    for (size_t i = 0; i < f_.ops.size(); ++i)
+      for (int v : f_.ops[i].operands) last_use[v] = static_cast<int>(i);
+    std::map<int, int> vreg, sreg;
+    std::vector<bool> vbusy(3, false), sbusy(8, false);
+    auto is_row = [&](const Type& t) { return t.rank() == 2 && t.shape[1] == C && C != 1; };
+    auto free_dead = [&](int i) {
+      for (auto& kv : vreg) if (vbusy[kv.second] && last_use[kv.first] <= i) vbusy[kv.second] = false;
+      for (auto& kv : sreg) if (sbusy[kv.second] && last_use[kv.first] <= i) sbusy[kv.second] = false;
+    };
+    auto alloc = [&](int vid, bool row) -> uint8_t {
+      auto& busy = row ? vbusy : sbusy;
+      for (size_t r = 0; r < busy.size(); ++r)
+        if (!busy[r]) {
+          busy[r] = true;
+          (row ? vreg : sreg)[vid] = static_cast<int>(r);
+          if (row) p.n_vregs = std::max(p.n_vregs, static_cast<int>(r) + 1);
+          else p.n_sregs = std::max(p.n_sregs, static_cast<int>(r) + 1);
+          return static_cast<uint8_t>(r);
+        }
+      unsupported(row ? "the row program needs more than 3 live rows" : "too many live row scalars");
+    };
+    std::map<int, int> in_slot;
+    for (size_t i = 0; i < f_.ops.size(); ++i) {
+      const Op& op = f_.ops[i];
+      const std::string& n = op.name;
+      int ii = static_cast<int>(i);
+      if (n == "xt.get_tile_block_id" || n == "func.return" || n == "return") continue;
+      if (n == "arith.constant") {
+        if (op.is_dense) unsupported("tensor constants are not supported");
+        continue;
+      }
+      if (n == "xt.load") {
+        const Access& a = loads_.at(op.results[0]);
+        bool sc = a.array.shape[1] == 1;
+        int slot;
+        auto it = in_slot.find(a.arg);
+        if (it == in_slot.end()) {
+          if (p.n_in == kMaxSlots) unsupported("too many input arrays");
+          slot = p.n_in++;
+          p.in_arg[slot] = a.arg;
+          p.in_is_scalar[slot] = sc;
+          in_slot[a.arg] = slot;
+        } else {
+          slot = it->second;
+        }
+        free_dead(ii - 1);
+        uint8_t r = alloc(op.results[0], !sc);
+        p.code.push_back({sc ? kLoadScalar : kLoad, r, static_cast<uint8_t>(slot), 0});
+        continue;
+      }
+      if (n == "xt.store") {
+        const Access* a = nullptr;
+        for (auto& s : stores_) if (s.op == ii) a = &s;
+        bool sc = a->array.shape[1] == 1;
+        if (p.n_out == kMaxSlots) unsupported("too many stores");
+        int slot = p.n_out++;
+        p.out_arg[slot] = a->arg;
+        p.out_is_scalar[slot] = sc;
+        uint8_t r = static_cast<uint8_t>(sc ? sreg.at(op.operands[0]) : vreg.at(op.operands[0]));
+        p.code.push_back({sc ? kStoreScalar : kStore, static_cast<uint8_t>(slot), r, 0});
+        continue;
+      }
+      const Type& res = op.result_types[0];
+      if (res.elem != Elem::F32) unsupported("row programs compute in f32");
+      auto operand_reg = [&](int v) -> uint8_t {
+        auto it = vreg.find(v);
+        if (it != vreg.end()) return static_cast<uint8_t>(it->second);
+        return static_cast<uint8_t>(sreg.at(v));
+      };
+      if (n == "xt.reduce_max" || n == "xt.reduce_sum") {
+        const Attr* ax = find_attr(op.attrs, "axis");
+        int64_t axis_v = ax->i < 0 ? ax->i + 2 : ax->i;
+        if (axis_v != 1) unsupported("row programs reduce along axis 1 only");
+        if (!is_row(op.operand_types[0])) unsupported("reductions must read a full row");
+        uint8_t a = operand_reg(op.operands[0]);
+        free_dead(ii);
+        uint8_t r = alloc(op.results[0], false);
+        p.code.push_back({n == "xt.reduce_max" ? kRowMax : kRowSum, r, a, 0});
+        continue;
+      }
+      static const std::map<std::string, uint8_t> kBin = {{"xt.add", kAdd}, {"xt.sub", kSub}, {"xt.mul", kMul}};
+      static const std::map<std::string, uint8_t> kUn = {
+          {"xt.exp", kExp}, {"xt.cos", kCos}, {"xt.sin", kSin}, {"xt.reciprocal", kRecip},
+          {"xt.rsqrt", kRsqrt}, {"xt.sigmoid", kSigmoid}, {"xt.tanh", kTanh}, {"xt.silu", kSilu}};
+      if (kBin.count(n)) {
+        bool lrow = is_row(op.operand_types[0]), rrow = is_row(op.operand_types[1]);
+        uint8_t a = operand_reg(op.operands[0]), b = operand_reg(op.operands[1]);
+        uint8_t opc;
+        if (lrow && rrow) opc = kBin.at(n);
+        else if (lrow && !rrow) opc = n == "xt.add" ? kBcastAdd : n == "xt.sub" ? kBcastSub : kBcastMul;
+        else if (!lrow && !rrow) opc = kBin.at(n) | 0x80;
+        else unsupported("a per-row scalar may only be the right operand of a row op");
+        free_dead(ii);
+        uint8_t r = alloc(op.results[0], lrow);
+        p.code.push_back({opc, r, a, b});
+        continue;
+      }
+      if (kUn.count(n)) {
+        bool row = is_row(op.operand_types[0]);
+        uint8_t a = operand_reg(op.operands[0]);
+        free_dead(ii);
+        uint8_t r = alloc(op.results[0], row);
+        p.code.push_back({static_cast<uint8_t>(kUn.at(n) | (row ? 0 : 0x80)), r, a, 0});
+        continue;
+      }
+      unsupported("'" + n + "' is not supported in row programs");
+    }
+    if (p.code.size() > static_cast<size_t>(kMaxInstr)) unsupported("the program is too long");
+    p.softmax = is_softmax_chain(p);
+    if (!p.softmax && C > 1024) unsupported("row programs other than softmax support rows up to 1024 elements");
+    return p;
+  }
+
+  // The softmax chain as plan_rows emits it for kernels/softmax.py and the
+  // reciprocal form of test/python/dsl_convert.py:30-37: Load v; RowMax s<-v;
+  // BcastSub v'<-v,s; Exp v''<-v'; RowSum s'<-v''; Recip(scalar) s''<-s';
+  // BcastMul v'''<-v'',s''; Store v'''.
+  static bool is_softmax_chain(const RowPlan& p) {
+    if (p.code.size() != 8 || p.n_in != 1 || p.n_out != 1 || p.in_is_scalar[0] || p.out_is_scalar[0])
+      return false;
+    const Instr* c = p.code.data();
+    return c[0].op == kLoad && c[1].op == kRowMax && c[1].a == c[0].dst && c[2].op == kBcastSub &&
+           c[2].a == c[0].dst && c[2].b == c[1].dst && c[3].op == kExp && c[3].a == c[2].dst &&
+           c[4].op == kRowSum && c[4].a == c[3].dst && c[5].op == (kRecip | 0x80) && c[5].a == c[4].dst &&
+           c[6].op == kBcastMul && c[6].a == c[3].dst && c[6].b == c[5].dst && c[7].op == kStore &&
+           c[7].a == c[6].dst;
+  }
+
+  // ---------------------------------------------------------------- gemm
+  struct Term {
+    const Access* a;
+    const Access* b;
+  };
+
+  const Access& load_of(int vid, const char* what) {
+    auto it = loads_.find(vid);
+    if (it == loads_.end()) unsupported(std::string(what) + " must be loaded directly from an array");
+    return it->second;
+  }
+
+  // Collects matmul terms of a sum tree (xt.add of matmuls) or an mma chain.
+  void collect_terms(int vid, std::vector<Term>& terms, int* acc_vid) {
+    const Op* op = def(vid);
+    if (!op) unsupported("the matmul result must come from xt.matmul / xt.mma");
+    if (uses_[vid] > 1) unsupported("intermediate matmul values may have only one use");
+    if (op->name == "xt.matmul") {
+      terms.push_back({&load_of(op->operands[0], "matmul lhs"), &load_of(op->operands[1], "matmul rhs")});
+      return;
+    }
+    if (op->name == "xt.add" && op->operand_types[0] == op->operand_types[1]) {
+      collect_terms(op->operands[0], terms, acc_vid);
+      collect_terms(op->operands[1], terms, acc_vid);
+      return;
+    }
+    if (op->name == "xt.mma") {
+      terms.push_back({&load_of(op->operands[0], "mma lhs"), &load_of(op->operands[1], "mma rhs")});
+      const Op* acc = def(op->operands[2]);
+      if (acc && (acc->name == "xt.mma" || acc->name == "xt.matmul" || acc->name == "xt.add")) {
+        collect_terms(op->operands[2], terms, acc_vid);
+      } else {
+        if (*acc_vid >= 0) unsupported("an mma chain may start from one accumulator tile");
+        *acc_vid = op->operands[2];
+      }
+      return;
+    }
+    unsupported("'" + op->name + "' cannot feed the matmul accumulator");
+  }
+
+  GemmPlan plan_gemm(std::vector<std::string>& notes) {
+    GemmPlan g;
+    if (stores_.size() != 1) unsupported("a matmul program must store exactly one tile");
+    const Access& st = stores_[0];
+    const Op& store_op = f_.ops[st.op];
+    int v = store_op.operands[0];
+    if (st.array.rank() != 2) unsupported("matmul output must be rank 2");
+    // walk back through the epilogue: [ftoi] <- (mul|add by row/scalar tile)*
+    std::vector<EpiStep> rev;
+    std::vector<const Access*> epi_loads;
+    const Op* op = def(v);
+    if (op && op->name == "xt.ftoi") {
+      g.ftoi = true;
+      v = op->operands[0];
+      op = def(v);
+    }
+    while (op && (op->name == "xt.mul" || op->name == "xt.add")) {
+      const Type& lt = op->operand_types[0];
+      const Type& rt = op->operand_types[1];
+      if (lt == rt) break;  // a tile + tile add: part of a K sum
+      int other = op->operands[1];
+      if (rt.shape != std::vector<int64_t>{1, rt.shape[1]} || (rt.shape[1] != lt.shape[1] && rt.shape[1] != 1))
+        unsupported("epilogue operands must be (1, tn) rows or (1, 1) scalars");
+      const Access& a = load_of(other, "epilogue operand");
+      if (a.array.elem != Elem::F32) unsupported("epilogue rows must be f32");
+      bool scalar = rt.shape[1] == 1;
+      if (!scalar && a.array.shape[0] != 1) unsupported("epilogue rows must come from (1, N) arrays");
+      EpiStep s;
+      s.kind = op->name == "xt.mul" ? (scalar ? kEpiMulScalar : kEpiMulRow)
+                                    : (scalar ? kEpiAddScalar : kEpiAddRow);
+      s.arg = a.arg;
+      rev.push_back(s);
+      epi_loads.push_back(&a);
+      if (uses_[v] > 1) unsupported("epilogue intermediates may have only one use");
+      v = op->operands[0];
+      op = def(v);
+    }
+    g.epi.assign(rev.rbegin(), rev.rend());
+    std::vector<Term> terms;
+    int acc_vid = -1;
+    collect_terms(v, terms, &acc_vid);
+
+    // all terms must share A/B arrays, M/N coordinates and tile shapes; their
+    // K coordinates must enumerate 0..n-1
+    const Access* a0 = terms[0].a;
+    const Access* b0 = terms[0].b;
+    std::set<int64_t> ks;
+    for (const Term& t : terms) {
+      if (t.a->arg != a0->arg || t.b->arg != b0->arg) unsupported("all matmul terms must read the same A and B");
+      if (t.a->tile != a0->tile || t.b->tile != b0->tile) unsupported("all matmul terms must use the same tiles");
+      if (!(t.a->idx[0] == a0->idx[0]) || !(t.b->idx[1] == b0->idx[1]))
+        unsupported("all matmul terms must address the same output tile");
+      if (t.a->idx[1].bid || t.b->idx[0].bid || t.a->idx[1].value != t.b->idx[0].value)
+        unsupported("matmul K coordinates must be equal constants on A and B");
+      ks.insert(t.a->idx[1].value);
+    }
+    if (static_cast<int64_t>(ks.size()) != static_cast<int64_t>(terms.size()) || *ks.begin() != 0 ||
+        *ks.rbegin() != static_cast<int64_t>(terms.size()) - 1)
+      unsupported("matmul K tiles must be 0 .. n-1, each once");
+    const Type& A = a0->array;
+    const Type& B = b0->array;
+    if (A.elem != B.elem) unsupported("A and B must have the same element type");
+    if (A.elem != Elem::BF16 && A.elem != Elem::I8)
+      unsupported("tensor-core matmul needs bf16 or i8 operands (f32 has no exact tensor-core form)");
+    g.ab_elem = A.elem;
+    g.tm = a0->tile[0];
+    g.tk = a0->tile[1];
+    g.tn = b0->tile[1];
+    g.k_steps = static_cast<int>(terms.size());
+    g.a_arg = a0->arg;
+    g.b_arg = b0->arg;
+    g.c_arg = st.arg;
+    g.c_elem = st.array.elem;
+    if (g.ftoi != (g.c_elem == Elem::I8)) unsupported("an int8 result needs astype(int8) and vice versa");
+    if (g.c_elem != Elem::F32 && g.c_elem != Elem::I8) unsupported("matmul output must be f32 or i8");
+    const Coord& mi = a0->idx[0];
+    const Coord& nj = b0->idx[1];
+    if (!(st.idx[0] == mi) || !(st.idx[1] == nj)) unsupported("the store must use the A row and B column coordinates");
+    if (st.tile[0] != g.tm || st.tile[1] != g.tn) unsupported("the stored tile must be tm x tn");
+    if (mi.bid && nj.bid && mi.dim == nj.dim) unsupported("M and N tiles must use different block axes");
+    if (!mi.bid && mi.value != 0) unsupported("a constant M coordinate must be 0");
+    if (!nj.bid && nj.value != 0) unsupported("a constant N coordinate must be 0");
+    g.m_axis = mi.bid ? mi.dim : -1;
+    g.n_axis = nj.bid ? nj.dim : -1;
+    g.M = std::min((mi.bid ? grid_[mi.dim] : 1) * g.tm, A.shape[0]);
+    g.N = std::min((nj.bid ? grid_[nj.dim] : 1) * g.tn, B.shape[1]);
+    g.K = std::min(g.k_steps * g.tk, std::min(A.shape[1], B.shape[0]));
+    if (st.array.shape[0] < g.M || st.array.shape[1] < g.N) unsupported("output array too small");
+    g.lda = A.shape[1];
+    g.ldb = B.shape[1];
+    g.ldc = st.array.shape[1];
+    int align = A.elem == Elem::BF16 ? 8 : 16;  // 16-byte TMA strides
+    if (g.lda % align || g.ldb % align)
+      unsupported("A and B rows must be multiples of 16 bytes for TMA");
+    if (acc_vid >= 0) {
+      const Access& acc = load_of(acc_vid, "mma accumulator");
+      if (acc.array.elem != Elem::F32 || acc.tile != st.tile || !(acc.idx == st.idx))
+        unsupported("the mma accumulator must be the f32 output tile");
+      g.acc_arg = acc.arg;
+    }
+    for (const Access* e : epi_loads) {
+      bool scalar = e->tile[1] == 1 && g.tn != 1;
+      if (e->idx[0].bid || e->idx[0].value != 0) unsupported("epilogue rows must be indexed (0, ...)");
+      if (scalar) {
+        if (e->idx[1].bid || e->idx[1].value != 0) unsupported("epilogue scalars must be indexed (0, 0)");
+      } else if (!(e->idx[1] == nj) || e->tile[1] != g.tn || e->array.shape[1] < g.N) {
+        unsupported("epilogue rows must be indexed by the B column coordinate");
+      }
+    }
+    // shared=k is a promise that the tile is the same for blocks that agree
+    // on axes >= k; note programs whose index breaks it (every load still
+    // reads the tile its index names)
+    for (auto& kv : loads_) {
+      const Access& a = kv.second;
+      if (a.shared > 0)
+        for (const Coord& c : a.idx)
+          if (c.bid && c.dim < a.shared)
+            notes.push_back("shared=" + std::to_string(a.shared) + " load of %" +
+                            m_.value(f_.args[a.arg]).name + " is indexed by xt.bid(" +
+                            std::to_string(c.dim) + "): loaded per block by its index");
+    }
+    return g;
+  }
+
+  // ---------------------------------------------------------------- conv
+  ConvPlan plan_conv() {
+    ConvPlan c;
+    if (stores_.size() != 1) unsupported("a conv program must store exactly one tile");
+    const Access& st = stores_[0];
+    const Op* op = def(f_.ops[st.op].operands[0]);
+    if (!op || op->name != "xt.load_conv2d") unsupported("the stored tile must be the load_conv2d result");
+    const Access& filt = load_of(op->operands[1], "the conv filter");
+    auto src = arg_pos_.find(op->operands[0]);
+    if (src == arg_pos_.end()) unsupported("the conv source must be a function argument");
+    const Type& in = op->operand_types[0];
+    const Type& ft = op->operand_types[1];
+    const Type& res = op->result_types[0];
+    for (const Coord& k : filt.idx)
+      if (k.bid || k.value != 0) unsupported("the filter must be loaded whole at index 0");
+    if (filt.tile != filt.array.shape) unsupported("the filter must be loaded whole");
+    const Attr* g = find_attr(op->attrs, "group");
+    if (g && g->i != 1) unsupported("grouped convolution is not supported");
+    std::vector<Coord> idx;
+    for (int k = 2; k < 6; ++k) idx.push_back(coord(op->operands[k]));
+    if (idx[3].bid || idx[3].value != 0) unsupported("the channel coordinate must be 0");
+    if (!(idx == st.idx)) unsupported("the store must use the load_conv2d coordinates");
+    if (res.shape[3] != ft.shape[3]) unsupported("the result must hold every filter output channel");
+    if (in.elem != Elem::BF16) unsupported("the tensor-core conv takes bf16 input and filter");
+    if (st.array.elem != Elem::F32) unsupported("the conv output must be f32");
+    c.in_arg = src->second;
+    c.filt_arg = filt.arg;
+    c.out_arg = st.arg;
+    c.elem = in.elem;
+    c.N = in.shape[0];
+    c.H = in.shape[1];
+    c.W = in.shape[2];
+    c.C = in.shape[3];
+    c.KH = ft.shape[0];
+    c.KW = ft.shape[1];
+    c.KO = ft.shape[3];
+    const Attr* pad = find_attr(op->attrs, "pad");
+    const Attr* stride = find_attr(op->attrs, "stride");
+    const Attr* dil = find_attr(op->attrs, "dilation");
+    c.pad_t = pad->arr[0];
+    c.pad_l = pad->arr[1];
+    c.stride_h = stride->arr[0];
+    c.stride_w = stride->arr[1];
+    c.dil_h = dil->arr[0];
+    c.dil_w = dil->arr[1];
+    c.tb = res.shape[0];
+    c.th = res.shape[1];
+    c.tw = res.shape[2];
+    const Type& out = st.array;
+    c.out_h = out.shape[1];
+    c.out_w = out.shape[2];
+    c.out_c = out.shape[3];
+    auto cov = [&](const Coord& k, int64_t tile, int64_t dim) {
+      auto r = covered(k, tile, dim);
+      if (r.first != 0) unsupported("conv tiles must start at the array origin");
+      return r.second;
+    };
+    c.ON = cov(idx[0], c.tb, std::min(c.N, out.shape[0]));
+    c.OH = cov(idx[1], c.th, out.shape[1]);
+    c.OW = cov(idx[2], c.tw, out.shape[2]);
+    c.OC = c.KO;
+    c.n_axis = idx[0].bid ? idx[0].dim : -1;
+    if (c.C % 8) unsupported("input channels must be a multiple of 8 (16-byte TMA rows)");
+    if (c.KO % 16 || c.KO > 256) unsupported("output channels must be a multiple of 16, at most 256");
+    if (c.stride_h != 1 || c.stride_w != 1) unsupported("strided convolution is not supported yet");
+    return c;
+  }
+};
+
+}  // namespace
+
+Plan make_plan(const Module& m, const Func& f) {
+  Classifier c(m, f);
+  return c.run();
+}
+
+std::string describe_plan(const Plan& p, int stage) {
+  std::ostringstream os;
+  auto arr = [&](int arg) { return "%" + p.arg_names.at(arg); };
+  os << "  // b200 @" << p.func << ": family " << family_name(p.family) << ", grid [" << p.grid[0] << ", "
+     << p.grid[1] << ", " << p.grid[2] << "]\n";
+  if (stage >= 1) {
+    os << "  //   xt_serialize -> every (x, y, z) Block maps onto the CUDA grid; no unrolling\n";
+  }
+  if (stage >= 2) {
+    switch (p.family) {
+      case Family::Ew:
+        os << "  //   xt_to_nova -> ew: " << p.ew.numel << " elements, " << p.ew.n_in << " inputs, "
+           << p.ew.n_out << " outputs, " << p.ew.code.size() << " register ops\n";
+        break;
+      case Family::Rows:
+        os << "  //   xt_to_nova -> rows: " << p.rows.rows << " rows x " << p.rows.cols << ", "
+           << p.rows.code.size() << " row ops (reductions along axis 1)\n";
+        break;
+      case Family::Gemm:
+        os << "  //   xt_to_nova -> gemm: M " << p.gemm.M << " N " << p.gemm.N << " K " << p.gemm.K << " ("
+           << elem_name(p.gemm.ab_elem) << " -> " << elem_name(p.gemm.c_elem) << "), A " << arr(p.gemm.a_arg)
+           << " B " << arr(p.gemm.b_arg) << " C " << arr(p.gemm.c_arg) << ", block tile " << p.gemm.tm << "x"
+           << p.gemm.tn << "x" << p.gemm.tk << " x" << p.gemm.k_steps << "\n";
+        break;
+      case Family::Conv:
+        os << "  //   xt_to_nova -> conv: implicit GEMM M " << p.conv.ON * p.conv.OH * p.conv.OW << " N "
+           << p.conv.OC << " K " << p.conv.KH * p.conv.KW * p.conv.C << ", pad [" << p.conv.pad_t << ", "
+           << p.conv.pad_l << "]\n";
+        break;
+    }
+  }
+  if (stage >= 3 && p.family == Family::Gemm) {
+    os << "  //   nova_optimize -> epilogue:";
+    if (p.gemm.acc_arg >= 0) os << " + " << arr(p.gemm.acc_arg);
+    for (const EpiStep& s : p.gemm.epi)
+      os << (s.kind == kEpiMulRow || s.kind == kEpiMulScalar ? " * " : " + ") << arr(s.arg);
+    if (p.gemm.ftoi) os << " -> i8 (round half even, saturate)";
+    os << "\n";
+  }
+  if (stage >= 4) {
+    const char* threads = p.family == Family::Gemm || p.family == Family::Conv
+                              ? "warp 0 TMA producer, warp 1 tcgen05.mma issuer, warps 4-7 TMEM epilogue"
+                              : p.family == Family::Rows ? "one warp per row, 8 warps per CTA"
+                                                         : "grid-stride, 4 elements per thread per step";
+    os << "  //   nova_threading -> " << threads << "\n";
+  }
+  if (stage >= 5) {
+    const char* sync = p.family == Family::Gemm || p.family == Family::Conv
+                           ? "mbarrier ring (full/empty per stage) + TMEM full/empty, bounded waits"
+                           : "none (blocks are independent)";
+    os << "  //   nova_barrier -> " << sync << "\n";
+  }
+  if (stage >= 6) {
+    const char* mem = p.family == Family::Gemm ? "4 smem stages of A 128x64 + B 64x256 (192 KiB), TMEM 512 columns"
+                      : p.family == Family::Conv ? "smem ring of shifted input tiles + resident filter, TMEM accumulator"
+                                                 : "registers only";
+    os << "  //   nova_allocate -> " << mem << "\n";
+  }
+  if (stage >= 7) os << "  //   nova_to_x1 -> launch via xt_launch (sm_100a)\n";
+  for (const std::string& n : p.notes) os << "  //   note: " << n << "\n";
+  return os.str();
+}
+
+}  // namespace xt

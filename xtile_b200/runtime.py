@@ -1,0 +1,107 @@
+"""Launching Block programs on B200 GPUs.
+
+The reference cannot execute a program; this is the new part of the
+interface.  ``launch`` runs a converted/parsed module on torch CUDA tensors
+(one per memref argument, in signature order), writing the stored arrays in
+place -- the DSL's ``xt.store`` into a mutable Array.  ``bid0_range`` runs
+only the Blocks whose ``xt.bid(0)`` lies in ``[lo, hi)``: one process per GPU
+passes its own range to split a Grid across GPUs.
+
+Tensors must be contiguous, on one CUDA device, with exactly the memref's
+shape and dtype (float32 / bfloat16 / int8), 16-byte aligned.  The launch is
+asynchronous on ``stream`` (default: torch's current stream of that device).
+"""
+from __future__ import annotations
+
+from typing import Sequence
+
+from . import dsl
+from ._native import native as _native
+from .api import Module, convert
+
+_TORCH_DTYPES = None
+
+
+def _dtype_map():
+    global _TORCH_DTYPES
+    if _TORCH_DTYPES is None:
+        import torch
+
+        _TORCH_DTYPES = {"f32": torch.float32, "bf16": torch.bfloat16, "i8": torch.int8}
+    return _TORCH_DTYPES
+
+
+def _check_arrays(module: Module, arrays: Sequence, func: str | None):
+    import torch
+
+    sig = module.arguments(func)
+    if len(arrays) != len(sig):
+        raise ValueError(f"launch expects {len(sig)} arrays "
+                         f"({', '.join('%' + s[0] for s in sig)}), got {len(arrays)}")
+    dtypes = _dtype_map()
+    device = None
+    for t, (name, is_memref, elem, shape) in zip(arrays, sig):
+        if not is_memref:
+            raise TypeError(f"argument %{name} is not a memref; only memref kernels can be launched")
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"array %{name} must be a torch tensor, got {type(t).__name__}")
+        if not t.is_cuda:
+            raise ValueError(f"array %{name} must be a CUDA tensor")
+        if device is None:
+            device = t.device
+        elif t.device != device:
+            raise ValueError(f"array %{name} is on {t.device}, expected {device}")
+        if elem not in dtypes or t.dtype != dtypes[elem]:
+            raise TypeError(f"array %{name} must be {elem}, got {t.dtype}")
+        if tuple(t.shape) != tuple(shape):
+            raise ValueError(f"array %{name} must have shape {tuple(shape)}, got {tuple(t.shape)}")
+        if not t.is_contiguous():
+            raise ValueError(f"array %{name} must be contiguous (row-major)")
+    return device
+
+
+def launch(module: Module, *arrays, func: str | None = None, stream=None,
+           bid0_range: tuple[int, int] | None = None) -> None:
+    """Run the Block program of ``func`` (default: the first) over its grid."""
+    import torch
+
+    device = _check_arrays(module, arrays, func)
+    if stream is None:
+        stream = torch.cuda.current_stream(device)
+    handle = stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+    lo, hi = (0, 0) if bid0_range is None else bid0_range
+    if bid0_range is not None and hi <= lo:
+        return
+    with torch.cuda.device(device):
+        _native.launch(module._CAPIPtr, [t.data_ptr() for t in arrays], int(lo), int(hi),
+                       int(handle), func)
+
+
+def run(kernel_fn: dsl.KernelFunction, *, args: tuple, grid: tuple, double_buffering: bool = False,
+        stream=None, bid0_range: tuple[int, int] | None = None) -> Module:
+    """Trace ``kernel_fn`` with tensors standing in for Arrays, then launch it.
+
+    ``args`` mixes torch tensors (one per Array parameter) and ints (compile
+    time constants), in the kernel's parameter order.  Returns the module, so
+    a caller can launch it again without re-tracing.
+    """
+    import torch
+
+    elems = {torch.float32: dsl.float32, torch.bfloat16: dsl.bfloat16, torch.int8: dsl.int8}
+    trace_args, tensors = [], []
+    for a in args:
+        if isinstance(a, torch.Tensor):
+            if a.dtype not in elems:
+                raise TypeError(f"unsupported tensor dtype {a.dtype}")
+            trace_args.append(dsl.Array(shape=tuple(int(d) for d in a.shape), dtype=elems[a.dtype]))
+            tensors.append(a)
+        else:
+            trace_args.append(a)
+    module = convert(kernel_fn, args=tuple(trace_args), grid=grid, double_buffering=double_buffering)
+    launch(module, *tensors, stream=stream, bid0_range=bid0_range)
+    return module
+
+
+def device_error() -> int:
+    """Reads and clears the current device's kernel error word (0: none)."""
+    return int(_native.device_error())
