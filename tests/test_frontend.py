@@ -226,3 +226,88 @@ def test_unsupported_programs_explain_why():
     m = xt.convert(case[1], args=case[2], grid=case[3], double_buffering=case[4])
     with pytest.raises(RuntimeError, match="no B200 kernel family"):
         m.plan()
+
+
+# --- the planner's register programs, evaluated on the CPU -------------------
+import numpy as np  # noqa: E402
+
+from oracle import xt_oracle  # noqa: E402
+
+_UNARY = {"exp": np.exp, "cos": np.cos, "sin": np.sin, "recip": lambda x: np.float32(1) / x,
+          "rsqrt": lambda x: np.float32(1) / np.sqrt(x), "tanh": np.tanh,
+          "sigmoid": lambda x: np.float32(1) / (np.float32(1) + np.exp(-x)),
+          "silu": lambda x: x / (np.float32(1) + np.exp(-x)), "itof": lambda x: x,
+          "ftoi": lambda x: xt_oracle.ftoi_i8(x).astype(np.float32)}
+_BINARY = {"add": np.add, "sub": np.subtract, "mul": np.multiply,
+           "bcast_add": np.add, "bcast_sub": np.subtract, "bcast_mul": np.multiply}
+
+
+def run_register_program(module, arrays):
+    """Evaluates the ew/rows register program of the stage dump with numpy."""
+    xt.nova_optimize(module)
+    names = [a[0] for a in module.arguments()]
+    mem = dict(zip(names, arrays))
+    regs = {}
+    for line in xt._module_asm(module).splitlines():
+        m = re.match(r"\s*//\s{5}(\w+) = (\w+) (.*)$", line)
+        s = re.match(r"\s*//\s{5}(store|store_scalar) %(\w+) <- (\w+)$", line)
+        if s:
+            dst = mem[s.group(2)]
+            dst[...] = regs[s.group(3)].astype(dst.dtype)
+        elif m:
+            dst, op, rest = m.groups()
+            ops = [o.strip() for o in rest.split(",")]
+            if op in ("load", "load_scalar"):
+                regs[dst] = mem[ops[0].lstrip("%")].astype(np.float32)
+            elif op == "rowmax":
+                regs[dst] = regs[ops[0]].max(axis=1, keepdims=True)
+            elif op == "rowsum":
+                regs[dst] = regs[ops[0]].astype(np.float64).sum(axis=1, keepdims=True).astype(np.float32)
+            elif op in _BINARY:
+                regs[dst] = _BINARY[op](regs[ops[0]], regs[ops[1]]).astype(np.float32)
+            else:
+                regs[dst] = _UNARY[op](regs[ops[0]]).astype(np.float32)
+
+
+def test_ew_register_program_matches_oracle():
+    @dsl.kernel
+    def ew_mixed(x, y, out, out2, trow, col):
+        i = xt.bid(0)
+        a = xt.load(x, index=(i, 0), shape=(trow, col))
+        b = xt.load(y, index=(i, 0), shape=(trow, col))
+        t = xt.exp(a) * b - a
+        xt.store(out, index=(i, 0), tile=t)
+        xt.store(out2, index=(i, 0), tile=xt.sigmoid(t) + xt.tanh(b))
+
+    A = xt.Array
+    m = xt.convert(ew_mixed, args=(A((30, 5), xt.float32),) * 4 + (10, 5), grid=(3, 1, 1))
+    rng = np.random.default_rng(0)
+    a = rng.standard_normal((30, 5)).astype(np.float32)
+    b = rng.standard_normal((30, 5)).astype(np.float32)
+    got = [a, b, np.zeros_like(a), np.zeros_like(a)]
+    run_register_program(m, got)
+    ref = [a, b, np.zeros_like(a), np.zeros_like(a)]
+    xt_oracle.run(xt._module_asm(m).split("// b200")[0] + "}", ref)
+    np.testing.assert_allclose(got[2], ref[2], rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(got[3], ref[3], rtol=1e-6, atol=1e-6)
+
+
+def test_rows_register_program_matches_oracle():
+    @dsl.kernel
+    def row_stats(x, y, mx, trow, col):
+        i = xt.bid(0)
+        t = xt.load(x, index=(i, 0), shape=(trow, col))
+        m = xt.max(t, axis=1)
+        xt.store(y, index=(i, 0), tile=(t - m) * (t - m))
+        xt.store(mx, index=(i, 0), tile=xt.reciprocal(xt.sum(t, axis=1)))
+
+    A = xt.Array
+    m = xt.convert(row_stats, args=(A((12, 7), xt.float32), A((12, 7), xt.float32), A((12, 1), xt.float32),
+                                    4, 7), grid=(3, 1, 1))
+    x = np.random.default_rng(1).standard_normal((12, 7)).astype(np.float32) + 3
+    got = [x, np.zeros_like(x), np.zeros((12, 1), np.float32)]
+    run_register_program(m, got)
+    ref = [x, np.zeros_like(x), np.zeros((12, 1), np.float32)]
+    xt_oracle.run(xt._module_asm(m).split("// b200")[0] + "}", ref)
+    np.testing.assert_array_equal(got[1], ref[1])
+    np.testing.assert_allclose(got[2], ref[2], rtol=1e-6)

@@ -36,6 +36,43 @@ struct Coord {
   bool operator==(const Coord& o) const { return bid == o.bid && dim == o.dim && value == o.value; }
 };
 
+// Linear-scan register file: a value owns its register from its definition
+// to its last use; freeing is by owner, so a register handed to a later value
+// is never released on behalf of an earlier one.
+class RegFile {
+ public:
+  RegFile(int size, std::map<int, int> last_use) : owner_(size, -1), last_use_(std::move(last_use)) {}
+  int alloc(int vid) {
+    for (size_t r = 0; r < owner_.size(); ++r)
+      if (owner_[r] < 0) {
+        owner_[r] = vid;
+        high_ = std::max(high_, static_cast<int>(r) + 1);
+        return static_cast<int>(r);
+      }
+    return -1;
+  }
+  int get(int vid) const {
+    for (size_t r = 0; r < owner_.size(); ++r)
+      if (owner_[r] == vid) return static_cast<int>(r);
+    throw Error(kUnsupported, "internal: value has no register");
+  }
+  bool has(int vid) const { return std::find(owner_.begin(), owner_.end(), vid) != owner_.end(); }
+  // frees the registers of values whose last use is at or before op ``upto``
+  void release_dead(int upto) {
+    for (int& o : owner_)
+      if (o >= 0) {
+        auto it = last_use_.find(o);
+        if (it == last_use_.end() || it->second <= upto) o = -1;
+      }
+  }
+  int high_water() const { return high_; }
+
+ private:
+  std::vector<int> owner_;
+  std::map<int, int> last_use_;
+  int high_ = 0;
+};
+
 struct Access {
   int op = -1;                 // op index
   int arg = -1;                // memref argument position
@@ -109,6 +146,14 @@ class Classifier {
 
   [[noreturn]] void unsupported(const std::string& why) const { throw Error(kUnsupported, why); }
 
+  // value id -> index of the last op that reads it
+  std::map<int, int> last_uses() const {
+    std::map<int, int> last;
+    for (size_t i = 0; i < f_.ops.size(); ++i)
+      for (int v : f_.ops[i].operands) last[v] = static_cast<int>(i);
+    return last;
+  }
+
   const Op* def(int vid) const {
     int d = m_.value(vid).def_op;
     return d < 0 ? nullptr : &f_.ops[d];
@@ -181,24 +226,12 @@ class Classifier {
     if (!ref->idx.empty() && ref->idx[0].bid && ref->idx[0].dim == 0)
       p.bid0_span = ref->tile[0] * (p.numel / ref->array.shape[0]);
 
-    std::map<int, int> reg_of;        // value id -> register
-    std::map<int, int> last_use;      // value id -> op index of last use
-    for (size_t i = 0; i < f_.ops.size(); ++i)
-      for (int v : f_.ops[i].operands) last_use[v] = static_cast<int>(i);
-    std::vector<bool> busy(8, false);
+    RegFile regs(8, last_uses());
     auto alloc = [&](int vid) {
-      for (int r = 0; r < 8; ++r)
-        if (!busy[r]) {
-          busy[r] = true;
-          reg_of[vid] = r;
-          p.n_regs = std::max(p.n_regs, r + 1);
-          return r;
-        }
-      unsupported("the program needs more than 8 live tiles");
-    };
-    auto release_dead = [&](int i) {
-      for (auto& kv : reg_of)
-        if (busy[kv.second] && last_use[kv.first] <= i) busy[kv.second] = false;
+      int r = regs.alloc(vid);
+      if (r < 0) unsupported("the program needs more than 8 live tiles");
+      p.n_regs = std::max(p.n_regs, regs.high_water());
+      return r;
     };
     std::map<int, int> in_slot;
     for (size_t i = 0; i < f_.ops.size(); ++i) {
@@ -208,7 +241,8 @@ class Classifier {
         if (n == "arith.constant" && op.is_dense) unsupported("tensor constants are not supported");
         continue;
       }
-      auto reg = [&](int v) { return static_cast<uint8_t>(reg_of.at(v)); };
+      auto reg = [&](int v) { return static_cast<uint8_t>(regs.get(v)); };
+      regs.release_dead(static_cast<int>(i) - 1);
       if (n == "xt.load") {
         const Access& a = loads_.at(op.results[0]);
         Elem e = a.array.elem;
@@ -253,10 +287,8 @@ class Classifier {
         if (n == "xt.ftoi" && op.result_types[0].elem != Elem::I8) unsupported("ftoi produces i8");
         uint8_t a = reg(op.operands[0]);
         uint8_t b = binary ? reg(op.operands[1]) : 0;
-        release_dead(static_cast<int>(i) - 1);
-        // operands dying at this op may be reused for its result
-        for (int v : op.operands)
-          if (last_use[v] <= static_cast<int>(i)) busy[reg_of[v]] = false;
+        // operands dying at this op may give their register to its result
+        regs.release_dead(static_cast<int>(i));
         int r = alloc(op.results[0]);
         p.code.push_back({it->second, static_cast<uint8_t>(r), a, b});
       }
@@ -302,27 +334,18 @@ class Classifier {
     p.row_axis = axis;
 
     // register allocation for row registers (v) and scalar registers (s)
-    std::map<int, int> last_use;
-    for (size_t i = 0; i < f_.ops.size(); ++i)
-      for (int v : f_.ops[i].operands) last_use[v] = static_cast<int>(i);
-    std::map<int, int> vreg, sreg;
-    std::vector<bool> vbusy(3, false), sbusy(8, false);
+    RegFile vregs(3, last_uses()), sregs(8, last_uses());
     auto is_row = [&](const Type& t) { return t.rank() == 2 && t.shape[1] == C && C != 1; };
     auto free_dead = [&](int i) {
-      for (auto& kv : vreg) if (vbusy[kv.second] && last_use[kv.first] <= i) vbusy[kv.second] = false;
-      for (auto& kv : sreg) if (sbusy[kv.second] && last_use[kv.first] <= i) sbusy[kv.second] = false;
+      vregs.release_dead(i);
+      sregs.release_dead(i);
     };
     auto alloc = [&](int vid, bool row) -> uint8_t {
-      auto& busy = row ? vbusy : sbusy;
-      for (size_t r = 0; r < busy.size(); ++r)
-        if (!busy[r]) {
-          busy[r] = true;
-          (row ? vreg : sreg)[vid] = static_cast<int>(r);
-          if (row) p.n_vregs = std::max(p.n_vregs, static_cast<int>(r) + 1);
-          else p.n_sregs = std::max(p.n_sregs, static_cast<int>(r) + 1);
-          return static_cast<uint8_t>(r);
-        }
-      unsupported(row ? "the row program needs more than 3 live rows" : "too many live row scalars");
+      int r = (row ? vregs : sregs).alloc(vid);
+      if (r < 0) unsupported(row ? "the row program needs more than 3 live rows" : "too many live row scalars");
+      p.n_vregs = vregs.high_water();
+      p.n_sregs = sregs.high_water();
+      return static_cast<uint8_t>(r);
     };
     std::map<int, int> in_slot;
     for (size_t i = 0; i < f_.ops.size(); ++i) {
@@ -361,16 +384,14 @@ class Classifier {
         int slot = p.n_out++;
         p.out_arg[slot] = a->arg;
         p.out_is_scalar[slot] = sc;
-        uint8_t r = static_cast<uint8_t>(sc ? sreg.at(op.operands[0]) : vreg.at(op.operands[0]));
+        uint8_t r = static_cast<uint8_t>(sc ? sregs.get(op.operands[0]) : vregs.get(op.operands[0]));
         p.code.push_back({sc ? kStoreScalar : kStore, static_cast<uint8_t>(slot), r, 0});
         continue;
       }
       const Type& res = op.result_types[0];
       if (res.elem != Elem::F32) unsupported("row programs compute in f32");
       auto operand_reg = [&](int v) -> uint8_t {
-        auto it = vreg.find(v);
-        if (it != vreg.end()) return static_cast<uint8_t>(it->second);
-        return static_cast<uint8_t>(sreg.at(v));
+        return static_cast<uint8_t>(vregs.has(v) ? vregs.get(v) : sregs.get(v));
       };
       if (n == "xt.reduce_max" || n == "xt.reduce_sum") {
         const Attr* ax = find_attr(op.attrs, "axis");
@@ -709,6 +730,45 @@ std::string describe_plan(const Plan& p, int stage) {
       os << (s.kind == kEpiMulRow || s.kind == kEpiMulScalar ? " * " : " + ") << arr(s.arg);
     if (p.gemm.ftoi) os << " -> i8 (round half even, saturate)";
     os << "\n";
+  }
+  if (stage >= 3 && (p.family == Family::Ew || p.family == Family::Rows)) {
+    // the register program the ew / rows kernels interpret
+    static const char* kNames[] = {"?", "load", "store", "add", "sub", "mul", "exp", "cos", "sin",
+                                   "recip", "rsqrt", "sigmoid", "tanh", "silu", "itof", "ftoi",
+                                   "bcast_add", "bcast_sub", "bcast_mul", "rowmax", "rowsum",
+                                   "load_scalar", "store_scalar"};
+    const bool rows = p.family == Family::Rows;
+    const std::vector<Instr>& code = rows ? p.rows.code : p.ew.code;
+    const int* in_arg = rows ? p.rows.in_arg : p.ew.in_arg;
+    const int* out_arg = rows ? p.rows.out_arg : p.ew.out_arg;
+    auto reg = [&](uint8_t op, int r, bool operand_b) {
+      if (!rows) return "r" + std::to_string(r);
+      uint8_t o = op & 0x7f;
+      bool scalar = (op & 0x80) || o == kRowMax || o == kRowSum || o == kLoadScalar ||
+                    (operand_b && (o == kBcastAdd || o == kBcastSub || o == kBcastMul));
+      return (scalar ? "s" : "v") + std::to_string(r);
+    };
+    os << "  //   nova_optimize -> register program (" << code.size() << " ops):\n";
+    for (const Instr& ins : code) {
+      uint8_t o = ins.op & 0x7f;
+      os << "  //     ";
+      if (o == kLoad || o == kLoadScalar) {
+        os << (o == kLoadScalar ? "s" : (rows ? "v" : "r")) << int(ins.dst) << " = " << kNames[o] << " "
+           << arr(in_arg[ins.a]) << "\n";
+      } else if (o == kStore || o == kStoreScalar) {
+        os << kNames[o] << " " << arr(out_arg[ins.dst]) << " <- "
+           << (o == kStoreScalar ? "s" : (rows ? "v" : "r")) << int(ins.a) << "\n";
+      } else if (o == kRowMax || o == kRowSum) {
+        os << "s" << int(ins.dst) << " = " << kNames[o] << " v" << int(ins.a) << "\n";
+      } else {
+        bool binary = o == kAdd || o == kSub || o == kMul || o == kBcastAdd || o == kBcastSub || o == kBcastMul;
+        bool scalar_dst = (ins.op & 0x80) != 0;
+        os << (rows ? (scalar_dst ? "s" : "v") : "r") << int(ins.dst) << " = " << kNames[o] << " "
+           << reg(ins.op, ins.a, false);
+        if (binary) os << ", " << reg(ins.op, ins.b, true);
+        os << "\n";
+      }
+    }
   }
   if (stage >= 4) {
     const char* threads = p.family == Family::Gemm || p.family == Family::Conv

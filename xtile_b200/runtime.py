@@ -31,16 +31,25 @@ def _dtype_map():
     return _TORCH_DTYPES
 
 
+def _signature(module: Module, func: str | None):
+    cache = module.__dict__.setdefault("_launch_sig", {})
+    sig = cache.get(func)
+    if sig is None:
+        dtypes = _dtype_map()
+        sig = cache[func] = [(name, is_memref, elem, tuple(shape), dtypes.get(elem))
+                             for name, is_memref, elem, shape in module.arguments(func)]
+    return sig
+
+
 def _check_arrays(module: Module, arrays: Sequence, func: str | None):
     import torch
 
-    sig = module.arguments(func)
+    sig = _signature(module, func)
     if len(arrays) != len(sig):
         raise ValueError(f"launch expects {len(sig)} arrays "
                          f"({', '.join('%' + s[0] for s in sig)}), got {len(arrays)}")
-    dtypes = _dtype_map()
     device = None
-    for t, (name, is_memref, elem, shape) in zip(arrays, sig):
+    for t, (name, is_memref, elem, shape, dtype) in zip(arrays, sig):
         if not is_memref:
             raise TypeError(f"argument %{name} is not a memref; only memref kernels can be launched")
         if not isinstance(t, torch.Tensor):
@@ -51,10 +60,10 @@ def _check_arrays(module: Module, arrays: Sequence, func: str | None):
             device = t.device
         elif t.device != device:
             raise ValueError(f"array %{name} is on {t.device}, expected {device}")
-        if elem not in dtypes or t.dtype != dtypes[elem]:
+        if dtype is None or t.dtype != dtype:
             raise TypeError(f"array %{name} must be {elem}, got {t.dtype}")
-        if tuple(t.shape) != tuple(shape):
-            raise ValueError(f"array %{name} must have shape {tuple(shape)}, got {tuple(t.shape)}")
+        if t.shape != shape:
+            raise ValueError(f"array %{name} must have shape {shape}, got {tuple(t.shape)}")
         if not t.is_contiguous():
             raise ValueError(f"array %{name} must be contiguous (row-major)")
     return device
@@ -72,9 +81,12 @@ def launch(module: Module, *arrays, func: str | None = None, stream=None,
     lo, hi = (0, 0) if bid0_range is None else bid0_range
     if bid0_range is not None and hi <= lo:
         return
-    with torch.cuda.device(device):
-        _native.launch(module._CAPIPtr, [t.data_ptr() for t in arrays], int(lo), int(hi),
-                       int(handle), func)
+    ptrs = [t.data_ptr() for t in arrays]
+    if torch.cuda.current_device() == device.index:
+        _native.launch(module._CAPIPtr, ptrs, int(lo), int(hi), int(handle), func)
+    else:
+        with torch.cuda.device(device):
+            _native.launch(module._CAPIPtr, ptrs, int(lo), int(hi), int(handle), func)
 
 
 def run(kernel_fn: dsl.KernelFunction, *, args: tuple, grid: tuple, double_buffering: bool = False,
