@@ -118,6 +118,21 @@ int xt_launch(const xt_module* module, const char* func, void* const* args, int 
  * a bounded wait runs out (0: none).  Synchronizes the device. */
 int xt_device_error(uint32_t* out_code);
 
+/* No counterpart in the reference.  Launches a matmul program (the gemm
+ * family only; other families are rejected) exactly like xt_launch, but
+ * without allocating device memory: for callers that cannot call cudaMalloc,
+ * such as engines that reserve all device memory up front, plugin enqueue
+ * paths that must not allocate, or latency-critical paths that cannot absorb
+ * cudaMalloc's implicit synchronisation.  The GEMM's scratch (its 4-byte error
+ * word) lives in a 256-byte static __device__ array that every GPU loading
+ * this library holds until exit; a launch needing more scratch is rejected.
+ * The first call on a device resolves that array's address (make it before
+ * any stream capture).  All calls share the array: each call clears the error
+ * word on its stream first, calls whose kernels overlap on the GPU race on
+ * it, and the word is not reported back. */
+int xt_matmul_launch_noalloc(const xt_module* module, const char* func, void* const* args, int n_args,
+                             int64_t bid0_begin, int64_t bid0_end, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -252,6 +252,21 @@ int launch_plan(const xt::Plan& p, void* const* args, int64_t b0, int64_t b1, cu
 
 }  // namespace
 
+namespace xt {
+
+// Plan of ``func`` (NULL: the first function) for launchers outside this
+// file; throws Error on a missing function or an unsupported program.
+std::shared_ptr<Plan> module_plan(const xt_module* module, const char* func) {
+  const Func* f = find_func(module, func);
+  if (!f) throw Error(kArgumentError, std::string("no function @") + (func ? func : "(first)"));
+  return get_plan(module, *f);
+}
+
+// Records ``msg`` as the calling thread's last error and returns ``code``.
+int record_error(int code, const std::string& msg) { return fail(code, msg); }
+
+}  // namespace xt
+
 extern "C" {
 
 const char* xt_last_error(void) { return g_last_error.c_str(); }
