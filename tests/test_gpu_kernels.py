@@ -309,3 +309,68 @@ def test_launch_rejects_bad_arguments():
         xt.launch(m, a.to(DEV), b.to(DEV))
     with pytest.raises(ValueError, match="outside the grid"):
         xt.launch(m, a.to(DEV), b.to(DEV), c, bid0_range=(0, 5))
+
+
+# ------------------------------------------------------------------ conv
+@xt.kernel
+def conv2d_tiles(inp, filt, out, tile_h, tile_w, cin, cout, kh, kw, ph, pw, dh, dw):
+    n, h, w = xt.bid(0), xt.bid(1), xt.bid(2)
+    f = xt.load(filt, index=(0, 0, 0, 0), shape=(kh, kw, cin, cout), shared=2)
+    y = xt.load_conv2d(inp, f, index=(n, h, w, 0), shape=(1, tile_h, tile_w, cout), group=1,
+                       pad=(ph, pw, ph, pw), stride=(1, 1), dilation=(dh, dw))
+    xt.store(out, index=(n, h, w, 0), tile=y)
+
+
+def conv_case(shape, kshape, tile, dtype, seed, pad=None, dil=(1, 1), blocks=None):
+    n, h, w, c = shape
+    kh, kw, _, ko = kshape
+    th, tw = tile
+    g = gen(seed)
+    if dtype == torch.int8:
+        x = torch.randint(-16, 16, shape, generator=g, dtype=torch.int8)
+        f = torch.randint(-16, 16, kshape, generator=g, dtype=torch.int8)
+    else:
+        x = (torch.randn(*shape, generator=g) * 0.1).to(dtype)
+        f = (torch.randn(*kshape, generator=g) * 0.1).to(dtype)
+    ph, pw = pad if pad is not None else (kh // 2, kw // 2)
+    out = torch.full((n, h, w, ko), float("nan"), device=DEV)
+    grid = (n, (h + th - 1) // th, (w + tw - 1) // tw)
+    m = xt.run(conv2d_tiles, args=(x.to(DEV), f.to(DEV), out, th, tw, c, ko, kh, kw, ph, pw, *dil), grid=grid)
+    assert m.plan()["family"] == "conv"
+    ref = oracle(m, [x, f, torch.zeros(n, h, w, ko)], blocks=blocks)[2]
+    return host(out), ref
+
+
+def test_conv_config4_bf16_sampled():
+    blocks = [(b, hb, 0) for b in (0, 13, 31) for hb in range(7)]
+    got, ref = conv_case((32, 56, 56, 64), (3, 3, 64, 64), (8, 56), torch.bfloat16, 3, blocks=blocks)
+    for b in (0, 13, 31):
+        bf16_close(got[b], ref[b])
+
+
+@pytest.mark.parametrize("shape,kshape,tile,pad,dil", [
+    ((2, 9, 70, 64), (3, 3, 64, 32), (3, 35), None, (1, 1)),     # two W tiles, odd H, ragged tiles
+    ((1, 16, 16, 96), (5, 5, 96, 64), (16, 16), (2, 2), (1, 1)),  # channel chunk past C (zero-filled)
+    ((1, 12, 20, 64), (3, 3, 64, 128), (4, 20), (2, 2), (2, 2)),  # dilation 2, 128 output channels
+])
+def test_conv_bf16_shapes(shape, kshape, tile, pad, dil):
+    got, ref = conv_case(shape, kshape, tile, torch.bfloat16, 4, pad=pad, dil=dil)
+    bf16_close(got, ref)
+
+
+def test_conv_int8_kernels_conv2d_pattern_bit_exact():
+    # kernels/conv2d.py defaults: n=1, 32x64 image, cin=128, cout=64, 3x3, tile 32x64
+    got, ref = conv_case((1, 32, 64, 128), (3, 3, 128, 64), (32, 64), torch.int8, 5)
+    assert np.array_equal(got, ref)
+
+
+def test_conv_bid0_shards_match_full_launch():
+    g = gen(6)
+    x = (torch.randn(8, 14, 14, 64, generator=g) * 0.1).to(torch.bfloat16).to(DEV)
+    f = (torch.randn(3, 3, 64, 64, generator=g) * 0.1).to(torch.bfloat16).to(DEV)
+    full = torch.empty(8, 14, 14, 64, device=DEV)
+    parts = torch.full((8, 14, 14, 64), float("nan"), device=DEV)
+    m = xt.run(conv2d_tiles, args=(x, f, full, 7, 14, 64, 64, 3, 3, 1, 1, 1, 1), grid=(8, 2, 1))
+    for lo, hi in [(0, 3), (3, 8)]:
+        xt.launch(m, x, f, parts, bid0_range=(lo, hi))
+    assert torch.equal(full, parts)

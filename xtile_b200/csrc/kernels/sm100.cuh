@@ -70,26 +70,30 @@ struct Abort {
   uint32_t* error_word;    // global memory, first error code wins
 };
 
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr uint64_t kWaitLimitCycles = 4000000000ull;  // ~2 s at the B200's 1.9-2.0 GHz SM clock
 
 // Waits for the phase of ``bar`` with parity ``parity`` to complete.  Gives up
-// after kWaitLimitNs or when another role aborted; a timeout records ``code``
-// in the error word and raises the CTA's abort flag.  Returns false when
-// giving up.
+// after kWaitLimitCycles SM cycles or when another role aborted; a timeout
+// records ``code`` in the error word and raises the CTA's abort flag.
+// Returns false when giving up.  The limit is checked only every 1024 polls
+// (with the cheap per-SM cycle counter) so the common, short wait costs
+// nothing but the polls themselves.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const Abort& ab, uint32_t code) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
-  while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = 0;
+  uint32_t polls = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if ((++polls & 1023u) != 0) continue;
     if (*ab.flag) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    const uint64_t now = clock64();
+    if (t0 == 0) {
+      t0 = now;
+    } else if (now - t0 > kWaitLimitCycles) {
       *ab.flag = 1;
       atomicCAS(ab.error_word, 0u, code);
       return false;
     }
   }
+  return true;
 }
 
 // Same wait with a short limit and no abort check, for teardown drains.
@@ -111,6 +115,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_addr(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t c0,
+                                            int32_t c1, int32_t c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
 
@@ -198,14 +211,25 @@ __device__ __forceinline__ void tmem_wait_ld() {
 // Shared-memory matrix descriptor: start address, leading / stride byte
 // offsets (all >> 4), version 1 (bits 46-47), base offset 0, swizzle mode in
 // bits 61-63 (2 = 128-byte swizzle).
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+// Layout-type codes (bits 61-63): 2 = 128-byte, 4 = 64-byte, 6 = 32-byte swizzle.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                              uint32_t layout) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFF);
   d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFF) << 16;
   d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFF) << 32;
   d |= 1ull << 46;
-  d |= 2ull << 61;
+  d |= static_cast<uint64_t>(layout & 7) << 61;
   return d;
+}
+
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  return smem_desc(saddr, lbo_bytes, sbo_bytes, 2);
+}
+
+// Layout code of a swizzle span in bytes (128, 64 or 32).
+__host__ __device__ constexpr uint32_t swizzle_layout_code(int span_bytes) {
+  return span_bytes == 128 ? 2u : span_bytes == 64 ? 4u : 6u;
 }
 
 // Instruction descriptor (dense): D format bits 4-5, A format 7-9, B format

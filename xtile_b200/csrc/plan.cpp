@@ -639,7 +639,8 @@ class Classifier {
     if (idx[3].bid || idx[3].value != 0) unsupported("the channel coordinate must be 0");
     if (!(idx == st.idx)) unsupported("the store must use the load_conv2d coordinates");
     if (res.shape[3] != ft.shape[3]) unsupported("the result must hold every filter output channel");
-    if (in.elem != Elem::BF16) unsupported("the tensor-core conv takes bf16 input and filter");
+    if (in.elem != Elem::BF16 && in.elem != Elem::I8)
+      unsupported("the tensor-core conv takes bf16 or int8 input and filter");
     if (st.array.elem != Elem::F32) unsupported("the conv output must be f32");
     c.in_arg = src->second;
     c.filt_arg = filt.arg;
@@ -678,8 +679,9 @@ class Classifier {
     c.OW = cov(idx[2], c.tw, out.shape[2]);
     c.OC = c.KO;
     c.n_axis = idx[0].bid ? idx[0].dim : -1;
-    if (c.C % 8) unsupported("input channels must be a multiple of 8 (16-byte TMA rows)");
-    if (c.KO % 16 || c.KO > 256) unsupported("output channels must be a multiple of 16, at most 256");
+    const int64_t eb = elem_bytes(c.elem);
+    if ((c.C * eb) % 16) unsupported("input channel rows must be multiples of 16 bytes (TMA strides)");
+    if (c.KO % 32 || c.KO > 256) unsupported("output channels must be a multiple of 32, at most 256");
     if (c.stride_h != 1 || c.stride_w != 1) unsupported("strided convolution is not supported yet");
     return c;
   }
