@@ -11,5 +11,5 @@ try:
     native = importlib.import_module("xtile_b200._xtile")
 except ImportError as exc:  # pragma: no cover - exercised only on an unbuilt tree
     raise ImportError(
-        "the xtile_b200 native extension is not built; run `python -m xtile_b200.build` "
+        "the xtile_b200 native extension is not built; run `python xtile_b200/build.py` "
         f"(or __graft_entry__.build()) first: {exc}") from exc

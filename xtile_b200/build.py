@@ -7,7 +7,7 @@
 Objects go to ``xtile_b200/_build``; a source is recompiled when it or any
 header it can include is newer than its object.
 
-    python -m xtile_b200.build [--force]
+    python xtile_b200/build.py [--force]
 """
 from __future__ import annotations
 
