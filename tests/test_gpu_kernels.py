@@ -215,7 +215,10 @@ def test_matmul_bf16_kloop_small():
 
 
 @pytest.mark.parametrize("mnk,tile", [((300, 200, 96), (128, 128, 96)), ((128, 520, 64), (128, 256, 64)),
-                                      ((64, 64, 8), (64, 64, 8))])
+                                      ((64, 64, 8), (64, 64, 8)),
+                                      # 3 k-blocks per tile, 320 tiles: tiles share pipeline groups
+                                      # and most CTAs end inside a group
+                                      ((5120, 2048, 192), (128, 256, 192))])
 def test_matmul_bf16_ragged(mnk, tile):
     M, N, K = mnk
     tm, tn, tk = tile

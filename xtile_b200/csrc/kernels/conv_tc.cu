@@ -7,19 +7,33 @@
 // accumulation); the output is f32.
 //
 // GEMM view: M = output pixels, N = output channels (KO), K = taps x channels.
-// One A tile is 128 GEMM rows = 2 output rows x 64 output columns of one image,
-// 128 bytes of channels each: a single 4D TMA box {channels, 64 w, 2 h, 1 n}
-// per (tap, channel chunk), placed at the tap's shifted (h, w) coordinates.
-// TMA fills coordinates outside the image with zeros, which is exactly the
-// padding (negative starts are allowed; the channel coordinate stays 16-byte
-// aligned).  Filter taps stream through the same smem ring from a 3D view
-// [taps][C][KO] (N-major B operand; its swizzle span, 128/64/32 bytes, is the
-// widest that the KO row divides into, so each MMA's N covers whole atoms).
+// One A tile is 128 GEMM rows = 2 output rows x 64 output columns of one
+// image, 128 bytes of channels each: one 4D TMA box {channels, 64 w, 2 h, 1 n}
+// per k-block (a filter tap and a channel chunk), placed at the tap's shifted
+// (h, w) coordinates.  TMA fills coordinates outside the image with zeros,
+// which is exactly the padding (negative starts are allowed; the channel
+// coordinate stays 128-byte aligned).
 //
-// Roles as in gemm_tc.cu: warp 0 TMA producer, warp 1 one thread issuing
-// tcgen05.mma (M=128, N=KO), warp 2 TMEM allocation (double-buffered
-// accumulator), warps 4-7 epilogue straight from TMEM to NHWC rows.  All
-// waits are bounded; a timeout sets the error word and every role stops.
+// The filter is the N-major B operand, read from a 3D view [taps][C][KO]; its
+// swizzle span (128/64/32 bytes) is the widest the KO row divides into, so
+// each MMA's N covers whole swizzle atoms.  When the whole filter fits in
+// shared memory (72 KiB for 3x3x64x64 bf16) it is loaded once per CTA and a
+// k-block costs one TMA; otherwise each k-block also streams its filter slice.
+//
+// Pipeline: a ring of per-k-block stages, each with an "empty" barrier the
+// MMAs' commit releases; "full" barriers guard groups of G consecutive stages
+// (arrival count G, one arrive.expect_tx per k-block), so the MMA thread
+// waits once per G k-blocks.  A wait issued behind queued MMAs costs a few
+// hundred cycles on sm_100a, which at N = 64 would otherwise cost more than
+// the MMAs themselves.
+//
+// Roles: warp 0 TMA producer, warp 1 one thread issuing tcgen05.mma (M=128,
+// N=KO) into a double-buffered TMEM accumulator, warp 2 TMEM allocation,
+// warps 4-7 the epilogue.  The epilogue reads 32 accumulator columns at a time
+// from TMEM, writes them to a 128-byte-swizzled staging tile in shared memory
+// and stores the tile with one TMA store; the store's tensor map spans only
+// the covered output, so ragged tiles are clipped by TMA.  All waits are
+// bounded; a timeout sets the error word and every role stops.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -34,23 +48,27 @@ using namespace sm100;
 
 constexpr int kThreads = 256;
 constexpr int kBM = 128;
-constexpr int kAStage = kBM * 128;  // 16 KiB
-constexpr int kMaxStages = 8;
+constexpr int kAStage = kBM * 128;    // 16 KiB
+constexpr int kStaging = kBM * 128;   // one 128 x 32-column f32 staging tile
+constexpr int kMaxStages = 12;
+constexpr int kMaxGroups = kMaxStages;
 
 enum : uint32_t { kErrProducer = 0x201, kErrMma = 0x202, kErrEpilogue = 0x203 };
 
 struct Params {
-  float* out;
-  int64_t out_h, out_w, out_c;
   int ON, OH, OW, n_begin;
   int tiles_h, tiles_w, num_tiles;
   int kc;              // channel chunks per tap
   int KH, KW, pad_t, pad_l, dil_h, dil_w;
   int N;               // output channels = MMA N
-  int b_chunks;        // column chunks of the filter tile, b_span bytes wide each
+  int b_chunks;        // column chunks of a k-block's filter slice, b_span bytes wide each
   int b_span;          // swizzle span of the filter operand: 128, 64 or 32 bytes
   uint32_t b_layout;   // UMMA layout code of that span
-  int stages, stage_bytes, b_chunk_bytes;
+  int b_chunk_bytes;   // kCh rows of C x b_span bytes
+  int b_kblock_bytes;  // b_chunks * b_chunk_bytes
+  int resident;        // 1: whole filter loaded once; 0: streamed per k-block
+  int stages, group, stage_bytes;  // ring of ``stages``; full barriers per ``group`` stages
+  int filter_offset, staging_offset, barrier_offset;  // shared-memory layout
   int tmem_cols;
   uint32_t idesc;
   uint32_t* error_word;
@@ -60,8 +78,9 @@ template <int AB>
 struct ConvTraits;
 template <>
 struct ConvTraits<kBF16> {
-  static constexpr int kCh = 64;       // channels per 128-byte chunk
+  static constexpr int kCh = 64;   // channels per 128-byte chunk
   static constexpr int kMmaK = 16;
+  static constexpr int kEb = 2;
   static __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     umma_bf16(d, a, b, idesc, acc);
   }
@@ -70,6 +89,7 @@ template <>
 struct ConvTraits<kI8> {
   static constexpr int kCh = 128;
   static constexpr int kMmaK = 32;
+  static constexpr int kEb = 1;
   static __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     umma_i8(d, a, b, idesc, acc);
   }
@@ -86,36 +106,40 @@ __device__ __forceinline__ void tile_coords(const Params& p, int t, int& n, int&
 template <int AB>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_tc(const __grid_constant__ CUtensorMap tma_in, const __grid_constant__ CUtensorMap tma_f,
-            const __grid_constant__ Params p) {
+            const __grid_constant__ CUtensorMap tma_out, const __grid_constant__ Params p) {
   using T = ConvTraits<AB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.stages * p.stage_bytes);
-  uint64_t* empty = full + kMaxStages;
+  uint8_t* filt = smem + p.filter_offset;
+  uint8_t* staging = smem + p.staging_offset;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.barrier_offset);  // one per group of stages
+  uint64_t* empty = full + kMaxGroups;                                    // one per stage
   uint64_t* tfull = empty + kMaxStages;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* fbar = drain + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fbar + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  const int n_groups = p.stages / p.group;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < p.stages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
+    for (int g = 0; g < n_groups; ++g) mbar_init(&full[g], p.group);
+    for (int s = 0; s < p.stages; ++s) mbar_init(&empty[s], 1);
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 128);
     }
     mbar_init(drain, 1);
+    mbar_init(fbar, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch(&tma_in);
     tma_prefetch(&tma_f);
+    tma_prefetch(&tma_out);
   }
   if (warp == 2) {
     tmem_alloc(tmem_slot, p.tmem_cols);
@@ -127,51 +151,92 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   const Abort ab{abort_flag, p.error_word};
   const int num_kb = p.KH * p.KW * p.kc;
+  const int chunk_elems = p.b_span / T::kEb;
 
   if (warp == 0) {
     if (lane == 0) {
       // -------------------------------------------------------------- producer
-      int stage = 0;
+      if (p.resident) {
+        // The whole filter, k-block by k-block, once per CTA.
+        mbar_arrive_expect_tx(fbar, static_cast<uint32_t>(num_kb * p.b_kblock_bytes));
+        int tap = 0, ci = 0;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          for (int j = 0; j < p.b_chunks; ++j)
+            tma_load_3d(filt + kb * p.b_kblock_bytes + j * p.b_chunk_bytes, &tma_f, fbar, j * chunk_elems,
+                        ci * T::kCh, tap);
+          if (++ci == p.kc) {
+            ci = 0;
+            ++tap;
+          }
+        }
+      }
+      const uint32_t kb_bytes = static_cast<uint32_t>(p.stage_bytes);
+      int stage = 0, grp = 0, gi = 0;
       uint32_t phase = 0;
-      int pending[kMaxStages];
-      for (int s = 0; s < kMaxStages; ++s) pending[s] = -1;
+      uint32_t armed = 0, armed_phase = 0;  // per group: armed at least once / parity of its last arming
       bool ok = true;
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
         int n, h0, w0;
         tile_coords(p, t, n, h0, w0);
+        const int img = p.n_begin + n;
+        int ci = 0, s = 0, tap = 0;
+        int wc = w0 - p.pad_l, hc = h0 - p.pad_t;  // input coordinates of tap (r, s)
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, ab, kErrProducer)) {
             ok = false;
             break;
           }
-          const int tap = kb / p.kc, chunk = kb - tap * p.kc;
-          const int r = tap / p.KW, s = tap - r * p.KW;
           uint8_t* st = smem + stage * p.stage_bytes;
-          mbar_arrive_expect_tx(&full[stage], p.stage_bytes);
-          tma_load_4d(st, &tma_in, &full[stage], chunk * T::kCh, w0 + s * p.dil_w - p.pad_l,
-                      h0 + r * p.dil_h - p.pad_t, p.n_begin + n);
-          const int chunk_elems = p.b_span / (AB == kBF16 ? 2 : 1);
-          for (int j = 0; j < p.b_chunks; ++j)
-            tma_load_3d(st + kAStage + j * p.b_chunk_bytes, &tma_f, &full[stage], j * chunk_elems,
-                        chunk * T::kCh, tap);
-          pending[stage] = static_cast<int>(phase);
-          if (++stage == p.stages) {
+          mbar_arrive_expect_tx(&full[grp], kb_bytes);
+          armed |= 1u << grp;
+          armed_phase = (armed_phase & ~(1u << grp)) | (phase << grp);
+          tma_load_4d(st, &tma_in, &full[grp], ci * T::kCh, wc, hc, img);
+          if (!p.resident)
+            for (int j = 0; j < p.b_chunks; ++j)
+              tma_load_3d(st + kAStage + j * p.b_chunk_bytes, &tma_f, &full[grp], j * chunk_elems, ci * T::kCh,
+                          tap);
+          if (++ci == p.kc) {
+            ci = 0;
+            ++tap;
+            wc += p.dil_w;
+            if (++s == p.KW) {
+              s = 0;
+              wc = w0 - p.pad_l;
+              hc += p.dil_h;
+            }
+          }
+          ++stage;
+          if (++gi == p.group) {
+            gi = 0;
+            ++grp;
+          }
+          if (stage == p.stages) {
             stage = 0;
+            grp = 0;
             phase ^= 1;
           }
         }
       }
-      if (*abort_flag)
-        for (int s = 0; s < p.stages; ++s)
-          if (pending[s] >= 0) mbar_wait_drain(&full[s], static_cast<uint32_t>(pending[s]), 500000000ull);
+      if (*abort_flag) {
+        // Complete the partly armed group with plain arrivals, then wait for
+        // every load still in flight before the CTA's shared memory goes away.
+        for (int i = gi; i > 0 && i < p.group; ++i) mbar_arrive(&full[grp]);
+        for (int g = 0; g < n_groups; ++g)
+          if ((armed >> g) & 1u) mbar_wait_drain(&full[g], (armed_phase >> g) & 1u, 500000000ull);
+        if (p.resident) mbar_wait_drain(fbar, 0, 500000000ull);
+      }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // -------------------------------------------------------------- MMA issuer
-      int stage = 0;
+      int stage = 0, grp = 0, gi = 0;
       uint32_t phase = 0;
       int iter = 0;
-      bool ok = true;
+      bool ok = !p.resident || mbar_wait(fbar, 0, ab, kErrMma);
+      const uint32_t smem_base = smem_addr(smem);
+      const uint32_t filt_base = smem_addr(filt);
+      const uint32_t b_lbo = static_cast<uint32_t>(p.b_chunk_bytes), b_sbo = 8u * p.b_span;
+      const uint32_t b_step = static_cast<uint32_t>(T::kMmaK * p.b_span);
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++iter) {
         const int acc = iter & 1;
         const uint32_t acc_phase = (iter >> 1) & 1;
@@ -179,25 +244,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * (p.tmem_cols / 2);
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, ab, kErrMma)) {
-            ok = false;
-            break;
+          if (gi == 0) {
+            if (!mbar_wait(&full[grp], phase, ab, kErrMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
           }
-          tc_fence_after();
-          const uint32_t a_base = smem_addr(smem + stage * p.stage_bytes);
-          const uint32_t b_base = a_base + kAStage;
+          const uint32_t a_base = smem_base + stage * p.stage_bytes;
+          const uint32_t b_base = p.resident ? filt_base + kb * p.b_kblock_bytes : a_base + kAStage;
+          const uint64_t ad = smem_desc_sw128(a_base, 16, 1024);
+          const uint64_t bd = smem_desc(b_base, b_lbo, b_sbo, p.b_layout);
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint64_t ad = smem_desc_sw128(a_base + k * 32, 16, 1024);
-            // N-major filter tile: chunks of b_span bytes are b_chunk_bytes apart
-            // (LBO), 8-row K groups are 8 * b_span bytes apart (SBO)
-            const uint64_t bd = smem_desc(b_base + k * T::kMmaK * p.b_span, p.b_chunk_bytes, 8 * p.b_span,
-                                          p.b_layout);
-            T::mma(d_tmem, ad, bd, p.idesc, (kb | k) != 0 ? 1u : 0u);
-          }
+          for (int k = 0; k < 4; ++k)
+            // A: K-major, 32 bytes of K per MMA; B: N-major, kMmaK rows of K
+            // (b_span bytes each) per MMA.  Descriptor addresses are in
+            // 16-byte units in the low bits.
+            T::mma(d_tmem, ad + static_cast<uint64_t>(k * 2), bd + static_cast<uint64_t>((k * b_step) >> 4), p.idesc,
+                   (kb | k) != 0 ? 1u : 0u);
           umma_commit(&empty[stage]);
-          if (++stage == p.stages) {
+          ++stage;
+          if (++gi == p.group) {
+            gi = 0;
+            ++grp;
+          }
+          if (stage == p.stages) {
             stage = 0;
+            grp = 0;
             phase ^= 1;
           }
         }
@@ -211,42 +284,56 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue
     const int q = warp - 4;
-    const int row = q * 32 + lane;  // GEMM row of the tile = (hh, ww)
-    const int hh = row >> 6, ww = row & 63;
-    int iter = 0;
+    const int row = q * 32 + lane;  // GEMM row of the tile = (hh, ww) = (row / 64, row % 64)
+    const uint32_t sw = static_cast<uint32_t>(row & 7);
+    const bool leader = threadIdx.x == 128;
+    const int nchunks = p.N / 32;
+    int iter = 0, cc = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++iter) {
       const int acc = iter & 1;
       const uint32_t acc_phase = (iter >> 1) & 1;
-      const bool ok = mbar_wait(&tfull[acc], acc_phase, ab, kErrEpilogue);
-      if (!__all_sync(0xffffffffu, ok)) break;
+      const bool ok = mbar_wait_warp(&tfull[acc], acc_phase, ab, kErrEpilogue);
+      if (named_barrier_or(2, 128, !ok)) break;
       tc_fence_after();
       int n, h0, w0;
       tile_coords(p, t, n, h0, w0);
-      const int h = h0 + hh, w = w0 + ww;
-      const bool valid = h < p.OH && w < p.OW;
-      float* dst = p.out + ((static_cast<int64_t>(p.n_begin + n) * p.out_h + h) * p.out_w + w) * p.out_c;
-      for (int c = 0; c < p.N / 32; ++c) {
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * (p.tmem_cols / 2);
+      for (int c = 0; c < nchunks; ++c, ++cc) {
         uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * (p.tmem_cols / 2) + c * 32,
-                           r);
+        tmem_ld_32x32b_x32(taddr + c * 32, r);
         tmem_wait_ld();
-        if (!valid) continue;
-        float v[32];
+        if (c == nchunks - 1) {
+          tc_fence_before();
+          mbar_arrive(&tempty[acc]);  // accumulator free for the MMAs of tile + 2
+        }
+        // 128-byte swizzled staging row: 16-byte unit j of row goes to unit j ^ (row % 8),
+        // the layout the output tensor map's 128-byte swizzle expects.
+        uint8_t* rowp = staging + (cc & 1) * kStaging + row * 128;
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          v[j] = AB == kI8 ? __int2float_rn(static_cast<int>(r[j])) : __uint_as_float(r[j]);
-        if ((p.out_c & 3) == 0) {
-#pragma unroll
-          for (int j = 0; j < 32; j += 4)
-            __stcs(reinterpret_cast<float4*>(dst + c * 32 + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) dst[c * 32 + j] = v[j];
+        for (int j = 0; j < 8; ++j) {
+          float4 v;
+          if (AB == kI8) {
+            v = make_float4(__int2float_rn(static_cast<int>(r[4 * j])), __int2float_rn(static_cast<int>(r[4 * j + 1])),
+                            __int2float_rn(static_cast<int>(r[4 * j + 2])),
+                            __int2float_rn(static_cast<int>(r[4 * j + 3])));
+          } else {
+            v = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]), __uint_as_float(r[4 * j + 2]),
+                            __uint_as_float(r[4 * j + 3]));
+          }
+          *reinterpret_cast<float4*>(rowp + ((static_cast<uint32_t>(j) ^ sw) << 4)) = v;
+        }
+        fence_proxy_async_smem();
+        // Before the barrier the leader waits until the previous store has read
+        // its buffer: that buffer is the one the next chunk writes.
+        if (leader) bulk_wait_group_read<0>();
+        named_barrier_sync(1, 128);
+        if (leader) {
+          tma_store_4d(&tma_out, staging + (cc & 1) * kStaging, c * 32, w0, h0, p.n_begin + n);
+          bulk_commit_group();
         }
       }
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);
     }
+    if (leader) bulk_wait_group<0>();
   }
   __syncthreads();
   if (warp == 2) {
@@ -259,16 +346,20 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+constexpr int kSmemLimit = 227 * 1024;                              // per-CTA dynamic shared memory
+constexpr int kDataBudget = kSmemLimit - 1024 - 256 - 2 * kStaging;  // stages + resident filter
+constexpr int kResidentLimit = 100 * 1024;
+
 template <int AB>
 cudaError_t launch_typed(const ConvArgs& a, cudaStream_t stream) {
   using T = ConvTraits<AB>;
   auto encode = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
   if (!encode) return cudaErrorInvalidValue;
-  const int eb = AB == kBF16 ? 2 : 1;
+  const int eb = T::kEb;
   const CUtensorMapDataType dt = AB == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUtensorMap m_in, m_f, m_out;
   // input NHWC: dims {C, W, H, N}, box {128 B of channels, 64 w, 2 h, 1 n}
-  CUtensorMap m_in, m_f;
   {
     cuuint64_t dims[4] = {static_cast<cuuint64_t>(a.C), static_cast<cuuint64_t>(a.W), static_cast<cuuint64_t>(a.H),
                           static_cast<cuuint64_t>(a.N)};
@@ -298,11 +389,20 @@ cudaError_t launch_typed(const ConvArgs& a, cudaStream_t stream) {
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
+  // output f32 [N][out_h][out_w][out_c], viewed over the covered extents only
+  // ({KO, OW, OH, n_begin + ON}) so TMA clips ragged tiles; box {32 channels, 64 w, 2 h, 1 n}
+  {
+    cuuint64_t dims[4] = {static_cast<cuuint64_t>(a.KO), static_cast<cuuint64_t>(a.OW),
+                          static_cast<cuuint64_t>(a.OH), static_cast<cuuint64_t>(a.n_begin + a.ON)};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(a.out_c) * 4, static_cast<cuuint64_t>(a.out_w * a.out_c) * 4,
+                             static_cast<cuuint64_t>(a.out_h * a.out_w * a.out_c) * 4};
+    cuuint32_t box[4] = {32, 64, 2, 1};
+    if (encode(&m_out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.out, dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
   Params p{};
-  p.out = a.out;
-  p.out_h = a.out_h;
-  p.out_w = a.out_w;
-  p.out_c = a.out_c;
   p.ON = static_cast<int>(a.ON);
   p.OH = static_cast<int>(a.OH);
   p.OW = static_cast<int>(a.OW);
@@ -322,29 +422,48 @@ cudaError_t launch_typed(const ConvArgs& a, cudaStream_t stream) {
   p.b_layout = swizzle_layout_code(span);
   p.b_chunks = row_bytes / span;
   p.b_chunk_bytes = T::kCh * span;  // kCh rows of C x span bytes of KO
-  p.stage_bytes = kAStage + p.b_chunks * p.b_chunk_bytes;
-  p.stages = (190 * 1024) / p.stage_bytes;
+  p.b_kblock_bytes = p.b_chunks * p.b_chunk_bytes;
+  const int num_kb = p.KH * p.KW * p.kc;
+  const int filter_bytes = num_kb * p.b_kblock_bytes;
+  p.resident = filter_bytes <= kResidentLimit && kDataBudget - filter_bytes >= 4 * kAStage;
+  p.stage_bytes = kAStage + (p.resident ? 0 : p.b_kblock_bytes);
+  const int ring_bytes = kDataBudget - (p.resident ? filter_bytes : 0);
+  p.stages = ring_bytes / p.stage_bytes;
   if (p.stages > kMaxStages) p.stages = kMaxStages;
+  if (p.stages < 2) return cudaErrorInvalidValue;
+  // Largest group of k-blocks per full barrier that divides a tile's k-blocks
+  // (so every CTA's k-block count is whole groups) and leaves two groups in
+  // the ring, so loading one group overlaps the MMAs of the other.
+  p.group = 1;
+  for (int g = 4; g > 1; --g)
+    if (num_kb % g == 0 && 2 * g <= p.stages) {
+      p.group = g;
+      break;
+    }
+  p.stages -= p.stages % p.group;
+  p.filter_offset = p.stages * p.stage_bytes;
+  p.staging_offset = p.filter_offset + (p.resident ? filter_bytes : 0);
+  p.barrier_offset = p.staging_offset + 2 * kStaging;
   int cols = 32;
   while (cols < 2 * p.N) cols *= 2;
   p.tmem_cols = cols;
   p.idesc = instr_desc(AB == kBF16 ? 1 : 2, 1, 1, 0, 1, kBM, static_cast<uint32_t>(p.N));
   p.error_word = a.error_word;
   if (p.num_tiles == 0) return cudaSuccess;
-  const int smem = p.stages * p.stage_bytes + 1024 + 256;
+  const int smem = p.barrier_offset + 256 + 1024;
   cudaError_t e = cudaFuncSetAttribute(conv_tc<AB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  conv_tc<AB><<<p.num_tiles < sms ? p.num_tiles : sms, kThreads, smem, stream>>>(m_in, m_f, p);
+  conv_tc<AB><<<p.num_tiles < sms ? p.num_tiles : sms, kThreads, smem, stream>>>(m_in, m_f, m_out, p);
   return cudaGetLastError();
 }
 
 }  // namespace
 
 cudaError_t launch_conv(const ConvArgs& a, cudaStream_t stream) {
-  if (a.KO % 32 != 0 || a.KO > 256) return cudaErrorInvalidValue;
+  if (a.KO % 32 != 0 || a.KO > 256 || a.out_c % 4 != 0) return cudaErrorInvalidValue;
   if (a.elem == kBF16) return launch_typed<kBF16>(a, stream);
   return launch_typed<kI8>(a, stream);
 }

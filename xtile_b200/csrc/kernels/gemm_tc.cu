@@ -9,8 +9,11 @@
 //
 // Structure (one CTA per SM, persistent over 128 x 256 output tiles):
 //   warp 0      TMA producer: A 128x(128 B) and B (128 B)x256 per stage,
-//               4-stage ring of mbarriers (full: TMA bytes landed,
-//               empty: the MMAs reading the stage completed)
+//               4-stage ring; per stage an "empty" mbarrier (the MMAs that
+//               read it completed), per pair of stages a "full" mbarrier
+//               (arrival count 2: both stages' bytes landed).  The MMA thread
+//               waits once per pair: a wait issued behind queued MMAs costs
+//               a few hundred cycles, as much as two 128x256x16 MMAs.
 //   warp 1      one thread issues tcgen05.mma (M=128, N=256, K=16|32) into a
 //               double-buffered TMEM accumulator (2 x 256 columns)
 //   warp 2      allocates / frees the 512 TMEM columns
@@ -35,6 +38,7 @@ using namespace sm100;
 constexpr int kBM = 128;
 constexpr int kBN = 256;
 constexpr int kStages = 4;
+constexpr int kGroup = 2;                      // stages per "full" barrier (one MMA-side wait each)
 constexpr int kThreads = 256;
 constexpr int kAStage = kBM * 128;             // 16 KiB: 128 rows x 128 B of K
 constexpr int kBStage = kBN * 128;             // 32 KiB: 128 B of K rows... x 256 columns
@@ -128,10 +132,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
+    for (int g = 0; g < kStages / kGroup; ++g) mbar_init(&full[g], kGroup);
+    for (int s = 0; s < kStages; ++s) mbar_init(&empty[s], 1);
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 128);
@@ -158,10 +160,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------------------------------------------------------- producer
-      int stage = 0;
+      int stage = 0, grp = 0, gi = 0;
       uint32_t phase = 0;
-      int pending[kStages];
-      for (int s = 0; s < kStages; ++s) pending[s] = -1;
+      uint32_t armed = 0, armed_phase = 0;  // per group: armed at least once / parity of its last arming
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int mt, nt;
@@ -173,32 +174,43 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], kStageBytes);
-          tma_load_2d(sa + stage * kAStage, &tma_a, &full[stage], kb * T::kBK, row0);
+          mbar_arrive_expect_tx(&full[grp], kStageBytes);
+          armed |= 1u << grp;
+          armed_phase = (armed_phase & ~(1u << grp)) | (phase << grp);
+          tma_load_2d(sa + stage * kAStage, &tma_a, &full[grp], kb * T::kBK, row0);
 #pragma unroll
           for (int c = 0; c < T::kChunks; ++c)
-            tma_load_2d(sb + stage * kBStage + c * T::kChunkBytes, &tma_b, &full[stage],
-                        col0 + c * T::kChunkN, kb * T::kBK);
-          pending[stage] = static_cast<int>(phase);
-          if (++stage == kStages) {
+            tma_load_2d(sb + stage * kBStage + c * T::kChunkBytes, &tma_b, &full[grp], col0 + c * T::kChunkN,
+                        kb * T::kBK);
+          ++stage;
+          if (++gi == kGroup) {
+            gi = 0;
+            ++grp;
+          }
+          if (stage == kStages) {
             stage = 0;
+            grp = 0;
             phase ^= 1;
           }
         }
       }
+      // A CTA whose k-block count is not whole groups ends inside a group:
+      // complete it with plain arrivals so its last wait (and a drain) ends.
+      for (int i = gi; i > 0 && i < kGroup; ++i) mbar_arrive(&full[grp]);
       if (*abort_flag) {
         // let every issued copy land before the CTA's shared memory is released
-        for (int s = 0; s < kStages; ++s)
-          if (pending[s] >= 0) mbar_wait_drain(&full[s], static_cast<uint32_t>(pending[s]), 500000000ull);
+        for (int g = 0; g < kStages / kGroup; ++g)
+          if ((armed >> g) & 1u) mbar_wait_drain(&full[g], (armed_phase >> g) & 1u, 500000000ull);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------------------------------------------------------- MMA issuer
-      int stage = 0;
+      int stage = 0, grp = 0, gi = 0;
       uint32_t phase = 0;
       int iter = 0;
       bool ok = true;
+      const uint32_t sa_base = smem_addr(sa), sb_base = smem_addr(sb);
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++iter) {
         const int acc = iter & 1;
         const uint32_t acc_phase = (iter >> 1) & 1;
@@ -206,25 +218,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kBN;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, ab, kErrMma)) {
-            ok = false;
-            break;
+          if (gi == 0) {
+            // one wait covers the kGroup stages of a group
+            if (!mbar_wait(&full[grp], phase, ab, kErrMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
           }
-          tc_fence_after();
-          const uint32_t a_base = smem_addr(sa + stage * kAStage);
-          const uint32_t b_base = smem_addr(sb + stage * kBStage);
+          // A: K-major, 128-byte swizzle, 32 bytes of K per MMA.  B: N-major,
+          // 128-byte swizzle; chunks of 128 B of N are kChunkBytes apart (LBO),
+          // 8-row K groups 1024 B apart (SBO), kMmaK rows of K per MMA.
+          // Descriptor start addresses are in 16-byte units in the low bits.
+          const uint64_t ad = smem_desc_sw128(sa_base + stage * kAStage, 16, 1024);
+          const uint64_t bd = smem_desc_sw128(sb_base + stage * kBStage, T::kChunkBytes, 1024);
 #pragma unroll
-          for (int k = 0; k < 128 / 32; ++k) {
-            // A: K-major, 128-byte swizzle; step 32 bytes of K inside the row
-            const uint64_t ad = smem_desc_sw128(a_base + k * 32, 16, 1024);
-            // B: N-major, 128-byte swizzle; chunks of 128 B of N are
-            // kChunkBytes apart (LBO), 8-row K groups 1024 B apart (SBO)
-            const uint64_t bd = smem_desc_sw128(b_base + k * T::kMmaK * 128, T::kChunkBytes, 1024);
-            T::mma(d_tmem, ad, bd, (kb | k) != 0 ? 1u : 0u);
-          }
+          for (int k = 0; k < 128 / 32; ++k)
+            T::mma(d_tmem, ad + static_cast<uint64_t>(k * 2), bd + static_cast<uint64_t>(k * T::kMmaK * 8),
+                   (kb | k) != 0 ? 1u : 0u);
           umma_commit(&empty[stage]);
-          if (++stage == kStages) {
+          ++stage;
+          if (++gi == kGroup) {
+            gi = 0;
+            ++grp;
+          }
+          if (stage == kStages) {
             stage = 0;
+            grp = 0;
             phase ^= 1;
           }
         }
@@ -242,8 +262,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++iter) {
       const int acc = iter & 1;
       const uint32_t acc_phase = (iter >> 1) & 1;
-      const bool ok = mbar_wait(&tfull[acc], acc_phase, ab, kErrEpilogue);
-      if (!__all_sync(0xffffffffu, ok)) break;
+      if (!mbar_wait_warp(&tfull[acc], acc_phase, ab, kErrEpilogue)) break;
       tc_fence_after();
       int mt, nt;
       tile_coords(t, p.tiles_m, p.tiles_n, mt, nt);

@@ -96,6 +96,40 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   return true;
 }
 
+// Warp-wide wait for waiters that expect long waits (the epilogue warps wait
+// for a whole tile's MMAs): only lane 0 polls, backing off with __nanosleep,
+// so 128 polling threads do not compete with the single producer and MMA
+// threads for the shared-memory pipe.  Every lane gets lane 0's result; the
+// __syncwarp orders the other lanes after lane 0's observation of the phase.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, const Abort& ab, uint32_t code) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) {
+    uint64_t t0 = 0;
+    uint32_t polls = 0, sleep_ns = 32;
+    while (!mbar_try_wait(bar, parity)) {
+      __nanosleep(sleep_ns);
+      if (sleep_ns < 256) sleep_ns *= 2;
+      if ((++polls & 255u) != 0) continue;
+      if (*ab.flag) {
+        ok = false;
+        break;
+      }
+      const uint64_t now = clock64();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitLimitCycles) {
+        *ab.flag = 1;
+        atomicCAS(ab.error_word, 0u, code);
+        ok = false;
+        break;
+      }
+    }
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok;
+}
+
 // Same wait with a short limit and no abort check, for teardown drains.
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
   const uint64_t t0 = global_timer_ns();
@@ -134,6 +168,61 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_addr(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
+}
+
+// Tiled TMA store from shared memory (bulk-group completion).  Elements of
+// the box outside the tensor map's dims are not written.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int32_t c0, int32_t c1,
+                                             int32_t c2, int32_t c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_addr(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int32_t c0, int32_t c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_addr(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Waits until at most N committed bulk groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Makes this thread's generic-proxy shared-memory writes visible to the
+// async proxy (TMA) before a bulk store reads them.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Barrier among ``count`` threads on hardware barrier ``id`` (id 0 is __syncthreads).
+__device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Barrier among ``count`` threads on barrier ``id`` that also ORs ``pred``
+// over them: every participant gets the same answer.
+__device__ __forceinline__ bool named_barrier_or(uint32_t id, uint32_t count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
 }
 
 // ---------------------------------------------------------------- tcgen05

@@ -682,6 +682,7 @@ class Classifier {
     const int64_t eb = elem_bytes(c.elem);
     if ((c.C * eb) % 16) unsupported("input channel rows must be multiples of 16 bytes (TMA strides)");
     if (c.KO % 32 || c.KO > 256) unsupported("output channels must be a multiple of 32, at most 256");
+    if (c.out_c % 4) unsupported("output channel rows must be multiples of 16 bytes (TMA stores)");
     if (c.stride_h != 1 || c.stride_w != 1) unsupported("strided convolution is not supported yet");
     return c;
   }
