@@ -355,6 +355,9 @@ def test_conv_config4_bf16_sampled():
     ((2, 9, 70, 64), (3, 3, 64, 32), (3, 35), None, (1, 1)),     # two W tiles, odd H, ragged tiles
     ((1, 16, 16, 96), (5, 5, 96, 64), (16, 16), (2, 2), (1, 1)),  # channel chunk past C (zero-filled)
     ((1, 12, 20, 64), (3, 3, 64, 128), (4, 20), (2, 2), (2, 2)),  # dilation 2, 128 output channels
+    ((1, 20, 300, 64), (3, 3, 64, 64), (10, 100), None, (1, 1)),  # window kernel, 4 column strips
+    ((2, 10, 30, 128), (3, 3, 128, 64), (5, 30), None, (1, 1)),   # window kernel, 2 channel chunks
+    ((1, 9, 9, 64), (1, 1, 64, 256), (9, 9), (0, 0), (1, 1)),     # 1x1, 256 output channels
 ])
 def test_conv_bf16_shapes(shape, kshape, tile, pad, dil):
     got, ref = conv_case(shape, kshape, tile, torch.bfloat16, 4, pad=pad, dil=dil)

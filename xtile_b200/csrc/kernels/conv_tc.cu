@@ -342,6 +342,273 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Window variant: one TMA box per (tile, channel chunk) holds every input
+// pixel that the tile's KH x KW taps read, and each tap's A operand is that
+// same shared-memory window starting at a different row.
+//
+// The GEMM rows of a tile are 128 consecutive positions f of a padded-width
+// raster of one strip (image n, output columns [w0, w0 + Wt)): f = h * Wp + w
+// with Wp = Wt + (KW - 1) * dil_w.  Output (h, w0 + w) is valid when w < Wt
+// (and w0 + w < OW, h < OH); the other rows compute values nobody stores.
+// The window is the input box {channels, Wp columns from w0 - pad_l, Hwin
+// rows from h_first - pad_t, image}, written by TMA as 128-byte rows, so tap
+// (r, s) of GEMM row i reads window row (f0 - h_first * Wp) + i
+// + r * dil_h * Wp + s * dil_w: its A descriptor starts at that row.  The
+// 128-byte swizzle is a function of the shared-memory address bits (the
+// window is 1024-byte aligned), so a start at any row needs no descriptor
+// base offset.  Compared with one box per tap, a tile moves 2.7x (3x3,
+// 56-wide rows) instead of 9x its own input bytes from L2.
+//
+// The epilogue stages each 32-column accumulator slice in a 128-byte
+// swizzled buffer, then the 128 epilogue threads copy it out row by row with
+// 16-byte stores (a warp writes four whole 128-byte rows per instruction),
+// skipping the rows that are not output pixels.
+constexpr int kWinMaxStages = 4;
+
+struct WinParams {
+  int ON, OH, OW, n_begin;
+  int Wt, Wp, Hwin, tiles_w, tiles_per_strip, num_tiles;
+  int kc, KH, KW, pad_t, pad_l, dil_h, dil_w;
+  int N;
+  int b_span, b_chunks, b_chunk_bytes, b_kblock_bytes;
+  uint32_t b_layout;
+  int stages, stage_bytes, box_bytes;
+  int filter_offset, staging_offset, barrier_offset;
+  int tmem_cols;
+  uint32_t idesc;
+  float* out;
+  int64_t out_h, out_w, out_c;
+  uint32_t* error_word;
+};
+
+__device__ __forceinline__ void win_tile(const WinParams& p, int t, int& n, int& w0, int& f0) {
+  const int strip = t / p.tiles_per_strip;
+  f0 = (t - strip * p.tiles_per_strip) * kBM;
+  n = strip / p.tiles_w;
+  w0 = (strip - n * p.tiles_w) * p.Wt;
+}
+
+template <int AB>
+__global__ void __launch_bounds__(kThreads, 1)
+    conv_window(const __grid_constant__ CUtensorMap tma_in, const __grid_constant__ CUtensorMap tma_f,
+                const __grid_constant__ WinParams p) {
+  using T = ConvTraits<AB>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* filt = smem + p.filter_offset;
+  uint8_t* staging = smem + p.staging_offset;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.barrier_offset);
+  uint64_t* empty = full + kWinMaxStages;
+  uint64_t* tfull = empty + kWinMaxStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint64_t* fbar = drain + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fbar + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(drain, 1);
+    mbar_init(fbar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch(&tma_in);
+    tma_prefetch(&tma_f);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, p.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const Abort ab{abort_flag, p.error_word};
+  const int n_taps = p.KH * p.KW;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // -------------------------------------------------------------- producer
+      // The whole filter, (tap, chunk) k-block by k-block, once per CTA.
+      const int chunk_elems = p.b_span / T::kEb;
+      mbar_arrive_expect_tx(fbar, static_cast<uint32_t>(n_taps * p.kc * p.b_kblock_bytes));
+      int tap = 0, ci = 0;
+      for (int kb = 0; kb < n_taps * p.kc; ++kb) {
+        for (int j = 0; j < p.b_chunks; ++j)
+          tma_load_3d(filt + kb * p.b_kblock_bytes + j * p.b_chunk_bytes, &tma_f, fbar, j * chunk_elems,
+                      ci * T::kCh, tap);
+        if (++ci == p.kc) {
+          ci = 0;
+          ++tap;
+        }
+      }
+      int stage = 0;
+      uint32_t phase = 0, issued = 0, issued_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        int n, w0, f0;
+        win_tile(p, t, n, w0, f0);
+        const int h_first = f0 / p.Wp;
+        for (int c = 0; c < p.kc; ++c) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, ab, kErrProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(p.box_bytes));
+          issued |= 1u << stage;
+          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+          tma_load_4d(smem + stage * p.stage_bytes, &tma_in, &full[stage], c * T::kCh, w0 - p.pad_l,
+                      h_first - p.pad_t, p.n_begin + n);
+          if (++stage == p.stages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (*abort_flag) {
+        for (int s = 0; s < p.stages; ++s)
+          if ((issued >> s) & 1u) mbar_wait_drain(&full[s], (issued_phase >> s) & 1u, 500000000ull);
+        mbar_wait_drain(fbar, 0, 500000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    // The whole warp runs the loop (warp-uniform descriptor arithmetic); one
+    // elected lane issues each tcgen05 instruction.
+    int stage = 0;
+    uint32_t phase = 0;
+    int iter = 0;
+    bool ok = __all_sync(0xffffffffu, mbar_wait(fbar, 0, ab, kErrMma));
+    const uint32_t smem_base = smem_addr(smem);
+    const uint64_t b_desc0 = smem_desc(smem_addr(filt), p.b_chunk_bytes, 8 * p.b_span, p.b_layout);
+    const uint32_t b_kb16 = static_cast<uint32_t>(p.b_kblock_bytes) >> 4;
+    const uint32_t b_step16 = static_cast<uint32_t>(T::kMmaK * p.b_span) >> 4;
+    const uint32_t r_step16 = static_cast<uint32_t>(p.dil_h * p.Wp) * 8u;  // window rows are 8 x 16 bytes
+    const uint32_t s_step16 = static_cast<uint32_t>(p.dil_w) * 8u;
+    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++iter) {
+      const int acc = iter & 1;
+      const uint32_t acc_phase = (iter >> 1) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&tempty[acc], acc_phase ^ 1, ab, kErrMma))) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * (p.tmem_cols / 2);
+      int n, w0, f0;
+      win_tile(p, t, n, w0, f0);
+      const uint32_t base_row = static_cast<uint32_t>(f0 - (f0 / p.Wp) * p.Wp);
+      for (int c = 0; c < p.kc; ++c) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, ab, kErrMma))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint64_t a_r = smem_desc_sw128(smem_base + stage * p.stage_bytes + base_row * 128u, 16, 1024);
+        int tap = 0;
+        for (int r = 0; r < p.KH; ++r, a_r += r_step16) {
+          uint64_t a_s = a_r;
+          for (int s = 0; s < p.KW; ++s, ++tap, a_s += s_step16) {
+            const uint64_t bd = b_desc0 + static_cast<uint64_t>((tap * p.kc + c) * b_kb16);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              if (elect_sync())
+                T::mma(d_tmem, a_s + static_cast<uint64_t>(2 * k), bd + static_cast<uint64_t>(k * b_step16),
+                       p.idesc, (c | tap | k) != 0 ? 1u : 0u);
+          }
+        }
+        if (elect_sync()) umma_commit(&empty[stage]);
+        if (++stage == p.stages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (ok && elect_sync()) umma_commit(&tfull[acc]);
+    }
+    if (*abort_flag) {
+      if (elect_sync()) umma_commit(drain);
+      mbar_wait_drain(drain, 0, 500000000ull);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp - 4;
+    const int row = q * 32 + lane;  // TMEM lane = GEMM row this thread reads
+    const uint32_t sw = static_cast<uint32_t>(row & 7);
+    const int et = threadIdx.x - 128;
+    const int cu = et & 7;    // 16-byte unit this thread copies out of each staged row
+    const int crow = et >> 3;  // staged rows crow + 16 k, k = 0..7
+    const uint32_t csw = static_cast<uint32_t>(crow & 7);
+    const int nchunks = p.N / 32;
+    int iter = 0, cc = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++iter) {
+      const int acc = iter & 1;
+      const uint32_t acc_phase = (iter >> 1) & 1;
+      const bool ok = mbar_wait_warp(&tfull[acc], acc_phase, ab, kErrEpilogue);
+      if (named_barrier_or(2, 128, !ok)) break;
+      tc_fence_after();
+      int n, w0, f0;
+      win_tile(p, t, n, w0, f0);
+      // output offsets (floats) of the 8 staged rows this thread copies; -1: not an output pixel
+      int64_t goff[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int f = f0 + crow + 16 * k;
+        const int h = f / p.Wp, w = f - h * p.Wp;
+        goff[k] = (h < p.OH && w < p.Wt && w0 + w < p.OW)
+                      ? ((static_cast<int64_t>(p.n_begin + n) * p.out_h + h) * p.out_w + w0 + w) * p.out_c + cu * 4
+                      : -1;
+      }
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * (p.tmem_cols / 2);
+      for (int c = 0; c < nchunks; ++c, ++cc) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, r);
+        tmem_wait_ld();
+        if (c == nchunks - 1) {
+          tc_fence_before();
+          mbar_arrive(&tempty[acc]);  // accumulator free for the MMAs of tile + 2
+        }
+        uint8_t* buf = staging + (cc & 1) * kStaging;
+        uint8_t* rowp = buf + row * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float4 v;
+          if (AB == kI8) {
+            v = make_float4(__int2float_rn(static_cast<int>(r[4 * j])), __int2float_rn(static_cast<int>(r[4 * j + 1])),
+                            __int2float_rn(static_cast<int>(r[4 * j + 2])),
+                            __int2float_rn(static_cast<int>(r[4 * j + 3])));
+          } else {
+            v = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]), __uint_as_float(r[4 * j + 2]),
+                            __uint_as_float(r[4 * j + 3]));
+          }
+          *reinterpret_cast<float4*>(rowp + ((static_cast<uint32_t>(j) ^ sw) << 4)) = v;
+        }
+        // One barrier per slice: a buffer is rewritten two slices later, after
+        // every thread has passed the next slice's barrier, i.e. finished this copy.
+        named_barrier_sync(1, 128);
+        const uint8_t* src = buf + crow * 128 + ((static_cast<uint32_t>(cu) ^ csw) << 4);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (goff[k] >= 0)
+            __stcs(reinterpret_cast<float4*>(p.out + goff[k] + c * 32),
+                   *reinterpret_cast<const float4*>(src + k * 16 * 128));
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, p.tmem_cols);
+  }
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -349,6 +616,80 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 constexpr int kSmemLimit = 227 * 1024;                              // per-CTA dynamic shared memory
 constexpr int kDataBudget = kSmemLimit - 1024 - 256 - 2 * kStaging;  // stages + resident filter
 constexpr int kResidentLimit = 100 * 1024;
+
+// Plans and launches the window kernel when its shapes fit: the filter stays
+// resident, the padded window row is at most 256 pixels (a TMA box limit),
+// at least two window stages fit beside the filter, and at least half of the
+// padded raster is output columns.  Returns false (nothing launched) otherwise.
+template <int AB, class EncodeInput>
+bool launch_window(const ConvArgs& a, const CUtensorMap& m_f, int span, EncodeInput& encode_input, CUtensorMap& m_in,
+                   int sms, cudaStream_t stream, cudaError_t* err) {
+  using T = ConvTraits<AB>;
+  const int eb = T::kEb;
+  WinParams p{};
+  p.KH = static_cast<int>(a.KH);
+  p.KW = static_cast<int>(a.KW);
+  p.dil_h = static_cast<int>(a.dil_h);
+  p.dil_w = static_cast<int>(a.dil_w);
+  p.pad_t = static_cast<int>(a.pad_t);
+  p.pad_l = static_cast<int>(a.pad_l);
+  p.kc = static_cast<int>((a.C + T::kCh - 1) / T::kCh);
+  p.N = static_cast<int>(a.KO);
+  p.b_span = span;
+  p.b_layout = swizzle_layout_code(span);
+  p.b_chunks = p.N * eb / span;
+  p.b_chunk_bytes = T::kCh * span;
+  p.b_kblock_bytes = p.b_chunks * p.b_chunk_bytes;
+  const int filter_bytes = p.KH * p.KW * p.kc * p.b_kblock_bytes;
+  if (filter_bytes > kDataBudget) return false;
+  const int OW = static_cast<int>(a.OW), halo_w = (p.KW - 1) * p.dil_w;
+  bool fits = false;
+  for (int tw = 1; tw <= OW && !fits; ++tw) {
+    p.Wt = (OW + tw - 1) / tw;
+    p.Wp = p.Wt + halo_w;
+    if (2 * p.Wt < p.Wp) return false;  // mostly halo: the per-tap kernel does better
+    if (p.Wp > 256) continue;
+    p.Hwin = (p.Wp - 1 + (p.KH - 1) * p.dil_h * p.Wp + halo_w + kBM + p.Wp - 1) / p.Wp;
+    if (p.Hwin > 256) continue;
+    p.box_bytes = p.Hwin * p.Wp * 128;
+    p.stage_bytes = (p.box_bytes + 1023) & ~1023;
+    p.stages = (kDataBudget - filter_bytes) / p.stage_bytes;
+    if (p.stages > kWinMaxStages) p.stages = kWinMaxStages;
+    fits = p.stages >= 2;
+    p.tiles_w = tw;
+  }
+  if (!fits) return false;
+  if (!encode_input(p.Wp, p.Hwin)) {
+    *err = cudaErrorInvalidValue;
+    return true;
+  }
+  p.ON = static_cast<int>(a.ON);
+  p.OH = static_cast<int>(a.OH);
+  p.OW = OW;
+  p.n_begin = static_cast<int>(a.n_begin);
+  p.tiles_per_strip = (p.OH * p.Wp + kBM - 1) / kBM;
+  p.num_tiles = p.ON * p.tiles_w * p.tiles_per_strip;
+  p.filter_offset = p.stages * p.stage_bytes;
+  p.staging_offset = p.filter_offset + filter_bytes;
+  p.barrier_offset = p.staging_offset + 2 * kStaging;
+  int cols = 32;
+  while (cols < 2 * p.N) cols *= 2;
+  p.tmem_cols = cols;
+  p.idesc = instr_desc(AB == kBF16 ? 1 : 2, 1, 1, 0, 1, kBM, static_cast<uint32_t>(p.N));
+  p.out = a.out;
+  p.out_h = a.out_h;
+  p.out_w = a.out_w;
+  p.out_c = a.out_c;
+  p.error_word = a.error_word;
+  *err = cudaSuccess;
+  if (p.num_tiles == 0) return true;
+  const int smem = p.barrier_offset + 256 + 1024;
+  *err = cudaFuncSetAttribute(conv_window<AB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (*err != cudaSuccess) return true;
+  conv_window<AB><<<p.num_tiles < sms ? p.num_tiles : sms, kThreads, smem, stream>>>(m_in, m_f, p);
+  *err = cudaGetLastError();
+  return true;
+}
 
 template <int AB>
 cudaError_t launch_typed(const ConvArgs& a, cudaStream_t stream) {
@@ -359,18 +700,18 @@ cudaError_t launch_typed(const ConvArgs& a, cudaStream_t stream) {
   const CUtensorMapDataType dt = AB == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUtensorMap m_in, m_f, m_out;
-  // input NHWC: dims {C, W, H, N}, box {128 B of channels, 64 w, 2 h, 1 n}
-  {
+  // input NHWC: dims {C, W, H, N}, box {128 B of channels, box_w, box_h, 1 image}
+  auto encode_input = [&](int box_w, int box_h) {
     cuuint64_t dims[4] = {static_cast<cuuint64_t>(a.C), static_cast<cuuint64_t>(a.W), static_cast<cuuint64_t>(a.H),
                           static_cast<cuuint64_t>(a.N)};
     cuuint64_t strides[3] = {static_cast<cuuint64_t>(a.C) * eb, static_cast<cuuint64_t>(a.W * a.C) * eb,
                              static_cast<cuuint64_t>(a.H * a.W * a.C) * eb};
-    cuuint32_t box[4] = {static_cast<cuuint32_t>(T::kCh), 64, 2, 1};
-    if (encode(&m_in, dt, 4, const_cast<void*>(a.in), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return cudaErrorInvalidValue;
-  }
+    cuuint32_t box[4] = {static_cast<cuuint32_t>(T::kCh), static_cast<cuuint32_t>(box_w),
+                         static_cast<cuuint32_t>(box_h), 1};
+    return encode(&m_in, dt, 4, const_cast<void*>(a.in), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  };
   // The filter is the N-major B operand.  Its swizzle span is the widest of
   // 128 / 64 / 32 bytes that the KO row divides into, so every MMA's N is a
   // whole number of swizzle atoms.
@@ -389,6 +730,14 @@ cudaError_t launch_typed(const ConvArgs& a, cudaStream_t stream) {
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  {
+    cudaError_t e;
+    if (launch_window<AB>(a, m_f, span, encode_input, m_in, sms, stream, &e)) return e;
+  }
+  if (!encode_input(64, 2)) return cudaErrorInvalidValue;
   // output f32 [N][out_h][out_w][out_c], viewed over the covered extents only
   // ({KO, OW, OH, n_begin + ON}) so TMA clips ragged tiles; box {32 channels, 64 w, 2 h, 1 n}
   {
@@ -453,9 +802,6 @@ cudaError_t launch_typed(const ConvArgs& a, cudaStream_t stream) {
   const int smem = p.barrier_offset + 256 + 1024;
   cudaError_t e = cudaFuncSetAttribute(conv_tc<AB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   conv_tc<AB><<<p.num_tiles < sms ? p.num_tiles : sms, kThreads, smem, stream>>>(m_in, m_f, m_out, p);
   return cudaGetLastError();
 }
