@@ -358,6 +358,7 @@ def test_conv_config4_bf16_sampled():
     ((1, 20, 300, 64), (3, 3, 64, 64), (10, 100), None, (1, 1)),  # window kernel, 4 column strips
     ((2, 10, 30, 128), (3, 3, 128, 64), (5, 30), None, (1, 1)),   # window kernel, 2 channel chunks
     ((1, 9, 9, 64), (1, 1, 64, 256), (9, 9), (0, 0), (1, 1)),     # 1x1, 256 output channels
+    ((1, 16, 16, 32), (5, 5, 32, 32), (16, 16), (2, 2), (1, 1)),  # window kernel, any-tap loop
 ])
 def test_conv_bf16_shapes(shape, kshape, tile, pad, dil):
     got, ref = conv_case(shape, kshape, tile, torch.bfloat16, 4, pad=pad, dil=dil)

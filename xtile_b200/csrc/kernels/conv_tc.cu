@@ -347,49 +347,87 @@ __global__ void __launch_bounds__(kThreads, 1)
 // pixel that the tile's KH x KW taps read, and each tap's A operand is that
 // same shared-memory window starting at a different row.
 //
-// The GEMM rows of a tile are 128 consecutive positions f of a padded-width
-// raster of one strip (image n, output columns [w0, w0 + Wt)): f = h * Wp + w
-// with Wp = Wt + (KW - 1) * dil_w.  Output (h, w0 + w) is valid when w < Wt
-// (and w0 + w < OW, h < OH); the other rows compute values nobody stores.
-// The window is the input box {channels, Wp columns from w0 - pad_l, Hwin
-// rows from h_first - pad_t, image}, written by TMA as 128-byte rows, so tap
-// (r, s) of GEMM row i reads window row (f0 - h_first * Wp) + i
+// The GEMM rows of a tile are 128 * sub consecutive positions f of a
+// padded-width raster of one strip (image n, output columns [w0, w0 + Wt)):
+// f = h * Wp + w with Wp = Wt + (KW - 1) * dil_w.  Output (h, w0 + w) is valid
+// when w < Wt (and w0 + w < OW, h < OH); the other rows compute values nobody
+// stores.  The window is the input box {channels, Wp columns from w0 - pad_l,
+// Hwin rows from h_first - pad_t, image}, written by TMA as 128-byte rows, so
+// tap (r, s) of GEMM row i reads window row (f0 - h_first * Wp) + i
 // + r * dil_h * Wp + s * dil_w: its A descriptor starts at that row.  The
 // 128-byte swizzle is a function of the shared-memory address bits (the
 // window is 1024-byte aligned), so a start at any row needs no descriptor
-// base offset.  Compared with one box per tap, a tile moves 2.7x (3x3,
-// 56-wide rows) instead of 9x its own input bytes from L2.
+// base offset.  A tile of sub = 2 M=128 sub-tiles shares one window and one
+// pair of barrier waits; for the 3x3, 56-wide case a tile moves 2x its own
+// input bytes from L2 (one box per tap would move 9x).
 //
-// The epilogue stages each 32-column accumulator slice in a 128-byte
-// swizzled buffer, then the 128 epilogue threads copy it out row by row with
-// 16-byte stores (a warp writes four whole 128-byte rows per instruction),
-// skipping the rows that are not output pixels.
+// The MMA warp issues a whole (tile, chunk) burst - sub x taps x 4 MMAs -
+// from one elected lane with every descriptor offset precomputed: with N = 64
+// the tensor pipe is bound by the issue rate, and a burst issues about 1.8x
+// faster than a loop that elects a lane per MMA.
+//
+// With N = 64 each 128x64x16 MMA reads 6 KiB of operands from shared memory,
+// so the MMAs are bound by shared-memory bandwidth (about 128 B per cycle),
+// not by the tensor pipe; nothing else in the kernel goes through shared
+// memory except the TMA window writes.  The epilogue reads two 32-column
+// accumulator slices per TMEM wait and each thread stores its own output
+// pixel's 128-byte slices from registers.
 constexpr int kWinMaxStages = 4;
+constexpr int kMaxFBars = 8;
 
 struct WinParams {
   int ON, OH, OW, n_begin;
   int Wt, Wp, Hwin, tiles_w, tiles_per_strip, num_tiles;
+  int sub;  // M=128 sub-tiles per tile (1 or 2)
   int kc, KH, KW, pad_t, pad_l, dil_h, dil_w;
   int N;
   int b_span, b_chunks, b_chunk_bytes, b_kblock_bytes;
   uint32_t b_layout;
   int stages, stage_bytes, box_bytes;
-  int filter_offset, staging_offset, barrier_offset;
+  int filter_offset, barrier_offset;
   int tmem_cols;
   uint32_t idesc;
   float* out;
   int64_t out_h, out_w, out_c;
+  int v8;  // output rows 32-byte aligned: 32-byte stores
   uint32_t* error_word;
 };
 
 __device__ __forceinline__ void win_tile(const WinParams& p, int t, int& n, int& w0, int& f0) {
   const int strip = t / p.tiles_per_strip;
-  f0 = (t - strip * p.tiles_per_strip) * kBM;
+  f0 = (t - strip * p.tiles_per_strip) * (kBM * p.sub);
   n = strip / p.tiles_w;
   w0 = (strip - n * p.tiles_w) * p.Wt;
 }
 
+// Stores 32 accumulator columns (f32, or s32 converted to f32) to 128
+// contiguous bytes of global memory with streaming stores: 32-byte stores
+// when ``dst`` is 32-byte aligned (half the store requests of 16-byte ones,
+// which matters because every thread writes a different output row), else
+// 16-byte stores.
 template <int AB>
+__device__ __forceinline__ float acc_value(uint32_t r) {
+  return AB == kI8 ? __int2float_rn(static_cast<int>(r)) : __uint_as_float(r);
+}
+
+template <int AB>
+__device__ __forceinline__ void store_row(float* dst, const uint32_t (&r)[32], bool v8) {
+  if (v8) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      st_global_cs_v8(dst + 8 * j, acc_value<AB>(r[8 * j]), acc_value<AB>(r[8 * j + 1]), acc_value<AB>(r[8 * j + 2]),
+                      acc_value<AB>(r[8 * j + 3]), acc_value<AB>(r[8 * j + 4]), acc_value<AB>(r[8 * j + 5]),
+                      acc_value<AB>(r[8 * j + 6]), acc_value<AB>(r[8 * j + 7]));
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      __stcs(reinterpret_cast<float4*>(dst) + j, make_float4(acc_value<AB>(r[4 * j]), acc_value<AB>(r[4 * j + 1]),
+                                                             acc_value<AB>(r[4 * j + 2]), acc_value<AB>(r[4 * j + 3])));
+  }
+}
+
+// KH_ x KW_ > 0: taps known at compile time (unrolled bursts); 0: any shape.
+template <int AB, int KH_, int KW_>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_window(const __grid_constant__ CUtensorMap tma_in, const __grid_constant__ CUtensorMap tma_f,
                 const __grid_constant__ WinParams p) {
@@ -397,14 +435,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* filt = smem + p.filter_offset;
-  uint8_t* staging = smem + p.staging_offset;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.barrier_offset);
   uint64_t* empty = full + kWinMaxStages;
   uint64_t* tfull = empty + kWinMaxStages;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint64_t* fbar = drain + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fbar + 1);
+  uint64_t* fbar = drain + 1;  // one per filter row (rows past the last barrier share it)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fbar + kMaxFBars);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -419,7 +456,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty[a], 128);
     }
     mbar_init(drain, 1);
-    mbar_init(fbar, 1);
+    for (int g = 0; g < kMaxFBars; ++g) mbar_init(&fbar[g], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -436,24 +473,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const Abort ab{abort_flag, p.error_word};
-  const int n_taps = p.KH * p.KW;
+  const int n_fbars = p.KH < kMaxFBars ? p.KH : kMaxFBars;
 
   if (warp == 0) {
     if (lane == 0) {
       // -------------------------------------------------------------- producer
-      // The whole filter, (tap, chunk) k-block by k-block, once per CTA.
+      // The first window goes out before the filter so the two loads overlap.
       const int chunk_elems = p.b_span / T::kEb;
-      mbar_arrive_expect_tx(fbar, static_cast<uint32_t>(n_taps * p.kc * p.b_kblock_bytes));
-      int tap = 0, ci = 0;
-      for (int kb = 0; kb < n_taps * p.kc; ++kb) {
-        for (int j = 0; j < p.b_chunks; ++j)
-          tma_load_3d(filt + kb * p.b_kblock_bytes + j * p.b_chunk_bytes, &tma_f, fbar, j * chunk_elems,
-                      ci * T::kCh, tap);
-        if (++ci == p.kc) {
-          ci = 0;
-          ++tap;
+      bool filter_pending = true;
+      auto load_filter = [&]() {
+        // The whole filter, (tap, chunk) k-block by k-block, once per CTA, one
+        // barrier per filter row: the first tile's MMAs start on row 0 while
+        // the other rows are still in flight.
+        int tap = 0, ci = 0, kb = 0;
+        for (int g = 0; g < n_fbars; ++g) {
+          const int rows = g + 1 < n_fbars ? 1 : p.KH - g;
+          const int kbs = rows * p.KW * p.kc;
+          mbar_arrive_expect_tx(&fbar[g], static_cast<uint32_t>(kbs * p.b_kblock_bytes));
+          for (int i = 0; i < kbs; ++i, ++kb) {
+            for (int j = 0; j < p.b_chunks; ++j)
+              tma_load_3d(filt + kb * p.b_kblock_bytes + j * p.b_chunk_bytes, &tma_f, &fbar[g], j * chunk_elems,
+                          ci * T::kCh, tap);
+            if (++ci == p.kc) {
+              ci = 0;
+              ++tap;
+            }
+          }
         }
-      }
+        filter_pending = false;
+      };
       int stage = 0;
       uint32_t phase = 0, issued = 0, issued_phase = 0;
       bool ok = true;
@@ -471,38 +519,52 @@ __global__ void __launch_bounds__(kThreads, 1)
           issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
           tma_load_4d(smem + stage * p.stage_bytes, &tma_in, &full[stage], c * T::kCh, w0 - p.pad_l,
                       h_first - p.pad_t, p.n_begin + n);
+          if (filter_pending) load_filter();
           if (++stage == p.stages) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
+      if (filter_pending) load_filter();
       if (*abort_flag) {
         for (int s = 0; s < p.stages; ++s)
           if ((issued >> s) & 1u) mbar_wait_drain(&full[s], (issued_phase >> s) & 1u, 500000000ull);
-        mbar_wait_drain(fbar, 0, 500000000ull);
+        for (int g = 0; g < n_fbars; ++g) mbar_wait_drain(&fbar[g], 0, 500000000ull);
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    // The whole warp runs the loop (warp-uniform descriptor arithmetic); one
-    // elected lane issues each tcgen05 instruction.
+    // The warp runs the loop converged; one elected lane issues each burst.
+    constexpr bool kFixed = KH_ > 0 && KW_ > 0;
+    constexpr int kTaps = kFixed ? KH_ * KW_ : 1;
+    constexpr int kKW = kFixed ? KW_ : 1;
     int stage = 0;
     uint32_t phase = 0;
     int iter = 0;
-    bool ok = __all_sync(0xffffffffu, mbar_wait(fbar, 0, ab, kErrMma));
+    bool ok = true;
+    bool first = true;  // the first chunk of the first tile waits for the filter, row by row
     const uint32_t smem_base = smem_addr(smem);
     const uint64_t b_desc0 = smem_desc(smem_addr(filt), p.b_chunk_bytes, 8 * p.b_span, p.b_layout);
     const uint32_t b_kb16 = static_cast<uint32_t>(p.b_kblock_bytes) >> 4;
     const uint32_t b_step16 = static_cast<uint32_t>(T::kMmaK * p.b_span) >> 4;
-    const uint32_t r_step16 = static_cast<uint32_t>(p.dil_h * p.Wp) * 8u;  // window rows are 8 x 16 bytes
+    // Descriptor offsets in 16-byte units: window rows are 128 bytes (8 units),
+    // 32 bytes of K per MMA step along a row.
+    uint32_t a_tap[kTaps], b_tap[kTaps];
+#pragma unroll
+    for (int t = 0; t < kTaps; ++t) {
+      a_tap[t] = kFixed ? static_cast<uint32_t>(((t / kKW) * p.dil_h * p.Wp + (t % kKW) * p.dil_w) * 8) : 0u;
+      b_tap[t] = static_cast<uint32_t>(t * p.kc) * b_kb16;
+    }
+    const uint32_t r_step16 = static_cast<uint32_t>(p.dil_h * p.Wp) * 8u;
     const uint32_t s_step16 = static_cast<uint32_t>(p.dil_w) * 8u;
+    const uint32_t half_cols = static_cast<uint32_t>(p.tmem_cols / 2);
     for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++iter) {
       const int acc = iter & 1;
       const uint32_t acc_phase = (iter >> 1) & 1;
       if (!__all_sync(0xffffffffu, mbar_wait(&tempty[acc], acc_phase ^ 1, ab, kErrMma))) break;
       tc_fence_after();
-      const uint32_t d_tmem = tmem_base + acc * (p.tmem_cols / 2);
+      const uint32_t d_tmem = tmem_base + acc * half_cols;
       int n, w0, f0;
       win_tile(p, t, n, w0, f0);
       const uint32_t base_row = static_cast<uint32_t>(f0 - (f0 / p.Wp) * p.Wp);
@@ -512,93 +574,117 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        uint64_t a_r = smem_desc_sw128(smem_base + stage * p.stage_bytes + base_row * 128u, 16, 1024);
-        int tap = 0;
-        for (int r = 0; r < p.KH; ++r, a_r += r_step16) {
-          uint64_t a_s = a_r;
-          for (int s = 0; s < p.KW; ++s, ++tap, a_s += s_step16) {
-            const uint64_t bd = b_desc0 + static_cast<uint64_t>((tap * p.kc + c) * b_kb16);
+        const uint64_t a0 = smem_desc_sw128(smem_base + stage * p.stage_bytes + base_row * 128u, 16, 1024);
+        const uint64_t b0 = b_desc0 + static_cast<uint64_t>(c * b_kb16);
+        if (kFixed) {
+          // one burst per filter row
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              if (elect_sync())
-                T::mma(d_tmem, a_s + static_cast<uint64_t>(2 * k), bd + static_cast<uint64_t>(k * b_step16),
-                       p.idesc, (c | tap | k) != 0 ? 1u : 0u);
+          for (int r = 0; r < KH_; ++r) {
+            if (first && r < n_fbars) {
+              ok = __all_sync(0xffffffffu, mbar_wait(&fbar[r], 0, ab, kErrMma));
+              if (!ok) break;
+              tc_fence_after();
+            }
+            if (elect_sync()) {
+              for (int s = 0; s < p.sub; ++s) {
+                const uint64_t as = a0 + static_cast<uint64_t>(s * kBM * 8);  // sub-tile s: window rows + 128 s
+                const uint32_t ds = d_tmem + static_cast<uint32_t>(s * p.N);
+#pragma unroll
+                for (int q = 0; q < kKW; ++q)
+#pragma unroll
+                  for (int k = 0; k < 4; ++k)
+                    T::mma(ds, as + a_tap[r * kKW + q] + 2 * k, b0 + b_tap[r * kKW + q] + k * b_step16, p.idesc,
+                           (c | r | q | k) != 0 ? 1u : 0u);
+              }
+              if (r == KH_ - 1) umma_commit(&empty[stage]);
+            }
+            __syncwarp();
           }
+          if (!ok) break;
+        } else {
+          for (int s = 0; s < p.sub; ++s) {
+            const uint32_t ds = d_tmem + static_cast<uint32_t>(s * p.N);
+            uint64_t a_r = a0 + static_cast<uint64_t>(s * kBM * 8);
+            int tap = 0;
+            for (int r = 0; r < p.KH && ok; ++r, a_r += r_step16) {
+              if (first && s == 0 && r < n_fbars) {
+                ok = __all_sync(0xffffffffu, mbar_wait(&fbar[r], 0, ab, kErrMma));
+                if (!ok) break;
+                tc_fence_after();
+              }
+              uint64_t a_s = a_r;
+              for (int q = 0; q < p.KW; ++q, ++tap, a_s += s_step16) {
+                const uint64_t bd = b0 + static_cast<uint64_t>(tap * p.kc) * b_kb16;
+                if (elect_sync()) {
+#pragma unroll
+                  for (int k = 0; k < 4; ++k)
+                    T::mma(ds, a_s + 2 * k, bd + k * b_step16, p.idesc, (c | tap | k) != 0 ? 1u : 0u);
+                }
+                __syncwarp();
+              }
+            }
+          }
+          if (!ok) break;
+          if (elect_sync()) umma_commit(&empty[stage]);
+          __syncwarp();
         }
-        if (elect_sync()) umma_commit(&empty[stage]);
+        first = false;
         if (++stage == p.stages) {
           stage = 0;
           phase ^= 1;
         }
       }
-      if (ok && elect_sync()) umma_commit(&tfull[acc]);
+      if (ok) {
+        if (elect_sync()) umma_commit(&tfull[acc]);
+        __syncwarp();
+      }
     }
     if (*abort_flag) {
       if (elect_sync()) umma_commit(drain);
+      __syncwarp();
       mbar_wait_drain(drain, 0, 500000000ull);
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue
+    // Each thread owns one GEMM row (one output pixel) of a sub-tile and
+    // stores its accumulator slices straight from registers: 128 contiguous
+    // bytes per 32 columns.  Staging through shared memory would add 64 KiB
+    // of shared-memory traffic per sub-tile, and with N = 64 the MMAs' operand
+    // reads already use most of the shared-memory bandwidth.
     const int q = warp - 4;
-    const int row = q * 32 + lane;  // TMEM lane = GEMM row this thread reads
-    const uint32_t sw = static_cast<uint32_t>(row & 7);
-    const int et = threadIdx.x - 128;
-    const int cu = et & 7;    // 16-byte unit this thread copies out of each staged row
-    const int crow = et >> 3;  // staged rows crow + 16 k, k = 0..7
-    const uint32_t csw = static_cast<uint32_t>(crow & 7);
+    const int row = q * 32 + lane;  // TMEM lane = GEMM row within a sub-tile
     const int nchunks = p.N / 32;
-    int iter = 0, cc = 0;
+    const uint32_t half_cols = static_cast<uint32_t>(p.tmem_cols / 2);
+    int iter = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++iter) {
       const int acc = iter & 1;
       const uint32_t acc_phase = (iter >> 1) & 1;
-      const bool ok = mbar_wait_warp(&tfull[acc], acc_phase, ab, kErrEpilogue);
-      if (named_barrier_or(2, 128, !ok)) break;
+      if (!mbar_wait_warp(&tfull[acc], acc_phase, ab, kErrEpilogue)) break;
       tc_fence_after();
       int n, w0, f0;
       win_tile(p, t, n, w0, f0);
-      // output offsets (floats) of the 8 staged rows this thread copies; -1: not an output pixel
-      int64_t goff[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int f = f0 + crow + 16 * k;
+      for (int s = 0; s < p.sub; ++s) {
+        const int f = f0 + s * kBM + row;
         const int h = f / p.Wp, w = f - h * p.Wp;
-        goff[k] = (h < p.OH && w < p.Wt && w0 + w < p.OW)
-                      ? ((static_cast<int64_t>(p.n_begin + n) * p.out_h + h) * p.out_w + w0 + w) * p.out_c + cu * 4
-                      : -1;
-      }
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * (p.tmem_cols / 2);
-      for (int c = 0; c < nchunks; ++c, ++cc) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(taddr + c * 32, r);
-        tmem_wait_ld();
-        if (c == nchunks - 1) {
-          tc_fence_before();
-          mbar_arrive(&tempty[acc]);  // accumulator free for the MMAs of tile + 2
-        }
-        uint8_t* buf = staging + (cc & 1) * kStaging;
-        uint8_t* rowp = buf + row * 128;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float4 v;
-          if (AB == kI8) {
-            v = make_float4(__int2float_rn(static_cast<int>(r[4 * j])), __int2float_rn(static_cast<int>(r[4 * j + 1])),
-                            __int2float_rn(static_cast<int>(r[4 * j + 2])),
-                            __int2float_rn(static_cast<int>(r[4 * j + 3])));
-          } else {
-            v = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]), __uint_as_float(r[4 * j + 2]),
-                            __uint_as_float(r[4 * j + 3]));
+        const bool valid = h < p.OH && w < p.Wt && w0 + w < p.OW;
+        float* dst = p.out + ((static_cast<int64_t>(p.n_begin + n) * p.out_h + h) * p.out_w + w0 + w) * p.out_c;
+        const uint32_t taddr =
+            tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * half_cols + static_cast<uint32_t>(s * p.N);
+        for (int c = 0; c < nchunks; c += 2) {
+          const bool two = c + 1 < nchunks;
+          uint32_t r0[32], r1[32];
+          tmem_ld_32x32b_x32(taddr + c * 32, r0);
+          if (two) tmem_ld_32x32b_x32(taddr + (c + 1) * 32, r1);
+          tmem_wait_ld();
+          if (s == p.sub - 1 && c + 2 >= nchunks) {
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);  // accumulators free for the MMAs of tile + 2
           }
-          *reinterpret_cast<float4*>(rowp + ((static_cast<uint32_t>(j) ^ sw) << 4)) = v;
+          if (valid) {
+            store_row<AB>(dst + c * 32, r0, p.v8);
+            if (two) store_row<AB>(dst + (c + 1) * 32, r1, p.v8);
+          }
         }
-        // One barrier per slice: a buffer is rewritten two slices later, after
-        // every thread has passed the next slice's barrier, i.e. finished this copy.
-        named_barrier_sync(1, 128);
-        const uint8_t* src = buf + crow * 128 + ((static_cast<uint32_t>(cu) ^ csw) << 4);
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-          if (goff[k] >= 0)
-            __stcs(reinterpret_cast<float4*>(p.out + goff[k] + c * 32),
-                   *reinterpret_cast<const float4*>(src + k * 16 * 128));
       }
     }
   }
@@ -616,11 +702,14 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 constexpr int kSmemLimit = 227 * 1024;                              // per-CTA dynamic shared memory
 constexpr int kDataBudget = kSmemLimit - 1024 - 256 - 2 * kStaging;  // stages + resident filter
 constexpr int kResidentLimit = 100 * 1024;
+constexpr int kWinDataBudget = kSmemLimit - 1024 - 256;              // window stages + filter
 
 // Plans and launches the window kernel when its shapes fit: the filter stays
 // resident, the padded window row is at most 256 pixels (a TMA box limit),
 // at least two window stages fit beside the filter, and at least half of the
-// padded raster is output columns.  Returns false (nothing launched) otherwise.
+// padded raster is output columns.  Tiles of two M=128 sub-tiles are used
+// when their window and accumulators fit.  Returns false (nothing launched)
+// otherwise.
 template <int AB, class EncodeInput>
 bool launch_window(const ConvArgs& a, const CUtensorMap& m_f, int span, EncodeInput& encode_input, CUtensorMap& m_in,
                    int sms, cudaStream_t stream, cudaError_t* err) {
@@ -641,22 +730,25 @@ bool launch_window(const ConvArgs& a, const CUtensorMap& m_f, int span, EncodeIn
   p.b_chunk_bytes = T::kCh * span;
   p.b_kblock_bytes = p.b_chunks * p.b_chunk_bytes;
   const int filter_bytes = p.KH * p.KW * p.kc * p.b_kblock_bytes;
-  if (filter_bytes > kDataBudget) return false;
+  if (filter_bytes > kWinDataBudget) return false;
   const int OW = static_cast<int>(a.OW), halo_w = (p.KW - 1) * p.dil_w;
   bool fits = false;
-  for (int tw = 1; tw <= OW && !fits; ++tw) {
-    p.Wt = (OW + tw - 1) / tw;
-    p.Wp = p.Wt + halo_w;
-    if (2 * p.Wt < p.Wp) return false;  // mostly halo: the per-tap kernel does better
-    if (p.Wp > 256) continue;
-    p.Hwin = (p.Wp - 1 + (p.KH - 1) * p.dil_h * p.Wp + halo_w + kBM + p.Wp - 1) / p.Wp;
-    if (p.Hwin > 256) continue;
-    p.box_bytes = p.Hwin * p.Wp * 128;
-    p.stage_bytes = (p.box_bytes + 1023) & ~1023;
-    p.stages = (kDataBudget - filter_bytes) / p.stage_bytes;
-    if (p.stages > kWinMaxStages) p.stages = kWinMaxStages;
-    fits = p.stages >= 2;
-    p.tiles_w = tw;
+  for (int sub = 4 * p.N <= 512 ? 2 : 1; sub >= 1 && !fits; --sub) {
+    for (int tw = 1; tw <= OW && !fits; ++tw) {
+      p.Wt = (OW + tw - 1) / tw;
+      p.Wp = p.Wt + halo_w;
+      if (2 * p.Wt < p.Wp) break;  // mostly halo: the per-tap kernel does better
+      if (p.Wp > 256) continue;
+      p.Hwin = (p.Wp - 1 + (p.KH - 1) * p.dil_h * p.Wp + halo_w + kBM * sub + p.Wp - 1) / p.Wp;
+      if (p.Hwin > 256) continue;
+      p.box_bytes = p.Hwin * p.Wp * 128;
+      p.stage_bytes = (p.box_bytes + 1023) & ~1023;
+      p.stages = (kWinDataBudget - filter_bytes) / p.stage_bytes;
+      if (p.stages > kWinMaxStages) p.stages = kWinMaxStages;
+      fits = p.stages >= 2;
+      p.tiles_w = tw;
+      p.sub = sub;
+    }
   }
   if (!fits) return false;
   if (!encode_input(p.Wp, p.Hwin)) {
@@ -667,27 +759,36 @@ bool launch_window(const ConvArgs& a, const CUtensorMap& m_f, int span, EncodeIn
   p.OH = static_cast<int>(a.OH);
   p.OW = OW;
   p.n_begin = static_cast<int>(a.n_begin);
-  p.tiles_per_strip = (p.OH * p.Wp + kBM - 1) / kBM;
+  p.tiles_per_strip = (p.OH * p.Wp + kBM * p.sub - 1) / (kBM * p.sub);
   p.num_tiles = p.ON * p.tiles_w * p.tiles_per_strip;
   p.filter_offset = p.stages * p.stage_bytes;
-  p.staging_offset = p.filter_offset + filter_bytes;
-  p.barrier_offset = p.staging_offset + 2 * kStaging;
+  p.barrier_offset = p.filter_offset + filter_bytes;
   int cols = 32;
-  while (cols < 2 * p.N) cols *= 2;
+  while (cols < 2 * p.sub * p.N) cols *= 2;
   p.tmem_cols = cols;
   p.idesc = instr_desc(AB == kBF16 ? 1 : 2, 1, 1, 0, 1, kBM, static_cast<uint32_t>(p.N));
   p.out = a.out;
   p.out_h = a.out_h;
   p.out_w = a.out_w;
   p.out_c = a.out_c;
+  p.v8 = a.out_c % 8 == 0 && reinterpret_cast<uintptr_t>(a.out) % 32 == 0;
   p.error_word = a.error_word;
   *err = cudaSuccess;
   if (p.num_tiles == 0) return true;
   const int smem = p.barrier_offset + 256 + 1024;
-  *err = cudaFuncSetAttribute(conv_window<AB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (*err != cudaSuccess) return true;
-  conv_window<AB><<<p.num_tiles < sms ? p.num_tiles : sms, kThreads, smem, stream>>>(m_in, m_f, p);
-  *err = cudaGetLastError();
+  const int grid = p.num_tiles < sms ? p.num_tiles : sms;
+  auto go = [&](auto kernel) {
+    *err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (*err != cudaSuccess) return;
+    kernel<<<grid, kThreads, smem, stream>>>(m_in, m_f, p);
+    *err = cudaGetLastError();
+  };
+  if (p.KH == 3 && p.KW == 3)
+    go(conv_window<AB, 3, 3>);
+  else if (p.KH == 1 && p.KW == 1)
+    go(conv_window<AB, 1, 1>);
+  else
+    go(conv_window<AB, 0, 0>);
   return true;
 }
 

@@ -213,6 +213,14 @@ __device__ __forceinline__ void bulk_wait_group() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// 32-byte streaming store (sm_100 256-bit global store); ``dst`` 32-byte aligned.
+__device__ __forceinline__ void st_global_cs_v8(void* dst, float a0, float a1, float a2, float a3, float a4, float a5,
+                                                float a6, float a7) {
+  asm volatile("st.global.cs.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "f"(a0), "f"(a1), "f"(a2),
+               "f"(a3), "f"(a4), "f"(a5), "f"(a6), "f"(a7)
+               : "memory");
+}
+
 // Makes this thread's generic-proxy shared-memory writes visible to the
 // async proxy (TMA) before a bulk store reads them.
 __device__ __forceinline__ void fence_proxy_async_smem() {
