@@ -373,6 +373,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // accumulator slices per TMEM wait and each thread stores its own output
 // pixel's 128-byte slices from registers.
 constexpr int kWinMaxStages = 4;
+constexpr int kWinThreads = 384;      // warps 0-3 roles, 4-11 epilogue
+constexpr int kWinEpiThreads = 256;
 constexpr int kMaxFBars = 8;
 
 struct WinParams {
@@ -428,7 +430,7 @@ __device__ __forceinline__ void store_row(float* dst, const uint32_t (&r)[32], b
 
 // KH_ x KW_ > 0: taps known at compile time (unrolled bursts); 0: any shape.
 template <int AB, int KH_, int KW_>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kWinThreads, 1)
     conv_window(const __grid_constant__ CUtensorMap tma_in, const __grid_constant__ CUtensorMap tma_f,
                 const __grid_constant__ WinParams p) {
   using T = ConvTraits<AB>;
@@ -439,8 +441,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + kWinMaxStages;
   uint64_t* tfull = empty + kWinMaxStages;
   uint64_t* tempty = tfull + 2;
-  uint64_t* drain = tempty + 2;
-  uint64_t* fbar = drain + 1;  // one per filter row (rows past the last barrier share it)
+  uint64_t* drain = tempty + 2;  // one per MMA warp
+  uint64_t* fbar = drain + 2;  // one per filter row (rows past the last barrier share it)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fbar + kMaxFBars);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
@@ -453,9 +455,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], kWinEpiThreads);
     }
-    mbar_init(drain, 1);
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     for (int g = 0; g < kMaxFBars; ++g) mbar_init(&fbar[g], 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -533,17 +536,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int g = 0; g < n_fbars; ++g) mbar_wait_drain(&fbar[g], 0, 500000000ull);
       }
     }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer
-    // The warp runs the loop converged; one elected lane issues each burst.
+  } else if (warp == 1 || warp == 3) {
+    // --------------------------------------------------------------- MMA issuers
+    // Warp 1 issues the CTA's even tiles into accumulator 0, warp 3 the odd
+    // ones into accumulator 1.  A warp's barrier checks between bursts cost a
+    // few hundred cycles while the MMAs saturate shared memory; the other
+    // warp's burst keeps the tensor pipe fed meanwhile.  Each warp runs its
+    // loop converged; one elected lane issues each burst.
+    const int mw = warp == 1 ? 0 : 1;
     constexpr bool kFixed = KH_ > 0 && KW_ > 0;
     constexpr int kTaps = kFixed ? KH_ * KW_ : 1;
     constexpr int kKW = kFixed ? KW_ : 1;
-    int stage = 0;
-    uint32_t phase = 0;
-    int iter = 0;
+    int iter = mw;
     bool ok = true;
-    bool first = true;  // the first chunk of the first tile waits for the filter, row by row
+    bool first = true;  // this warp's first chunk waits for the filter, row by row
     const uint32_t smem_base = smem_addr(smem);
     const uint64_t b_desc0 = smem_desc(smem_addr(filt), p.b_chunk_bytes, 8 * p.b_span, p.b_layout);
     const uint32_t b_kb16 = static_cast<uint32_t>(p.b_kblock_bytes) >> 4;
@@ -559,8 +565,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t r_step16 = static_cast<uint32_t>(p.dil_h * p.Wp) * 8u;
     const uint32_t s_step16 = static_cast<uint32_t>(p.dil_w) * 8u;
     const uint32_t half_cols = static_cast<uint32_t>(p.tmem_cols / 2);
-    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++iter) {
-      const int acc = iter & 1;
+    for (int t = blockIdx.x + mw * gridDim.x; t < p.num_tiles && ok; t += 2 * gridDim.x, iter += 2) {
+      const int acc = mw;
       const uint32_t acc_phase = (iter >> 1) & 1;
       if (!__all_sync(0xffffffffu, mbar_wait(&tempty[acc], acc_phase ^ 1, ab, kErrMma))) break;
       tc_fence_after();
@@ -569,6 +575,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       win_tile(p, t, n, w0, f0);
       const uint32_t base_row = static_cast<uint32_t>(f0 - (f0 / p.Wp) * p.Wp);
       for (int c = 0; c < p.kc; ++c) {
+        // position of this chunk in the producer's sequence of (tile, chunk) windows
+        const int g = iter * p.kc + c;
+        const int stage = g % p.stages;
+        const uint32_t phase = static_cast<uint32_t>(g / p.stages) & 1u;
         if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, ab, kErrMma))) {
           ok = false;
           break;
@@ -629,10 +639,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
         }
         first = false;
-        if (++stage == p.stages) {
-          stage = 0;
-          phase ^= 1;
-        }
       }
       if (ok) {
         if (elect_sync()) umma_commit(&tfull[acc]);
@@ -640,9 +646,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (*abort_flag) {
-      if (elect_sync()) umma_commit(drain);
+      if (elect_sync()) umma_commit(&drain[mw]);
       __syncwarp();
-      mbar_wait_drain(drain, 0, 500000000ull);
+      mbar_wait_drain(&drain[mw], 0, 500000000ull);
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue
@@ -650,8 +656,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // stores its accumulator slices straight from registers: 128 contiguous
     // bytes per 32 columns.  Staging through shared memory would add 64 KiB
     // of shared-memory traffic per sub-tile, and with N = 64 the MMAs' operand
-    // reads already use most of the shared-memory bandwidth.
-    const int q = warp - 4;
+    // reads already use most of the shared-memory bandwidth.  Two groups of
+    // four warps: with two sub-tiles each group takes one, otherwise they
+    // alternate over pairs of 32-column slices.  A warp reads the TMEM lane
+    // quarter warp % 4.
+    const int q = warp & 3;
+    const int eg = (warp - 4) >> 2;
     const int row = q * 32 + lane;  // TMEM lane = GEMM row within a sub-tile
     const int nchunks = p.N / 32;
     const uint32_t half_cols = static_cast<uint32_t>(p.tmem_cols / 2);
@@ -663,28 +673,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       int n, w0, f0;
       win_tile(p, t, n, w0, f0);
-      for (int s = 0; s < p.sub; ++s) {
+      bool arrived = false;
+      for (int s = (p.sub == 2 ? eg : 0); s < p.sub; s += (p.sub == 2 ? 2 : 1)) {
         const int f = f0 + s * kBM + row;
         const int h = f / p.Wp, w = f - h * p.Wp;
         const bool valid = h < p.OH && w < p.Wt && w0 + w < p.OW;
         float* dst = p.out + ((static_cast<int64_t>(p.n_begin + n) * p.out_h + h) * p.out_w + w0 + w) * p.out_c;
         const uint32_t taddr =
             tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * half_cols + static_cast<uint32_t>(s * p.N);
-        for (int c = 0; c < nchunks; c += 2) {
+        for (int c = (p.sub == 2 ? 0 : 2 * eg); c < nchunks; c += (p.sub == 2 ? 2 : 4)) {
           const bool two = c + 1 < nchunks;
           uint32_t r0[32], r1[32];
           tmem_ld_32x32b_x32(taddr + c * 32, r0);
           if (two) tmem_ld_32x32b_x32(taddr + (c + 1) * 32, r1);
           tmem_wait_ld();
-          if (s == p.sub - 1 && c + 2 >= nchunks) {
+          if (c + (p.sub == 2 ? 2 : 4) >= nchunks) {
             tc_fence_before();
-            mbar_arrive(&tempty[acc]);  // accumulators free for the MMAs of tile + 2
+            mbar_arrive(&tempty[acc]);  // this thread's last read: accumulators free for tile + 2
+            arrived = true;
           }
           if (valid) {
             store_row<AB>(dst + c * 32, r0, p.v8);
             if (two) store_row<AB>(dst + (c + 1) * 32, r1, p.v8);
           }
         }
+      }
+      if (!arrived) {  // a group with no slice of this tile
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
       }
     }
   }
@@ -780,7 +796,7 @@ bool launch_window(const ConvArgs& a, const CUtensorMap& m_f, int span, EncodeIn
   auto go = [&](auto kernel) {
     *err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (*err != cudaSuccess) return;
-    kernel<<<grid, kThreads, smem, stream>>>(m_in, m_f, p);
+    kernel<<<grid, kWinThreads, smem, stream>>>(m_in, m_f, p);
     *err = cudaGetLastError();
   };
   if (p.KH == 3 && p.KW == 3)
