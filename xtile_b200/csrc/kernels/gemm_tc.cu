@@ -7,18 +7,17 @@
 // folded like lib/nova/NovaOptimize.cpp:126-296 folds them into nova.matmul)
 // and the int8 cast (round half to even, saturate).
 //
-// Structure (one CTA per SM, persistent over 128 x 256 output tiles):
-//   warp 0      TMA producer: A 128x(128 B) and B (128 B)x256 per stage,
-//               4-stage ring; per stage an "empty" mbarrier (the MMAs that
-//               read it completed), per pair of stages a "full" mbarrier
-//               (arrival count 2: both stages' bytes landed).  The MMA thread
-//               waits once per pair: a wait issued behind queued MMAs costs
-//               a few hundred cycles, as much as two 128x256x16 MMAs.
-//   warp 1      one thread issues tcgen05.mma (M=128, N=256, K=16|32) into a
-//               double-buffered TMEM accumulator (2 x 256 columns)
-//   warp 2      allocates / frees the 512 TMEM columns
-//   warps 4-7   epilogue: tcgen05.ld 32 columns at a time, apply the
-//               epilogue, store to global; overlaps the next tile's MMAs
+// Structure: clusters of two CTAs on neighbouring SMs (cta_group::2), one
+// CTA per SM, persistent over 256 x 256 output tiles; each CTA of a pair
+// owns 128 rows of the tile:
+//   warp 0      TMA producer (both CTAs): this CTA's A 128x(128 B) and B
+//               (128 B)x128 per stage, 6-stage ring
+//   warp 1      leader CTA only: one elected thread issues
+//               tcgen05.mma.cta_group::2 (M=256, N=256, K=16|32) into a
+//               double-buffered TMEM accumulator (2 x 256 columns per CTA)
+//   warp 2      allocates / frees the 512 TMEM columns (pair allocation)
+//   warps 4-7   epilogue (both CTAs): tcgen05.ld 32 columns at a time, apply
+//               the epilogue, store to global; overlaps the next tile's MMAs
 // Every mbarrier wait is bounded (2 s); a timeout records an error code in
 // the workspace error word and all roles stop, drain in-flight copies and
 // MMAs, free TMEM and return.
@@ -35,17 +34,10 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kBM = 128;
-constexpr int kBN = 256;
-constexpr int kStages = 4;
-constexpr int kGroup = 2;                      // stages per "full" barrier (one MMA-side wait each)
+constexpr int kBN = 256;                       // accumulator columns per tile
 constexpr int kThreads = 256;
-constexpr int kAStage = kBM * 128;             // 16 KiB: 128 rows x 128 B of K
-constexpr int kBStage = kBN * 128;             // 32 KiB: 128 B of K rows... x 256 columns
-constexpr int kStageBytes = kAStage + kBStage;
 constexpr int kTmemCols = 2 * kBN;
 constexpr int kGroupM = 16;                    // tile rasterization group (L2 reuse)
-constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 
 enum : uint32_t { kErrProducer = 0x101, kErrMma = 0x102, kErrEpilogue = 0x103 };
 
@@ -59,33 +51,6 @@ struct Params {
   uint8_t epi_kind[4];
   const float* epi_ptr[4];
   uint32_t* error_word;
-};
-
-template <int AB>
-struct Traits;
-template <>
-struct Traits<kBF16> {
-  static constexpr int kBK = 64;               // K elements per stage (128 B)
-  static constexpr int kChunkN = 64;           // N elements per 128-byte B chunk
-  static constexpr int kChunks = kBN / kChunkN;
-  static constexpr int kChunkBytes = kBK * 128;
-  static constexpr int kMmaK = 16;
-  static constexpr uint32_t kIdesc = instr_desc(1 /*f32*/, 1 /*bf16*/, 1 /*bf16*/, 0, 1, kBM, kBN);
-  static __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
-    umma_bf16(d, a, b, kIdesc, acc);
-  }
-};
-template <>
-struct Traits<kI8> {
-  static constexpr int kBK = 128;
-  static constexpr int kChunkN = 128;
-  static constexpr int kChunks = kBN / kChunkN;
-  static constexpr int kChunkBytes = kBK * 128;
-  static constexpr int kMmaK = 32;
-  static constexpr uint32_t kIdesc = instr_desc(2 /*s32*/, 1 /*s8*/, 1 /*s8*/, 0, 1, kBM, kBN);
-  static __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
-    umma_i8(d, a, b, kIdesc, acc);
-  }
 };
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& mt, int& nt) {
@@ -112,18 +77,69 @@ __device__ __forceinline__ int8_t to_i8(float v) {
   return v != v ? 0 : static_cast<int8_t>(static_cast<int>(fminf(fmaxf(rintf(v), -128.0f), 127.0f)));
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair kernel (cta_group::2): a cluster of two CTAs on neighbouring SMs
+// computes a 256 x 256 tile.  Each CTA loads its 128 rows of A and its 128
+// columns of B; one thread of the leader CTA (cluster rank 0) issues
+// tcgen05.mma.cta_group::2 with M = 256, N = 256, and the tensor cores of the
+// pair exchange the B halves.  Per SM and k-block that is 32 KiB of TMA
+// writes and 32 KiB of operand reads for 128 x 256 x 64 multiply-adds, where
+// the single-CTA 128 x 256 tile needs 48 + 48 KiB: shared-memory bandwidth
+// (about 128 B per cycle per SM) bounds the single-CTA tile at roughly 70% of
+// the tensor pipe, the pair tile runs at its full rate.
+//
+// Barriers: both CTAs' loads complete on the leader's "full" barrier (the
+// leader's producer arms it with both CTAs' bytes); the leader's MMA commits
+// arrive on "empty" and "tfull" in both CTAs (commit multicast); each CTA's
+// epilogue, once it has read an accumulator, arrives once on the leader's
+// "tempty" (arrival count 2).  The CTAs pass a cluster barrier after set-up
+// and before freeing TMEM, so no CTA exits while its peer still uses its
+// shared memory or TMEM.
+constexpr int kPStages = 6;
+constexpr int kPAStage = 128 * 128;             // this CTA's 128 rows x 128 B of K
+constexpr int kPBStage = 128 * 128;             // this CTA's 128 columns: 128 B of K-rows x 128 columns
+constexpr int kPStageBytes = kPAStage + kPBStage;
+constexpr int kPSmemBytes = kPStages * kPStageBytes + 1024 + 256;
+
+template <int AB>
+struct PairTraits;
+template <>
+struct PairTraits<kBF16> {
+  static constexpr int kBK = 64;        // K elements per stage
+  static constexpr int kChunkN = 64;    // N elements per 128-byte B chunk
+  static constexpr int kChunks = 2;     // chunks for this CTA's 128 columns
+  static constexpr int kChunkBytes = kBK * 128;
+  static constexpr int kMmaK = 16;
+  static constexpr uint32_t kIdesc = instr_desc(1, 1, 1, 0, 1, 256, 256);
+  static __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
+    umma_bf16_pair(d, a, b, kIdesc, acc);
+  }
+};
+template <>
+struct PairTraits<kI8> {
+  static constexpr int kBK = 128;
+  static constexpr int kChunkN = 128;
+  static constexpr int kChunks = 1;
+  static constexpr int kChunkBytes = kBK * 128;
+  static constexpr int kMmaK = 32;
+  static constexpr uint32_t kIdesc = instr_desc(2, 1, 1, 0, 1, 256, 256);
+  static __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
+    umma_i8_pair(d, a, b, kIdesc, acc);
+  }
+};
+
 template <int AB>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_tc(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-            const __grid_constant__ Params p) {
-  using T = Traits<AB>;
+    gemm_pair(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+              const __grid_constant__ Params p) {
+  using T = PairTraits<AB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;
-  uint8_t* sb = smem + kStages * kAStage;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sb + kStages * kBStage);
-  uint64_t* empty = full + kStages;
-  uint64_t* tfull = empty + kStages;
+  uint8_t* sb = smem + kPStages * kPAStage;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sb + kPStages * kPBStage);
+  uint64_t* empty = full + kPStages;
+  uint64_t* tfull = empty + kPStages;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -131,12 +147,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
   if (threadIdx.x == 0) {
-    for (int g = 0; g < kStages / kGroup; ++g) mbar_init(&full[g], kGroup);
-    for (int s = 0; s < kStages; ++s) mbar_init(&empty[s], 1);
+    for (int s = 0; s < kPStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], 2);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -147,126 +169,117 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch(&tma_b);
   }
   if (warp == 2) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialised before any cross-CTA arrive or load
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const Abort ab{abort_flag, p.error_word};
-  const int num_tiles = p.tiles_m * p.tiles_n;
+  const int num_tiles = p.tiles_m * p.tiles_n;  // pair tiles
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------------------------------------------------------- producer
-      int stage = 0, grp = 0, gi = 0;
-      uint32_t phase = 0;
-      uint32_t armed = 0, armed_phase = 0;  // per group: armed at least once / parity of its last arming
+      // ---------------------------------------------------------------- producer (both CTAs)
+      const uint32_t full0 = mapa_shared(smem_addr(full), 0);  // the leader's barriers
+      int stage = 0;
+      uint32_t phase = 0, armed = 0, armed_phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int t = pair; t < num_tiles && ok; t += npairs) {
         int mt, nt;
         tile_coords(t, p.tiles_m, p.tiles_n, mt, nt);
-        const int32_t row0 = static_cast<int32_t>(p.m_begin + static_cast<int64_t>(mt) * kBM);
-        const int32_t col0 = nt * kBN;
+        const int32_t row0 = static_cast<int32_t>(p.m_begin + static_cast<int64_t>(mt) * 256 + rank * 128);
+        const int32_t col0 = nt * 256 + static_cast<int32_t>(rank) * 128;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, ab, kErrProducer)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[grp], kStageBytes);
-          armed |= 1u << grp;
-          armed_phase = (armed_phase & ~(1u << grp)) | (phase << grp);
-          tma_load_2d(sa + stage * kAStage, &tma_a, &full[grp], kb * T::kBK, row0);
+          if (leader) {
+            mbar_arrive_expect_tx(&full[stage], 2 * kPStageBytes);
+            armed |= 1u << stage;
+            armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
+          }
+          const uint32_t bar = full0 + static_cast<uint32_t>(stage) * 8u;
+          tma_load_2d_pair(sa + stage * kPAStage, &tma_a, bar, kb * T::kBK, row0);
 #pragma unroll
           for (int c = 0; c < T::kChunks; ++c)
-            tma_load_2d(sb + stage * kBStage + c * T::kChunkBytes, &tma_b, &full[grp], col0 + c * T::kChunkN,
-                        kb * T::kBK);
-          ++stage;
-          if (++gi == kGroup) {
-            gi = 0;
-            ++grp;
-          }
-          if (stage == kStages) {
+            tma_load_2d_pair(sb + stage * kPBStage + c * T::kChunkBytes, &tma_b, bar, col0 + c * T::kChunkN,
+                             kb * T::kBK);
+          if (++stage == kPStages) {
             stage = 0;
-            grp = 0;
             phase ^= 1;
           }
         }
       }
-      // A CTA whose k-block count is not whole groups ends inside a group:
-      // complete it with plain arrivals so its last wait (and a drain) ends.
-      for (int i = gi; i > 0 && i < kGroup; ++i) mbar_arrive(&full[grp]);
-      if (*abort_flag) {
-        // let every issued copy land before the CTA's shared memory is released
-        for (int g = 0; g < kStages / kGroup; ++g)
-          if ((armed >> g) & 1u) mbar_wait_drain(&full[g], (armed_phase >> g) & 1u, 500000000ull);
-      }
+      if (*abort_flag && leader)
+        for (int s = 0; s < kPStages; ++s)
+          if ((armed >> s) & 1u) mbar_wait_drain(&full[s], (armed_phase >> s) & 1u, 500000000ull);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------------------------------------------------------- MMA issuer
-      int stage = 0, grp = 0, gi = 0;
+    if (leader) {
+      // ---------------------------------------------------------------- MMA issuer (leader CTA)
+      int stage = 0;
       uint32_t phase = 0;
       int iter = 0;
       bool ok = true;
       const uint32_t sa_base = smem_addr(sa), sb_base = smem_addr(sb);
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++iter) {
+      for (int t = pair; t < num_tiles && ok; t += npairs, ++iter) {
         const int acc = iter & 1;
         const uint32_t acc_phase = (iter >> 1) & 1;
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, ab, kErrMma)) break;
+        if (!__all_sync(0xffffffffu, mbar_wait(&tempty[acc], acc_phase ^ 1, ab, kErrMma))) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kBN;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (gi == 0) {
-            // one wait covers the kGroup stages of a group
-            if (!mbar_wait(&full[grp], phase, ab, kErrMma)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
+          if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, ab, kErrMma))) {
+            ok = false;
+            break;
           }
+          tc_fence_after();
           // A: K-major, 128-byte swizzle, 32 bytes of K per MMA.  B: N-major,
-          // 128-byte swizzle; chunks of 128 B of N are kChunkBytes apart (LBO),
+          // 128-byte swizzle; chunks of 128 B of N kChunkBytes apart (LBO),
           // 8-row K groups 1024 B apart (SBO), kMmaK rows of K per MMA.
-          // Descriptor start addresses are in 16-byte units in the low bits.
-          const uint64_t ad = smem_desc_sw128(sa_base + stage * kAStage, 16, 1024);
-          const uint64_t bd = smem_desc_sw128(sb_base + stage * kBStage, T::kChunkBytes, 1024);
+          const uint64_t ad = smem_desc_sw128(sa_base + stage * kPAStage, 16, 1024);
+          const uint64_t bd = smem_desc_sw128(sb_base + stage * kPBStage, T::kChunkBytes, 1024);
+          if (elect_sync()) {
 #pragma unroll
-          for (int k = 0; k < 128 / 32; ++k)
-            T::mma(d_tmem, ad + static_cast<uint64_t>(k * 2), bd + static_cast<uint64_t>(k * T::kMmaK * 8),
-                   (kb | k) != 0 ? 1u : 0u);
-          umma_commit(&empty[stage]);
-          ++stage;
-          if (++gi == kGroup) {
-            gi = 0;
-            ++grp;
+            for (int k = 0; k < 128 / 32; ++k)
+              T::mma(d_tmem, ad + static_cast<uint64_t>(k * 2), bd + static_cast<uint64_t>(k * T::kMmaK * 8),
+                     (kb | k) != 0 ? 1u : 0u);
+            umma_commit_pair(&empty[stage], 0x3);
           }
-          if (stage == kStages) {
+          __syncwarp();
+          if (++stage == kPStages) {
             stage = 0;
-            grp = 0;
             phase ^= 1;
           }
         }
-        if (ok) umma_commit(&tfull[acc]);
+        if (ok) {
+          if (elect_sync()) umma_commit_pair(&tfull[acc], 0x3);
+          __syncwarp();
+        }
       }
       if (*abort_flag) {
-        umma_commit(drain);
+        if (elect_sync()) umma_commit_pair(drain, 0x1);
+        __syncwarp();
         mbar_wait_drain(drain, 0, 500000000ull);
       }
     }
   } else if (warp >= 4) {
-    // -------------------------------------------------------------------- epilogue
+    // -------------------------------------------------------------------- epilogue (both CTAs)
     const int q = warp - 4;  // TMEM lane quarter
+    const uint32_t tempty0 = mapa_shared(smem_addr(tempty), 0);
     int iter = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++iter) {
+    for (int t = pair; t < num_tiles; t += npairs, ++iter) {
       const int acc = iter & 1;
       const uint32_t acc_phase = (iter >> 1) & 1;
-      if (!mbar_wait_warp(&tfull[acc], acc_phase, ab, kErrEpilogue)) break;
+      const bool ok = mbar_wait_warp(&tfull[acc], acc_phase, ab, kErrEpilogue);
+      if (named_barrier_or(2, 128, !ok)) break;  // all four warps stop together (named barriers below)
       tc_fence_after();
       int mt, nt;
       tile_coords(t, p.tiles_m, p.tiles_n, mt, nt);
-      const int64_t r_local = static_cast<int64_t>(mt) * kBM + q * 32 + lane;
+      const int64_t r_local = static_cast<int64_t>(mt) * 256 + rank * 128 + q * 32 + lane;
       const int64_t row = p.m_begin + r_local;
       const bool row_ok = r_local < p.M;
       const bool plain = p.acc == nullptr && p.n_epi == 0;
@@ -275,7 +288,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kBN + c * 32, r);
         tmem_wait_ld();
-        const int64_t col0 = static_cast<int64_t>(nt) * kBN + c * 32;
+        if (c == kBN / 32 - 1) {
+          // every thread of this CTA has read the accumulator: one arrival for the CTA
+          tc_fence_before();
+          named_barrier_sync(1, 128);
+          if (threadIdx.x == 128) mbar_arrive_cluster(tempty0 + static_cast<uint32_t>(acc) * 8u);
+        }
+        const int64_t col0 = static_cast<int64_t>(nt) * 256 + c * 32;
         if (!row_ok || col0 >= p.N) continue;
         float v[32];
 #pragma unroll
@@ -289,7 +308,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (p.c_elem == kF32) {
           float* dst = static_cast<float*>(p.C) + row * p.ldc + col0;
-          if (full_chunk && (p.ldc & 3) == 0) {
+          if (full_chunk && (p.ldc & 7) == 0 && (reinterpret_cast<uintptr_t>(p.C) & 31) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8)
+              st_global_cs_v8(dst + j, v[j], v[j + 1], v[j + 2], v[j + 3], v[j + 4], v[j + 5], v[j + 6], v[j + 7]);
+          } else if (full_chunk && (p.ldc & 3) == 0) {
 #pragma unroll
             for (int j = 0; j < 32; j += 4)
               *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
@@ -315,14 +338,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);
     }
   }
   __syncthreads();
+  cluster_sync();  // the peer is done with this CTA's shared memory and TMEM, and vice versa
   if (warp == 2) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    tmem_dealloc_pair(tmem_base, kTmemCols);
   }
 }
 
@@ -344,13 +366,13 @@ bool make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
 }
 
 template <int AB>
-cudaError_t launch_typed(const GemmArgs& a, cudaStream_t stream) {
-  using T = Traits<AB>;
+cudaError_t launch_pair(const GemmArgs& a, cudaStream_t stream) {
+  using T = PairTraits<AB>;
   const CUtensorMapDataType dt = AB == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const int eb = AB == kBF16 ? 2 : 1;
   CUtensorMap ma, mb;
-  // A: [rows up to m_begin + M] x [K], box 128 rows x 128 bytes of K
-  if (!make_map_2d(&ma, a.A, dt, eb, a.K, a.m_begin + a.M, a.lda, 128 / eb, kBM)) return cudaErrorInvalidValue;
+  // A: [rows up to m_begin + M] x [K], box 128 rows x 128 bytes of K (one CTA's half of a pair tile)
+  if (!make_map_2d(&ma, a.A, dt, eb, a.K, a.m_begin + a.M, a.lda, 128 / eb, 128)) return cudaErrorInvalidValue;
   // B: [K] x [N], box kBK rows x 128 bytes of N
   if (!make_map_2d(&mb, a.B, dt, eb, a.N, a.K, a.ldb, 128 / eb, T::kBK)) return cudaErrorInvalidValue;
   Params p{};
@@ -360,8 +382,8 @@ cudaError_t launch_typed(const GemmArgs& a, cudaStream_t stream) {
   p.N = a.N;
   p.ldc = a.ldc;
   p.m_begin = a.m_begin;
-  p.tiles_m = static_cast<int>((a.M + kBM - 1) / kBM);
-  p.tiles_n = static_cast<int>((a.N + kBN - 1) / kBN);
+  p.tiles_m = static_cast<int>((a.M + 255) / 256);
+  p.tiles_n = static_cast<int>((a.N + 255) / 256);
   p.num_kb = static_cast<int>((a.K + T::kBK - 1) / T::kBK);
   p.c_elem = a.c_elem;
   p.n_epi = a.n_epi;
@@ -372,7 +394,7 @@ cudaError_t launch_typed(const GemmArgs& a, cudaStream_t stream) {
   p.error_word = a.error_word;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc<AB>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(gemm_pair<AB>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
@@ -381,15 +403,27 @@ cudaError_t launch_typed(const GemmArgs& a, cudaStream_t stream) {
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int tiles = p.tiles_m * p.tiles_n;
   if (tiles == 0 || p.num_kb == 0) return cudaSuccess;
-  gemm_tc<AB><<<tiles < sms ? tiles : sms, kThreads, kSmemBytes, stream>>>(ma, mb, p);
-  return cudaGetLastError();
+  const int pairs = tiles < sms / 2 ? tiles : sms / 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kPSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_pair<AB>, ma, mb, p);
 }
 
 }  // namespace
 
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
-  if (a.ab_elem == kBF16) return launch_typed<kBF16>(a, stream);
-  return launch_typed<kI8>(a, stream);
+  if (a.ab_elem == kBF16) return launch_pair<kBF16>(a, stream);
+  return launch_pair<kI8>(a, stream);
 }
 
 void* tensor_map_encoder() {
