@@ -229,6 +229,11 @@ def cpu_baseline(w: dict, xt, torch, budget_s: float = 12.0) -> dict:
             "sample": f"{done} of {len(order)} Blocks in {dt:.1f} s (numpy oracle, BLAS threads={threads})"}
 
 
+def bid0_share(grid0: int, world: int, rank: int) -> tuple[int, int]:
+    """Blocks [lo, hi) along bid0 that ``rank`` of ``world`` computes."""
+    return rank * grid0 // world, (rank + 1) * grid0 // world
+
+
 def nccl_gather(out, rows_per_rank, world, rank, dist):
     if world == 1:
         return
@@ -280,7 +285,9 @@ def main() -> None:
     if world > 1 and not sharded:
         # not a sharded configuration: every rank runs an independent replica
         w["config"]["parallelism"] = f"{world} independent replicas"
-    lo, hi = (rank * grid0 // world, (rank + 1) * grid0 // world) if sharded else (0, grid0)
+    if sharded and (grid0 % world or w["out_shape"][0] % grid0):
+        raise SystemExit(f"bench: grid0={grid0} does not split evenly over {world} ranks")
+    lo, hi = bid0_share(grid0, world, rank) if sharded else (0, grid0)
     rows_per_rank = w["out_shape"][0] // world if sharded else 0
 
     # device-resident inputs; rotate enough sets to defeat the 126 MB L2

@@ -1,0 +1,90 @@
+"""World-size-2 runs of the bid0 sharding on the CPU (gloo backend).
+
+Each rank computes its share of a matmul Grid's Blocks - the share
+``bench.bid0_share`` gives it, the one ``bench.py`` launches on that rank's
+GPU - with the reference interpreter standing in for the kernel; the shares
+are gathered to rank 0 with the benchmark's own gather and rank 0 compares
+with a single-process run of the whole Grid.  This covers the partition
+arithmetic, the gather and the order of the collectives; the kernels
+themselves are covered by the GPU tests.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import bench
+import xtile_b200 as xt
+from oracle import xt_oracle
+
+
+@xt.kernel
+def matmul_rows(lhs, rhs, out, tm, tn, tk):
+    i, j = xt.bid(0), xt.bid(1)
+    a = xt.load(lhs, index=(i, 0), shape=(tm, tk))
+    b = xt.load(rhs, index=(0, j), shape=(tk, tn), shared=1)
+    xt.store(out, index=(i, j), tile=xt.matmul(a, b))
+
+
+M, N, K, TM, TN = 64, 32, 16, 8, 16
+GRID = (M // TM, N // TN, 1)
+
+
+def inputs():
+    rng = np.random.default_rng(11)
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    b = rng.standard_normal((K, N)).astype(np.float32)
+    return xt_oracle.f32_to_bf16(a), xt_oracle.f32_to_bf16(b)  # bf16 bit patterns
+
+
+def module_text():
+    A = xt.Array
+    mod = xt.convert(matmul_rows, args=(A((M, K), xt.bfloat16), A((K, N), xt.bfloat16), A((M, N), xt.float32),
+                                        TM, TN, K), grid=GRID)
+    return str(mod)
+
+
+def shard_worker(rank, world, port, text):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        a, b = inputs()
+        out = np.full((M, N), np.nan, dtype=np.float32)
+        lo, hi = bench.bid0_share(GRID[0], world, rank)
+        blocks = [(i, j, 0) for i in range(lo, hi) for j in range(GRID[1])]
+        xt_oracle.run(text, [a, b, out], blocks=blocks)
+        out_t = torch.from_numpy(out)
+        bench.nccl_gather(out_t, M // world, world, rank, dist)
+        if rank == 0:
+            ref = np.zeros((M, N), dtype=np.float32)
+            xt_oracle.run(text, [a, b, ref])
+            assert np.array_equal(out_t.numpy(), ref), "gathered shards differ from the single-rank result"
+            # each rank computed exactly its own rows
+            assert (hi - lo) * TM == M // world
+    finally:
+        dist.destroy_process_group()
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("world", [2])
+def test_bid0_shards_gathered_to_rank0(world):
+    text = module_text()
+    mp.start_processes(shard_worker, args=(world, free_port(), text), nprocs=world, join=True, start_method="spawn")
+
+
+def test_bid0_share_partitions_the_grid():
+    for grid0 in (1, 7, 128):
+        for world in (1, 2, 3, 8):
+            spans = [bench.bid0_share(grid0, world, r) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == grid0
+            assert all(spans[r][1] == spans[r + 1][0] for r in range(world - 1))
