@@ -38,6 +38,11 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "TFLOP/s (matmul/conv) & HBM GB/s (add/softmax) vs B200 peak, 1–8 GPUs"
 L2_BYTES = 126 * 2 ** 20
+# SMs the sharded GEMM leaves to the NCCL gather it overlaps, and NCCL's
+# channel cap.  On 2 B200s, 16 free SMs did not let the gather's kernels run
+# beside the GEMM at all (it waited for the GEMM to finish); 32 did.
+GATHER_SMS = 32
+GATHER_CHANNELS = 16
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 # DRAM bytes per launch of the dominant kernel from one ncu capture
@@ -276,6 +281,10 @@ def main() -> None:
 
         import torch.distributed as dist
 
+        # NCCL runs one CTA per channel: keep them within the SMs the GEMM leaves
+        # free, so the gather of step i really runs beside the GEMM of step i + 1
+        os.environ.setdefault("NCCL_MAX_NCHANNELS", str(GATHER_CHANNELS))
+        os.environ.setdefault("NCCL_MAX_P2P_NCHANNELS", str(GATHER_CHANNELS))
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     w = build_workload(args.workload, xt, torch, world, rank)
     mod = w["module"]
@@ -295,18 +304,47 @@ def main() -> None:
     out = torch.empty(w["out_shape"], dtype=w["out_dtype"], device=dev)
     ws_bytes = sum(t.numel() * t.element_size() for t in inputs_dev) + out.numel() * out.element_size()
     n_sets = 1 if ws_bytes > 3 * L2_BYTES else int(-(-3 * L2_BYTES // ws_bytes)) + 1
-    sets = [(inputs_dev, out)] + [([t.clone() for t in inputs_dev], torch.empty_like(out))
-                                  for _ in range(n_sets - 1)]
+    if sharded:
+        # two output buffers: step i + 1 computes into one while step i's rows
+        # are still being gathered out of the other
+        n_sets = 2
+        sets = [(inputs_dev, out), (inputs_dev, torch.empty_like(out))]
+    else:
+        sets = [(inputs_dev, out)] + [([t.clone() for t in inputs_dev], torch.empty_like(out))
+                                      for _ in range(n_sets - 1)]
     stream = torch.cuda.current_stream(dev)
+    comm = torch.cuda.Stream(dev) if sharded else None
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    computed = [torch.cuda.Event() for _ in range(n_sets)]
+    gathered = [torch.cuda.Event() for _ in range(n_sets)]
 
     def step(i):
         ins, o = sets[i % n_sets]
         xt.launch(mod, *ins, o, bid0_range=(lo, hi))
 
+    def sharded_step(i, start=None, end=None):
+        # compute on the default stream, gather on the communication stream:
+        # the gather of step i overlaps the compute of step i + 1
+        ins, o = sets[i % n_sets]
+        if i >= n_sets:
+            stream.wait_event(gathered[i % n_sets])  # that gather has read o
+        if start is not None:
+            start.record(stream)
+        with xt.sm_budget(sms - GATHER_SMS if world > 1 else 0):
+            xt.launch(mod, *ins, o, bid0_range=(lo, hi))
+        if end is not None:
+            end.record(stream)
+        computed[i % n_sets].record(stream)
+        comm.wait_event(computed[i % n_sets])
+        with torch.cuda.stream(comm):
+            nccl_gather(o, rows_per_rank, world, rank, dist)
+        gathered[i % n_sets].record(comm)
+
     for i in range(args.warmup):
-        step(i)
         if sharded:
-            nccl_gather(sets[i % n_sets][1], rows_per_rank, world, rank, dist)
+            sharded_step(i)
+        else:
+            step(i)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -314,7 +352,7 @@ def main() -> None:
     # ---- timed region: K steps.  Microsecond-scale steps are captured once in
     # a CUDA graph and replayed, so host launch overhead does not starve the
     # GPU; the millisecond-scale sharded step (with its NCCL gather) launches
-    # eagerly with per-launch events.
+    # eagerly with per-launch events, its gather on a second stream.
     use_graph = not sharded
     graph = None
     # In graph mode the two timing events are nodes of the graph itself
@@ -348,11 +386,8 @@ def main() -> None:
             graph.replay()
         else:
             for i in range(args.steps):
-                starts[i].record(stream)
-                step(i)
-                ends[i].record(stream)
-                if sharded:
-                    nccl_gather(sets[i % n_sets][1], rows_per_rank, world, rank, dist)
+                sharded_step(i, starts[i], ends[i])
+            stream.wait_stream(comm)  # every gather is inside the timed region
         t_end.record(stream)
         torch.cuda.synchronize()
         if dist:
@@ -471,7 +506,7 @@ def main() -> None:
         "config": {**w["config"], "l2": f"{n_sets} rotating input/output sets" if n_sets > 1
                    else "working set larger than L2",
                    "timing": ("CUDA-graph replay of K launches, events recorded inside the graph"
-                              if not sharded else "eager launches")},
+                              if not sharded else "eager launches; step i's gather overlaps step i+1's compute")},
         "roofline": {"bound": w["bound"], "achieved": round(achieved_r, 2), "peak": peak, "unit": roof_unit,
                      "frac": round(achieved_r / peak, 4), "peak_kind": f"{peak_kind} (burst)",
                      "traffic": NCU_TRAFFIC_BYTES.get(args.workload),

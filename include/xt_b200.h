@@ -118,6 +118,14 @@ int xt_launch(const xt_module* module, const char* func, void* const* args, int 
  * a bounded wait runs out (0: none).  Synchronizes the device. */
 int xt_device_error(uint32_t* out_code);
 
+/* No counterpart in the reference.  Caps the SMs that the persistent kernels
+ * (gemm and conv families) of later launches from the calling thread occupy;
+ * 0 (the default) means all SMs.  A launch that runs beside a communication
+ * kernel (an NCCL gather of the previous step's rows, say) leaves the other
+ * SMs to it, so the two overlap instead of queueing behind each other.  The
+ * GEMM rounds the budget down to an even number (its CTAs come in pairs). */
+int xt_set_sm_budget(int sms);
+
 /* No counterpart in the reference.  Launches a matmul program (the gemm
  * family only; other families are rejected) exactly like xt_launch, but
  * without allocating device memory: for callers that cannot call cudaMalloc,

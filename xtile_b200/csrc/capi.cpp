@@ -103,6 +103,9 @@ int cuda_fail(cudaError_t e, const char* what) {
 
 int64_t clamp64(int64_t v, int64_t lo, int64_t hi) { return v < lo ? lo : (v > hi ? hi : v); }
 
+// SM budget of the persistent (gemm, conv) kernels launched by this thread.
+thread_local int t_sm_budget = 0;
+
 int launch_plan(const xt::Plan& p, void* const* args, int64_t b0, int64_t b1, cudaStream_t stream) {
   using namespace xt;
   const int64_t g0 = p.grid[0];
@@ -191,6 +194,7 @@ int launch_plan(const xt::Plan& p, void* const* args, int64_t b0, int64_t b1, cu
         a.epi_ptr[i] = static_cast<const float*>(args[g.epi[i].arg]);
       }
       a.error_word = ws->error_word;
+      a.max_sms = t_sm_budget;
       if (full) {
         a.m_begin = 0;
         a.M = g.M;
@@ -232,6 +236,7 @@ int launch_plan(const xt::Plan& p, void* const* args, int64_t b0, int64_t b1, cu
       a.dil_w = c.dil_w;
       a.elem = elem_code(c.elem);
       a.error_word = ws->error_word;
+      a.max_sms = t_sm_budget;
       if (full) {
         a.n_begin = 0;
         a.ON = c.ON;
@@ -475,6 +480,12 @@ int xt_device_error(uint32_t* out_code) {
   if (e != cudaSuccess) return cuda_fail(e, "error word read");
   if (code) cudaMemset(ws->error_word, 0, sizeof code);
   *out_code = code;
+  return XT_OK;
+}
+
+int xt_set_sm_budget(int sms) {
+  if (sms < 0) return fail(XT_EARGUMENT, "xt_set_sm_budget: negative SM count");
+  t_sm_budget = sms;
   return XT_OK;
 }
 

@@ -54,6 +54,7 @@ struct GemmArgs {
   uint8_t epi_kind[4];
   const float* epi_ptr[4];
   uint32_t* error_word;
+  int max_sms;             // SMs the persistent grid may occupy (0: all)
 };
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream);
 
@@ -69,6 +70,7 @@ struct ConvArgs {
   int64_t pad_t, pad_l, dil_h, dil_w;
   uint8_t elem;
   uint32_t* error_word;
+  int max_sms;             // SMs the persistent grid may occupy (0: all)
 };
 cudaError_t launch_conv(const ConvArgs& a, cudaStream_t stream);
 

@@ -850,6 +850,7 @@ cudaError_t launch_typed(const ConvArgs& a, cudaStream_t stream) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (a.max_sms > 0 && a.max_sms < sms) sms = a.max_sms;
   {
     cudaError_t e;
     if (launch_window<AB>(a, m_f, span, encode_input, m_in, sms, stream, &e)) return e;

@@ -403,7 +403,9 @@ cudaError_t launch_pair(const GemmArgs& a, cudaStream_t stream) {
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int tiles = p.tiles_m * p.tiles_n;
   if (tiles == 0 || p.num_kb == 0) return cudaSuccess;
-  const int pairs = tiles < sms / 2 ? tiles : sms / 2;
+  if (a.max_sms > 0 && a.max_sms < sms) sms = a.max_sms;
+  int pairs = tiles < sms / 2 ? tiles : sms / 2;
+  if (pairs < 1) pairs = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
   cfg.blockDim = dim3(kThreads);

@@ -179,6 +179,12 @@ PYBIND11_MODULE(_xtile, m) {
         ("Run the " + n + " stage in place and return the module.").c_str());
   }
   m.def("plan", &plan, py::arg("module"), py::arg("func") = py::none());
+  m.def(
+      "set_sm_budget",
+      [](int sms) {
+        if (xt_set_sm_budget(sms) != XT_OK) throw std::invalid_argument(xt_last_error());
+      },
+      py::arg("sms"));
   m.def("launch", &launch, py::arg("module"), py::arg("ptrs"), py::arg("bid0_begin"), py::arg("bid0_end"),
         py::arg("stream"), py::arg("func") = py::none());
   m.def("func_names", &func_names, py::arg("module"));

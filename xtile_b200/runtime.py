@@ -117,3 +117,23 @@ def run(kernel_fn: dsl.KernelFunction, *, args: tuple, grid: tuple, double_buffe
 def device_error() -> int:
     """Reads and clears the current device's kernel error word (0: none)."""
     return int(_native.device_error())
+
+
+class sm_budget:
+    """Caps the SMs the persistent kernels (gemm, conv) launched by this
+    thread occupy, for the duration of a ``with`` block (0: all SMs).
+
+    Used when a launch runs beside a communication kernel, e.g. the NCCL
+    gather of the previous step's rows: the kernel leaves the other SMs to the
+    collective so the two overlap instead of queueing behind each other.
+    """
+
+    def __init__(self, sms: int) -> None:
+        self.sms = int(sms)
+
+    def __enter__(self) -> "sm_budget":
+        _native.set_sm_budget(self.sms)
+        return self
+
+    def __exit__(self, *exc) -> None:
+        _native.set_sm_budget(0)
