@@ -258,6 +258,9 @@ def main() -> None:
     ap.add_argument("--workload", default="sharded_matmul",
                     choices=["add", "softmax", "matmul", "conv2d", "sharded_matmul"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="sharded_matmul on N>1 GPUs: ranks store their rows straight into rank 0's output "
+                         "over NVLink (peer), or compute locally and gather with NCCL")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
@@ -314,6 +317,20 @@ def main() -> None:
                                       for _ in range(n_sets - 1)]
     stream = torch.cuda.current_stream(dev)
     comm = torch.cuda.Stream(dev) if sharded else None
+    # peer gather: every rank's kernel stores its rows into rank 0's output
+    # arrays (mapped over NVLink with CUDA IPC); a one-element all-reduce per
+    # step is the GPU-side barrier after which rank 0 holds all rows
+    peer = sharded and world > 1 and args.gather == "peer"
+    targets = [o for _, o in sets]
+    flag = torch.zeros(1, device=dev)
+    if peer:
+        w["config"]["parallelism"] = (f"bid0 split over {world} GPUs; each rank's kernel stores its C rows "
+                                      f"into rank 0's output over NVLink (CUDA IPC)")
+        handles = [xt.export_array(o) for o in targets] if rank == 0 else None
+        box = [handles]
+        dist.broadcast_object_list(box, src=0)
+        if rank != 0:
+            targets = [xt.PeerArray.open(h, tuple(w["out_shape"]), w["out_dtype"]) for h in box[0]]
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     computed = [torch.cuda.Event() for _ in range(n_sets)]
     gathered = [torch.cuda.Event() for _ in range(n_sets)]
@@ -323,6 +340,15 @@ def main() -> None:
         xt.launch(mod, *ins, o, bid0_range=(lo, hi))
 
     def sharded_step(i, start=None, end=None):
+        if peer:
+            ins, o = sets[i % n_sets][0], targets[i % n_sets]
+            if start is not None:
+                start.record(stream)
+            xt.launch(mod, *ins, o, bid0_range=(lo, hi))
+            if end is not None:
+                end.record(stream)
+            dist.all_reduce(flag)
+            return
         # compute on the default stream, gather on the communication stream:
         # the gather of step i overlaps the compute of step i + 1
         ins, o = sets[i % n_sets]
@@ -442,9 +468,13 @@ def main() -> None:
             else:
                 for d, h in zip(ins, host_in):
                     d.copy_(h, non_blocking=True)
-            xt.launch(mod, *ins, o, bid0_range=(lo, hi))
-            if sharded:
-                nccl_gather(o, rows_per_rank, world, rank, dist)
+            if peer:
+                xt.launch(mod, *ins, targets[0], bid0_range=(lo, hi))
+                dist.all_reduce(flag)
+            else:
+                xt.launch(mod, *ins, o, bid0_range=(lo, hi))
+                if sharded:
+                    nccl_gather(o, rows_per_rank, world, rank, dist)
             if host_out.numel():
                 host_out.copy_(o, non_blocking=True)
 
@@ -468,6 +498,9 @@ def main() -> None:
 
     if dist:
         dist.barrier()
+    if peer and rank != 0:
+        for t in targets:
+            t.close()
     if rank != 0:
         dist.destroy_process_group()
         return
@@ -506,7 +539,10 @@ def main() -> None:
         "config": {**w["config"], "l2": f"{n_sets} rotating input/output sets" if n_sets > 1
                    else "working set larger than L2",
                    "timing": ("CUDA-graph replay of K launches, events recorded inside the graph"
-                              if not sharded else "eager launches; step i's gather overlaps step i+1's compute")},
+                              if not sharded else
+                              ("eager launches; rows stored into rank 0's output over NVLink, one-element "
+                               "all-reduce per step" if peer else
+                               "eager launches; step i's NCCL gather overlaps step i+1's compute"))},
         "roofline": {"bound": w["bound"], "achieved": round(achieved_r, 2), "peak": peak, "unit": roof_unit,
                      "frac": round(achieved_r / peak, 4), "peak_kind": f"{peak_kind} (burst)",
                      "traffic": NCU_TRAFFIC_BYTES.get(args.workload),

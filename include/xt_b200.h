@@ -126,6 +126,17 @@ int xt_device_error(uint32_t* out_code);
  * GEMM rounds the budget down to an even number (its CTAs come in pairs). */
 int xt_set_sm_budget(int sms);
 
+/* No counterpart in the reference.  CUDA IPC for row gathers without a
+ * collective: xt_ipc_export gives the 64-byte handle of the device allocation
+ * holding ``ptr`` and ptr's byte offset in it; xt_ipc_open maps such an
+ * allocation of another process of the node into this one on the current
+ * device (*base: the mapping's base address; accesses go over NVLink), and
+ * xt_ipc_close unmaps it.  A process passes base + offset to xt_launch as an
+ * output array, and its kernel's stores land in the exporting GPU's array. */
+int xt_ipc_export(const void* ptr, unsigned char* handle64, uint64_t* offset);
+int xt_ipc_open(const unsigned char* handle64, void** base);
+int xt_ipc_close(void* base);
+
 /* No counterpart in the reference.  Launches a matmul program (the gemm
  * family only; other families are rejected) exactly like xt_launch, but
  * without allocating device memory: for callers that cannot call cudaMalloc,

@@ -55,11 +55,11 @@ from .api import (
     xt_serialize,
     xt_to_nova,
 )
-from .runtime import device_error, launch, run, sm_budget
+from .runtime import PeerArray, device_error, export_array, launch, run, sm_budget
 
 __all__ = [
-    "Array", "DType", "Module", "add", "astype", "bfloat16", "bid", "cdiv", "compile", "convert",
-    "cos", "device_error", "exp", "float32", "int8", "kernel", "launch", "load", "load_conv2d",
+    "Array", "DType", "Module", "PeerArray", "add", "astype", "bfloat16", "bid", "cdiv", "compile", "convert",
+    "cos", "device_error", "exp", "export_array", "float32", "int8", "kernel", "launch", "load", "load_conv2d",
     "matmul", "max", "mma", "mul", "nova_allocate", "nova_barrier", "nova_optimize",
     "nova_threading", "nova_to_x1", "parse", "reciprocal", "reshape", "rsqrt", "run",
     "save_compile_results", "save_ir", "sigmoid", "silu", "sin", "sm_budget", "store", "sub", "sum", "tanh",

@@ -1,5 +1,6 @@
 // C ABI of libxt_b200.so (include/xt_b200.h): module handles, stage dumps,
 // planning and launching.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdlib>
@@ -480,6 +481,47 @@ int xt_device_error(uint32_t* out_code) {
   if (e != cudaSuccess) return cuda_fail(e, "error word read");
   if (code) cudaMemset(ws->error_word, 0, sizeof code);
   *out_code = code;
+  return XT_OK;
+}
+
+typedef CUresult (*MemGetAddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+int xt_ipc_export(const void* ptr, unsigned char* handle64, uint64_t* offset) {
+  if (!ptr || !handle64 || !offset) return fail(XT_EARGUMENT, "xt_ipc_export: null argument");
+  static MemGetAddressRangeFn range = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<MemGetAddressRangeFn>(nullptr);
+    return reinterpret_cast<MemGetAddressRangeFn>(f);
+  }();
+  if (!range) return fail(XT_ECUDA, "xt_ipc_export: cuMemGetAddressRange unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail(XT_EARGUMENT, "xt_ipc_export: pointer is not device memory");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return fail(XT_ECUDA, std::string("xt_ipc_export: ") + cudaGetErrorString(e));
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  std::memcpy(handle64, &h, sizeof h);
+  *offset = static_cast<uint64_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return XT_OK;
+}
+
+int xt_ipc_open(const unsigned char* handle64, void** base) {
+  if (!handle64 || !base) return fail(XT_EARGUMENT, "xt_ipc_open: null argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle64, sizeof h);
+  cudaError_t e = cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(XT_ECUDA, std::string("xt_ipc_open: ") + cudaGetErrorString(e));
+  return XT_OK;
+}
+
+int xt_ipc_close(void* base) {
+  cudaError_t e = cudaIpcCloseMemHandle(base);
+  if (e != cudaSuccess) return fail(XT_ECUDA, std::string("xt_ipc_close: ") + cudaGetErrorString(e));
   return XT_OK;
 }
 

@@ -50,6 +50,7 @@ struct Params {
   int n_epi;
   uint8_t epi_kind[4];
   const float* epi_ptr[4];
+  int tma_store;  // plain f32 output: epilogue stores through shared memory with TMA
   uint32_t* error_word;
 };
 
@@ -99,7 +100,8 @@ constexpr int kPStages = 6;
 constexpr int kPAStage = 128 * 128;             // this CTA's 128 rows x 128 B of K
 constexpr int kPBStage = 128 * 128;             // this CTA's 128 columns: 128 B of K-rows x 128 columns
 constexpr int kPStageBytes = kPAStage + kPBStage;
-constexpr int kPSmemBytes = kPStages * kPStageBytes + 1024 + 256;
+constexpr int kPStaging = 4 * 2 * 32 * 128;     // per epilogue warp: two 32-row x 32-column f32 buffers
+constexpr int kPSmemBytes = kPStages * kPStageBytes + kPStaging + 1024 + 256;
 
 template <int AB>
 struct PairTraits;
@@ -131,13 +133,14 @@ struct PairTraits<kI8> {
 template <int AB>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-              const __grid_constant__ Params p) {
+              const __grid_constant__ CUtensorMap tma_c, const __grid_constant__ Params p) {
   using T = PairTraits<AB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;
   uint8_t* sb = smem + kPStages * kPAStage;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sb + kPStages * kPBStage);
+  uint8_t* staging = sb + kPStages * kPBStage;
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + kPStaging);
   uint64_t* empty = full + kPStages;
   uint64_t* tfull = empty + kPStages;
   uint64_t* tempty = tfull + 2;
@@ -167,6 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch(&tma_a);
     tma_prefetch(&tma_b);
+    if (p.tma_store) tma_prefetch(&tma_c);
   }
   if (warp == 2) {
     tmem_alloc_pair(tmem_slot, kTmemCols);
@@ -294,6 +298,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           named_barrier_sync(1, 128);
           if (threadIdx.x == 128) mbar_arrive_cluster(tempty0 + static_cast<uint32_t>(acc) * 8u);
         }
+        if (p.tma_store) {
+          // Stage this warp's 32 rows x 32 columns in a 128-byte swizzled
+          // buffer and write them with one TMA store: whole 128-byte row
+          // segments, clipped at the array's edges by TMA.  That matters most
+          // when C is another GPU's memory (row gathers over NVLink).
+          uint8_t* buf = staging + (q * 2 + (c & 1)) * 4096;
+          if (lane == 0) bulk_wait_group_read<1>();  // the store that last used buf has read it
+          __syncwarp();
+          const uint32_t sw = static_cast<uint32_t>(lane & 7);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float4 v4;
+            if (AB == kI8)
+              v4 = make_float4(__int2float_rn(static_cast<int>(r[4 * j])), __int2float_rn(static_cast<int>(r[4 * j + 1])),
+                               __int2float_rn(static_cast<int>(r[4 * j + 2])),
+                               __int2float_rn(static_cast<int>(r[4 * j + 3])));
+            else
+              v4 = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]), __uint_as_float(r[4 * j + 2]),
+                               __uint_as_float(r[4 * j + 3]));
+            *reinterpret_cast<float4*>(buf + lane * 128 + ((static_cast<uint32_t>(j) ^ sw) << 4)) = v4;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tma_c, buf, nt * 256 + c * 32,
+                         static_cast<int32_t>(p.m_begin + static_cast<int64_t>(mt) * 256 + rank * 128 + q * 32));
+            bulk_commit_group();
+          }
+          continue;
+        }
         const int64_t col0 = static_cast<int64_t>(nt) * 256 + c * 32;
         if (!row_ok || col0 >= p.N) continue;
         float v[32];
@@ -339,6 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    if (p.tma_store && lane == 0) bulk_wait_group<0>();  // this warp's stores are complete
   }
   __syncthreads();
   cluster_sync();  // the peer is done with this CTA's shared memory and TMEM, and vice versa
@@ -375,6 +410,11 @@ cudaError_t launch_pair(const GemmArgs& a, cudaStream_t stream) {
   if (!make_map_2d(&ma, a.A, dt, eb, a.K, a.m_begin + a.M, a.lda, 128 / eb, 128)) return cudaErrorInvalidValue;
   // B: [K] x [N], box kBK rows x 128 bytes of N
   if (!make_map_2d(&mb, a.B, dt, eb, a.N, a.K, a.ldb, 128 / eb, T::kBK)) return cudaErrorInvalidValue;
+  // C through TMA stores for plain f32 output: [rows up to m_begin + M] x [N], box 32 rows x 32 columns
+  CUtensorMap mc = ma;
+  const bool tma_store = a.c_elem == kF32 && a.acc == nullptr && a.n_epi == 0 && (a.ldc * 4) % 16 == 0 &&
+                         (reinterpret_cast<uintptr_t>(a.C) & 15) == 0 &&
+                         make_map_2d(&mc, a.C, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.N, a.m_begin + a.M, a.ldc, 32, 32);
   Params p{};
   p.C = a.C;
   p.acc = a.acc;
@@ -392,6 +432,7 @@ cudaError_t launch_pair(const GemmArgs& a, cudaStream_t stream) {
     p.epi_ptr[i] = a.epi_ptr[i];
   }
   p.error_word = a.error_word;
+  p.tma_store = tma_store ? 1 : 0;
   static bool attr_set = false;
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(gemm_pair<AB>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes);
@@ -418,7 +459,7 @@ cudaError_t launch_pair(const GemmArgs& a, cudaStream_t stream) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_pair<AB>, ma, mb, p);
+  return cudaLaunchKernelEx(&cfg, gemm_pair<AB>, ma, mb, mc, p);
 }
 
 }  // namespace

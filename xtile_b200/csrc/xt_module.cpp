@@ -180,6 +180,33 @@ PYBIND11_MODULE(_xtile, m) {
   }
   m.def("plan", &plan, py::arg("module"), py::arg("func") = py::none());
   m.def(
+      "ipc_export",
+      [](uintptr_t ptr) {
+        unsigned char h[64];
+        uint64_t off = 0;
+        if (xt_ipc_export(reinterpret_cast<const void*>(ptr), h, &off) != XT_OK)
+          throw std::runtime_error(xt_last_error());
+        return py::make_tuple(py::bytes(reinterpret_cast<const char*>(h), 64), off);
+      },
+      py::arg("ptr"));
+  m.def(
+      "ipc_open",
+      [](py::bytes handle) {
+        std::string h = handle;
+        if (h.size() != 64) throw std::invalid_argument("ipc_open: handle must be 64 bytes");
+        void* base = nullptr;
+        if (xt_ipc_open(reinterpret_cast<const unsigned char*>(h.data()), &base) != XT_OK)
+          throw std::runtime_error(xt_last_error());
+        return reinterpret_cast<uintptr_t>(base);
+      },
+      py::arg("handle"));
+  m.def(
+      "ipc_close",
+      [](uintptr_t base) {
+        if (xt_ipc_close(reinterpret_cast<void*>(base)) != XT_OK) throw std::runtime_error(xt_last_error());
+      },
+      py::arg("base"));
+  m.def(
       "set_sm_budget",
       [](int sms) {
         if (xt_set_sm_budget(sms) != XT_OK) throw std::invalid_argument(xt_last_error());

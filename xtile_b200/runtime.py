@@ -41,6 +41,44 @@ def _signature(module: Module, func: str | None):
     return sig
 
 
+class PeerArray:
+    """An array in another GPU's memory, mapped into this process over NVLink.
+
+    ``export_array(t)`` on the owning process gives a picklable handle;
+    ``PeerArray.open(handle, shape, dtype)`` maps it here.  ``launch`` takes a
+    PeerArray wherever it takes a tensor: the kernel reads or writes the
+    owner's memory directly (the sharded matmul stores its rows straight into
+    rank 0's output this way, with no separate gather).
+    """
+
+    def __init__(self, base: int, offset: int, shape: tuple, dtype) -> None:
+        self._base = base
+        self.ptr = base + offset
+        self.shape = tuple(shape)
+        self.dtype = dtype
+
+    @classmethod
+    def open(cls, handle: tuple, shape: tuple, dtype) -> "PeerArray":
+        blob, offset = handle
+        return cls(int(_native.ipc_open(blob)), int(offset), shape, dtype)
+
+    def data_ptr(self) -> int:
+        return self.ptr
+
+    def close(self) -> None:
+        if self._base:
+            _native.ipc_close(self._base)
+            self._base = 0
+
+
+def export_array(t) -> tuple:
+    """Picklable CUDA IPC handle of tensor ``t`` for ``PeerArray.open``."""
+    if not t.is_cuda or not t.is_contiguous():
+        raise ValueError("export_array: a contiguous CUDA tensor is required")
+    blob, offset = _native.ipc_export(t.data_ptr())
+    return bytes(blob), int(offset)
+
+
 def _check_arrays(module: Module, arrays: Sequence, func: str | None):
     import torch
 
@@ -52,6 +90,12 @@ def _check_arrays(module: Module, arrays: Sequence, func: str | None):
     for t, (name, is_memref, elem, shape, dtype) in zip(arrays, sig):
         if not is_memref:
             raise TypeError(f"argument %{name} is not a memref; only memref kernels can be launched")
+        if isinstance(t, PeerArray):
+            if dtype is None or t.dtype != dtype:
+                raise TypeError(f"array %{name} must be {elem}, got {t.dtype}")
+            if t.shape != shape:
+                raise ValueError(f"array %{name} must have shape {shape}, got {t.shape}")
+            continue
         if not isinstance(t, torch.Tensor):
             raise TypeError(f"array %{name} must be a torch tensor, got {type(t).__name__}")
         if not t.is_cuda:
@@ -66,6 +110,8 @@ def _check_arrays(module: Module, arrays: Sequence, func: str | None):
             raise ValueError(f"array %{name} must have shape {shape}, got {tuple(t.shape)}")
         if not t.is_contiguous():
             raise ValueError(f"array %{name} must be contiguous (row-major)")
+    if device is None:
+        raise ValueError("launch needs at least one local CUDA tensor to pick the device")
     return device
 
 
