@@ -47,7 +47,14 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 
 # DRAM bytes per launch of the dominant kernel from one ncu capture
 # (dram__bytes_read.sum + dram__bytes_write.sum), summarised in profiles/.
-NCU_TRAFFIC_BYTES: dict[str, float] = {}
+# ncu flushes the caches before the capture, so output bytes still in L2 when
+# the kernel ends are not in these figures (they are written back later).
+NCU_TRAFFIC_BYTES: dict[str, float] = {
+    "matmul": 89_688_320 + 40_005_376,
+    "conv2d": 12_956_416 + 256,
+    "add": 33_561_088 + 10_496,
+    "softmax": 33_567_488 + 498_432,
+}
 
 
 # ---------------------------------------------------------------- workloads

@@ -56,3 +56,16 @@ def test_parse_and_print_through_c_abi():
     bad = ctypes.c_void_p()
     assert lib.xt_parse(b"func.func @k() {\n xt.nope() : () -> ()\n}", ctypes.byref(bad)) == 1
     assert b"custom op 'xt.nope' is unknown" in lib.xt_last_error()
+
+
+def test_host_side_argument_checks_of_new_entry_points():
+    lib = ctypes.CDLL(str(LIB))
+    lib.xt_last_error.restype = ctypes.c_char_p
+    assert lib.xt_set_sm_budget(-1) == 5                       # XT_EARGUMENT
+    assert b"negative" in lib.xt_last_error()
+    assert lib.xt_set_sm_budget(0) == 0
+    handle = (ctypes.c_ubyte * 64)()
+    offset = ctypes.c_uint64()
+    assert lib.xt_ipc_export(None, handle, ctypes.byref(offset)) == 5
+    base = ctypes.c_void_p()
+    assert lib.xt_ipc_open(None, ctypes.byref(base)) == 5
