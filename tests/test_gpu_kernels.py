@@ -218,7 +218,10 @@ def test_matmul_bf16_kloop_small():
                                       ((64, 64, 8), (64, 64, 8)),
                                       # 3 k-blocks per tile, 320 tiles: tiles share pipeline groups
                                       # and most CTAs end inside a group
-                                      ((5120, 2048, 192), (128, 256, 192))])
+                                      ((5120, 2048, 192), (128, 256, 192)),
+                                      # 80 pair tiles on 74 pairs: the last 6 split into column halves
+                                      ((2560, 2048, 128), (128, 256, 128)),
+                                      ((2523, 1944, 96), (128, 256, 96))])
 def test_matmul_bf16_ragged(mnk, tile):
     M, N, K = mnk
     tm, tn, tk = tile

@@ -46,6 +46,7 @@ struct Params {
   const float* acc;
   int64_t M, N, ldc, m_begin;
   int tiles_m, tiles_n, num_kb;
+  int tail_begin, num_items;  // work items: whole tiles, then the last partial wave split in column halves
   uint8_t c_elem;
   int n_epi;
   uint8_t epi_kind[4];
@@ -53,6 +54,32 @@ struct Params {
   int tma_store;  // plain f32 output: epilogue stores through shared memory with TMA
   uint32_t* error_word;
 };
+
+// Work item -> tile and its column range.  Items below tail_begin are whole
+// 256 x 256 tiles; the tiles of the last, partial wave are split into two
+// 256 x 128 items each, so that wave finishes in half the time.
+struct Item {
+  int mt, col0, ncols;  // pair-tile row, first output column, 256 or 128 columns
+};
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& mt, int& nt);
+
+template <class P>
+__device__ __forceinline__ Item item_coords(const P& p, int item) {
+  Item it;
+  int nt;
+  if (item < p.tail_begin) {
+    tile_coords(item, p.tiles_m, p.tiles_n, it.mt, nt);
+    it.col0 = nt * 256;
+    it.ncols = 256;
+  } else {
+    const int j = item - p.tail_begin;
+    tile_coords(p.tail_begin + (j >> 1), p.tiles_m, p.tiles_n, it.mt, nt);
+    it.col0 = nt * 256 + (j & 1) * 128;
+    it.ncols = 128;
+  }
+  return it;
+}
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& mt, int& nt) {
   const int per_group = kGroupM * tiles_n;
@@ -113,8 +140,9 @@ struct PairTraits<kBF16> {
   static constexpr int kChunkBytes = kBK * 128;
   static constexpr int kMmaK = 16;
   static constexpr uint32_t kIdesc = instr_desc(1, 1, 1, 0, 1, 256, 256);
-  static __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
-    umma_bf16_pair(d, a, b, kIdesc, acc);
+  static constexpr uint32_t kIdescHalf = instr_desc(1, 1, 1, 0, 1, 256, 128);
+  static __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    umma_bf16_pair(d, a, b, idesc, acc);
   }
 };
 template <>
@@ -125,8 +153,9 @@ struct PairTraits<kI8> {
   static constexpr int kChunkBytes = kBK * 128;
   static constexpr int kMmaK = 32;
   static constexpr uint32_t kIdesc = instr_desc(2, 1, 1, 0, 1, 256, 256);
-  static __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
-    umma_i8_pair(d, a, b, kIdesc, acc);
+  static constexpr uint32_t kIdescHalf = instr_desc(2, 1, 1, 0, 1, 256, 128);  // unused: int8 tiles are never split
+  static __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    umma_i8_pair(d, a, b, idesc, acc);
   }
 };
 
@@ -181,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const Abort ab{abort_flag, p.error_word};
-  const int num_tiles = p.tiles_m * p.tiles_n;  // pair tiles
+  const int num_items = p.num_items;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -190,25 +219,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0, armed = 0, armed_phase = 0;
       bool ok = true;
-      for (int t = pair; t < num_tiles && ok; t += npairs) {
-        int mt, nt;
-        tile_coords(t, p.tiles_m, p.tiles_n, mt, nt);
-        const int32_t row0 = static_cast<int32_t>(p.m_begin + static_cast<int64_t>(mt) * 256 + rank * 128);
-        const int32_t col0 = nt * 256 + static_cast<int32_t>(rank) * 128;
+      for (int t = pair; t < num_items && ok; t += npairs) {
+        const Item it = item_coords(p, t);
+        const int32_t row0 = static_cast<int32_t>(p.m_begin + static_cast<int64_t>(it.mt) * 256 + rank * 128);
+        // this CTA's half of the item's columns: 128 (two 64-column chunks, or one int8 chunk) or 64
+        const int32_t col0 = it.col0 + static_cast<int32_t>(rank) * (it.ncols / 2);
+        const int chunks = it.ncols == 256 ? T::kChunks : 1;
+        const uint32_t bytes = static_cast<uint32_t>(2 * (kPAStage + chunks * T::kChunkBytes));
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, ab, kErrProducer)) {
             ok = false;
             break;
           }
           if (leader) {
-            mbar_arrive_expect_tx(&full[stage], 2 * kPStageBytes);
+            mbar_arrive_expect_tx(&full[stage], bytes);
             armed |= 1u << stage;
             armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
           }
           const uint32_t bar = full0 + static_cast<uint32_t>(stage) * 8u;
           tma_load_2d_pair(sa + stage * kPAStage, &tma_a, bar, kb * T::kBK, row0);
-#pragma unroll
-          for (int c = 0; c < T::kChunks; ++c)
+          for (int c = 0; c < chunks; ++c)
             tma_load_2d_pair(sb + stage * kPBStage + c * T::kChunkBytes, &tma_b, bar, col0 + c * T::kChunkN,
                              kb * T::kBK);
           if (++stage == kPStages) {
@@ -229,9 +259,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int iter = 0;
       bool ok = true;
       const uint32_t sa_base = smem_addr(sa), sb_base = smem_addr(sb);
-      for (int t = pair; t < num_tiles && ok; t += npairs, ++iter) {
+      for (int t = pair; t < num_items && ok; t += npairs, ++iter) {
         const int acc = iter & 1;
         const uint32_t acc_phase = (iter >> 1) & 1;
+        const uint32_t idesc = t < p.tail_begin ? T::kIdesc : T::kIdescHalf;
         if (!__all_sync(0xffffffffu, mbar_wait(&tempty[acc], acc_phase ^ 1, ab, kErrMma))) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kBN;
@@ -249,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (elect_sync()) {
 #pragma unroll
             for (int k = 0; k < 128 / 32; ++k)
-              T::mma(d_tmem, ad + static_cast<uint64_t>(k * 2), bd + static_cast<uint64_t>(k * T::kMmaK * 8),
+              T::mma(d_tmem, ad + static_cast<uint64_t>(k * 2), bd + static_cast<uint64_t>(k * T::kMmaK * 8), idesc,
                      (kb | k) != 0 ? 1u : 0u);
             umma_commit_pair(&empty[stage], 0x3);
           }
@@ -275,24 +306,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp - 4;  // TMEM lane quarter
     const uint32_t tempty0 = mapa_shared(smem_addr(tempty), 0);
     int iter = 0;
-    for (int t = pair; t < num_tiles; t += npairs, ++iter) {
+    for (int t = pair; t < num_items; t += npairs, ++iter) {
       const int acc = iter & 1;
       const uint32_t acc_phase = (iter >> 1) & 1;
       const bool ok = mbar_wait_warp(&tfull[acc], acc_phase, ab, kErrEpilogue);
       if (named_barrier_or(2, 128, !ok)) break;  // all four warps stop together (named barriers below)
       tc_fence_after();
-      int mt, nt;
-      tile_coords(t, p.tiles_m, p.tiles_n, mt, nt);
+      const Item it = item_coords(p, t);
+      const int mt = it.mt;
+      const int nchunks = it.ncols / 32;
       const int64_t r_local = static_cast<int64_t>(mt) * 256 + rank * 128 + q * 32 + lane;
       const int64_t row = p.m_begin + r_local;
       const bool row_ok = r_local < p.M;
       const bool plain = p.acc == nullptr && p.n_epi == 0;
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
+      for (int c = 0; c < nchunks; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kBN + c * 32, r);
         tmem_wait_ld();
-        if (c == kBN / 32 - 1) {
+        if (c == nchunks - 1) {
           // every thread of this CTA has read the accumulator: one arrival for the CTA
           tc_fence_before();
           named_barrier_sync(1, 128);
@@ -322,13 +354,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tma_c, buf, nt * 256 + c * 32,
+            tma_store_2d(&tma_c, buf, it.col0 + c * 32,
                          static_cast<int32_t>(p.m_begin + static_cast<int64_t>(mt) * 256 + rank * 128 + q * 32));
             bulk_commit_group();
           }
           continue;
         }
-        const int64_t col0 = static_cast<int64_t>(nt) * 256 + c * 32;
+        const int64_t col0 = static_cast<int64_t>(it.col0) + c * 32;
         if (!row_ok || col0 >= p.N) continue;
         float v[32];
 #pragma unroll
@@ -426,6 +458,7 @@ cudaError_t launch_pair(const GemmArgs& a, cudaStream_t stream) {
   p.tiles_n = static_cast<int>((a.N + 255) / 256);
   p.num_kb = static_cast<int>((a.K + T::kBK - 1) / T::kBK);
   p.c_elem = a.c_elem;
+  p.tail_begin = p.num_items = p.tiles_m * p.tiles_n;
   p.n_epi = a.n_epi;
   for (int i = 0; i < 4; ++i) {
     p.epi_kind[i] = a.epi_kind[i];
@@ -447,6 +480,13 @@ cudaError_t launch_pair(const GemmArgs& a, cudaStream_t stream) {
   if (a.max_sms > 0 && a.max_sms < sms) sms = a.max_sms;
   int pairs = tiles < sms / 2 ? tiles : sms / 2;
   if (pairs < 1) pairs = 1;
+  // Split the last partial wave's tiles into column halves (bf16 only: an
+  // int8 half is 64 bytes wide, narrower than the 128-byte swizzle atom).
+  const int tail = tiles % pairs;
+  if (AB == kBF16 && tiles > pairs && tail > 0 && 2 * tail <= pairs) {
+    p.tail_begin = tiles - tail;
+    p.num_items = tiles + tail;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
   cfg.blockDim = dim3(kThreads);
