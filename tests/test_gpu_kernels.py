@@ -362,15 +362,16 @@ def test_conv_config4_bf16_sampled():
     ((2, 10, 30, 128), (3, 3, 128, 64), (5, 30), None, (1, 1)),   # window kernel, 2 channel chunks
     ((1, 9, 9, 64), (1, 1, 64, 256), (9, 9), (0, 0), (1, 1)),     # 1x1, 256 output channels
     ((1, 16, 16, 32), (5, 5, 32, 32), (16, 16), (2, 2), (1, 1)),  # window kernel, any-tap loop
-    ((3, 16, 16, 32), (5, 5, 32, 32), (16, 16), (2, 2), (1, 1)),  # CTA-pair kernel, any-tap loop, odd images
+    ((3, 16, 16, 32), (5, 5, 32, 32), (16, 16), (2, 2), (1, 1)),  # 5 stacked taps, 4 shifted rows
+    ((1, 12, 20, 64), (3, 3, 64, 64), (4, 20), (2, 2), (2, 2)),   # stacked taps with dilation 2
 ])
 def test_conv_bf16_shapes(shape, kshape, tile, pad, dil):
     got, ref = conv_case(shape, kshape, tile, torch.bfloat16, 4, pad=pad, dil=dil)
     bf16_close(got, ref)
 
 
-def test_conv_int8_cta_pair_bit_exact():
-    # two images: the CTA-pair kernel with kind::i8
+def test_conv_int8_two_images_bit_exact():
+    # two images, stacked taps with kind::i8
     got, ref = conv_case((2, 16, 32, 128), (3, 3, 128, 64), (16, 32), torch.int8, 8)
     assert np.array_equal(got, ref)
 

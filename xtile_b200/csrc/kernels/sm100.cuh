@@ -117,10 +117,10 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, c
   bool ok = true;
   if ((threadIdx.x & 31) == 0) {
     uint64_t t0 = 0;
-    uint32_t polls = 0, sleep_ns = 32;
+    uint32_t polls = 0, sleep_ns = 16;
     while (!mbar_try_wait(bar, parity)) {
       __nanosleep(sleep_ns);
-      if (sleep_ns < 256) sleep_ns *= 2;
+      if (sleep_ns < 64) sleep_ns *= 2;  // short: a long sleep delays the epilogue behind a finished tile
       if ((++polls & 255u) != 0) continue;
       if (*ab.flag) {
         ok = false;
