@@ -25,6 +25,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "../kernels.h"
 #include "sm100.cuh"
 
@@ -466,14 +468,16 @@ cudaError_t launch_pair(const GemmArgs& a, cudaStream_t stream) {
   }
   p.error_word = a.error_word;
   p.tma_store = tma_store ? 1 : 0;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_pair<AB>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
+  // the shared-memory opt-in is per device: remember which devices have it
+  static std::atomic<uint64_t> attr_devices{0};
+  const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
+  if (!(attr_devices.load(std::memory_order_relaxed) & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_pair<AB>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_devices.fetch_or(bit, std::memory_order_relaxed);
+  }
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int tiles = p.tiles_m * p.tiles_n;
   if (tiles == 0 || p.num_kb == 0) return cudaSuccess;
