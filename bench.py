@@ -76,7 +76,7 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
         args = (A((2048, 2048), xt.float32),) * 3
         mod = xt.convert(add_tiles, args=(*args, 32, 64), grid=(64, 32, 1), double_buffering=True)
         return dict(module=mod, inputs=[a, b], out_shape=(2048, 2048), out_dtype=torch.float32,
-                    unit="GB/s", bound="hbm", dtype="f32",
+                    unit="GB/s", dtype="f32",
                     config={"workload": "add", "shape": [2048, 2048], "block_tile": [32, 64],
                             "grid": [64, 32, 1]})
     if name == "softmax":
@@ -92,7 +92,7 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
         mod = xt.convert(softmax_rows, args=(A((8192, 1024), xt.float32), A((8192, 1024), xt.float32),
                                              1, 1024), grid=(8192, 1, 1), double_buffering=True)
         return dict(module=mod, inputs=[x], out_shape=(8192, 1024), out_dtype=torch.float32,
-                    unit="GB/s", bound="hbm", dtype="f32",
+                    unit="GB/s", dtype="f32",
                     config={"workload": "softmax", "shape": [8192, 1024], "block_tile": [1, 1024],
                             "grid": [8192, 1, 1]})
     if name in ("matmul", "sharded_matmul"):
@@ -126,7 +126,7 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
         if name == "sharded_matmul":
             cfg["parallelism"] = f"bid0 split over {world} GPU(s), NCCL gather of C rows to rank 0"
         return dict(module=mod, inputs=[a, b], out_shape=(M, N), out_dtype=torch.float32,
-                    unit="TFLOP/s", bound="tensor", dtype="bf16", config=cfg, sharded=name == "sharded_matmul")
+                    unit="TFLOP/s", dtype="bf16", config=cfg, sharded=name == "sharded_matmul")
     if name == "conv2d":
         @xt.kernel
         def conv2d_bf16(inp, filt, out, tile_h, tile_w, cin, cout, kh, kw):
@@ -143,7 +143,7 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
                                             A((32, 56, 56, 64), xt.float32), 8, 56, 64, 64, 3, 3),
                          grid=(32, 7, 1), double_buffering=True)
         return dict(module=mod, inputs=[x, f], out_shape=(32, 56, 56, 64), out_dtype=torch.float32,
-                    unit="TFLOP/s", bound="tensor", dtype="bf16",
+                    unit="TFLOP/s", dtype="bf16",
                     config={"workload": "conv2d", "input": [32, 56, 56, 64], "filter": [3, 3, 64, 64],
                             "pad": 1, "block_tile": [1, 8, 56, 64], "grid": [32, 7, 1]})
     raise SystemExit(f"unknown workload {name}")
@@ -519,17 +519,30 @@ def main() -> None:
     job_units = work if (sharded or world == 1) else work * world
     ms_per_step = total_ms / args.steps
     value = job_units / (ms_per_step * 1e-3) / scale
-    # one launch processes this rank's share of the Grid
-    launch_work = work * (hi - lo) / grid0
-    achieved = launch_work / (kernel_ms * 1e-3) / scale
-    if w["bound"] == "hbm":
+    # One launch processes this rank's share of the Grid.  The binding
+    # roofline is the one whose floor (work / peak) is longer: a TFLOP/s
+    # workload below the ridge point (FLOP per byte < tensor peak / HBM peak)
+    # is bound by HBM, not by the tensor pipe.
+    launch_bytes = plan["bytes"] * (hi - lo) / grid0
+    launch_flops = plan["flops"] * (hi - lo) / grid0
+    hbm_floor = launch_bytes / (peaks["hbm_gbs"] * 1e9)
+    tensor_floor = launch_flops / (peaks["bf16_tflops"] * 1e12)
+    bound = "hbm" if hbm_floor >= tensor_floor else "tensor"
+    if bound == "hbm":
         peak = peaks["hbm_gbs"]
-        achieved_r = launch_work / (kernel_ms * 1e-3) / 1e9
+        achieved_r = launch_bytes / (kernel_ms * 1e-3) / 1e9
         roof_unit = "GB/s"
     else:
         peak = peaks["bf16_tflops"]
-        achieved_r = achieved
+        achieved_r = launch_flops / (kernel_ms * 1e-3) / 1e12
         roof_unit = "TFLOP/s"
+    other = None
+    if launch_flops > 0:
+        # the non-binding roofline's fraction, for reference
+        if bound == "hbm":
+            other = {"tensor_frac": round(launch_flops / (kernel_ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4)}
+        else:
+            other = {"hbm_frac": round(launch_bytes / (kernel_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4)}
     line = {
         "metric": METRIC,
         "value": round(value, 3),
@@ -550,10 +563,10 @@ def main() -> None:
                               ("eager launches; rows stored into rank 0's output over NVLink, one-element "
                                "all-reduce per step" if peer else
                                "eager launches; step i's NCCL gather overlaps step i+1's compute"))},
-        "roofline": {"bound": w["bound"], "achieved": round(achieved_r, 2), "peak": peak, "unit": roof_unit,
+        "roofline": {"bound": bound, "achieved": round(achieved_r, 2), "peak": peak, "unit": roof_unit,
                      "frac": round(achieved_r / peak, 4), "peak_kind": f"{peak_kind} (burst)",
                      "traffic": NCU_TRAFFIC_BYTES.get(args.workload),
-                     "kernel_ms": round(kernel_ms, 4)},
+                     "kernel_ms": round(kernel_ms, 4), **(other or {})},
         "clocks": clock,
         "gpu_launches": args.steps,
         "device_error": err,

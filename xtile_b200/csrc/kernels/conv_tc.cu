@@ -38,6 +38,7 @@
 #include <cuda_runtime.h>
 
 #include "../kernels.h"
+#include "pdl.cuh"
 #include "sm100.cuh"
 
 namespace xt {
@@ -148,6 +149,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // set-up done: the next launch may be scheduled; global memory only after
+  // the previous one has completed
+  griddep_launch_dependents();
+  griddep_wait();
   const uint32_t tmem_base = *tmem_slot;
   const Abort ab{abort_flag, p.error_word};
   const int num_kb = p.KH * p.KW * p.kc;
@@ -474,6 +479,10 @@ __global__ void __launch_bounds__(kWinThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // set-up done: the next launch may be scheduled; global memory only after
+  // the previous one has completed
+  griddep_launch_dependents();
+  griddep_wait();
   const uint32_t tmem_base = *tmem_slot;
   const Abort ab{abort_flag, p.error_word};
   const int n_fbars = p.KH < kMaxFBars ? p.KH : kMaxFBars;
@@ -796,8 +805,7 @@ bool launch_window(const ConvArgs& a, const CUtensorMap& m_f, int span, EncodeIn
   auto go = [&](auto kernel) {
     *err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (*err != cudaSuccess) return;
-    kernel<<<grid, kWinThreads, smem, stream>>>(m_in, m_f, p);
-    *err = cudaGetLastError();
+    *err = PdlLaunch(grid, kWinThreads, smem, stream)(kernel, m_in, m_f, p);
   };
   if (p.KH == 3 && p.KW == 3)
     go(conv_window<AB, 3, 3>);
@@ -920,8 +928,7 @@ cudaError_t launch_typed(const ConvArgs& a, cudaStream_t stream) {
   const int smem = p.barrier_offset + 256 + 1024;
   cudaError_t e = cudaFuncSetAttribute(conv_tc<AB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  conv_tc<AB><<<p.num_tiles < sms ? p.num_tiles : sms, kThreads, smem, stream>>>(m_in, m_f, m_out, p);
-  return cudaGetLastError();
+  return PdlLaunch(p.num_tiles < sms ? p.num_tiles : sms, kThreads, smem, stream)(conv_tc<AB>, m_in, m_f, m_out, p);
 }
 
 }  // namespace

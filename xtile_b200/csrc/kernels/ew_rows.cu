@@ -17,6 +17,7 @@
 #include <cuda_runtime.h>
 
 #include "../kernels.h"
+#include "pdl.cuh"
 
 namespace xt {
 namespace dev {
@@ -73,6 +74,8 @@ __global__ void __launch_bounds__(kThreads) ew_binary_f32(const float* __restric
   // array (the loop only runs again past the grid-size limit): every load is
   // issued at kernel start, which measured faster on this HBM-bound op than
   // a persistent grid-stride loop with two vectors in flight per thread.
+  griddep_launch_dependents();
+  griddep_wait();
   const float4* a4 = reinterpret_cast<const float4*>(a);
   const float4* b4 = reinterpret_cast<const float4*>(b);
   float4* c4 = reinterpret_cast<float4*>(c);
@@ -111,6 +114,8 @@ __device__ __forceinline__ void put(float (&r)[N], int idx, float v) {
 }
 
 __global__ void __launch_bounds__(kThreads) ew_program(const __grid_constant__ EwArgs p) {
+  griddep_launch_dependents();
+  griddep_wait();
   int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
   for (int64_t i = p.begin + static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < p.end;
        i += stride) {
@@ -154,7 +159,9 @@ __global__ void __launch_bounds__(kThreads) softmax_rows_vec4(const float* __res
                                                                int64_t row_end, int64_t cols) {
   const int lane = threadIdx.x & 31;
   const int64_t row = row_begin + static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5);
+  griddep_launch_dependents();
   if (row >= row_end) return;
+  griddep_wait();
   const int64_t c4 = cols >> 2;
   const float4* xr = reinterpret_cast<const float4*>(x + row * cols);
   float4* yr = reinterpret_cast<float4*>(y + row * cols);
@@ -227,7 +234,9 @@ template <int PL>
 __global__ void __launch_bounds__(kThreads) rows_program(const __grid_constant__ RowArgs p) {
   const int lane = threadIdx.x & 31;
   const int64_t row = p.row_begin + static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5);
+  griddep_launch_dependents();
   if (row >= p.row_end) return;
+  griddep_wait();
   float v[kRowV][PL];
   float s[kRowS];
 #pragma unroll
@@ -333,16 +342,15 @@ cudaError_t launch_ew(const EwArgs& a, cudaStream_t stream) {
          15) == 0) {
       const int64_t n4 = n / 4;
       const int blocks = grid_for(n4 > 0 ? n4 : 1, kThreads, 0x7fffffff);
+      PdlLaunch launch(blocks, kThreads, 0, stream);
       switch (a.code[2].op) {
-        case kAdd: ew_binary_f32<kAdd><<<blocks, kThreads, 0, stream>>>(x, y, z, n4, n); break;
-        case kSub: ew_binary_f32<kSub><<<blocks, kThreads, 0, stream>>>(x, y, z, n4, n); break;
-        default: ew_binary_f32<kMul><<<blocks, kThreads, 0, stream>>>(x, y, z, n4, n); break;
+        case kAdd: return launch(ew_binary_f32<kAdd>, x, y, z, n4, n);
+        case kSub: return launch(ew_binary_f32<kSub>, x, y, z, n4, n);
+        default: return launch(ew_binary_f32<kMul>, x, y, z, n4, n);
       }
-      return cudaGetLastError();
     }
   }
-  ew_program<<<grid_for(n, kThreads, max_blocks), kThreads, 0, stream>>>(a);
-  return cudaGetLastError();
+  return PdlLaunch(grid_for(n, kThreads, max_blocks), kThreads, 0, stream)(ew_program, a);
 }
 
 cudaError_t launch_rows(const RowArgs& a, cudaStream_t stream) {
@@ -356,22 +364,22 @@ cudaError_t launch_rows(const RowArgs& a, cudaStream_t stream) {
     const int64_t chunks = (a.cols / 4 + 31) / 32;
     const float* x = a.in[0];
     float* y = a.out[0];
-    if (chunks <= 1) softmax_rows_vec4<1><<<blocks, kThreads, 0, stream>>>(x, y, a.row_begin, a.row_end, a.cols);
-    else if (chunks <= 2) softmax_rows_vec4<2><<<blocks, kThreads, 0, stream>>>(x, y, a.row_begin, a.row_end, a.cols);
-    else if (chunks <= 4) softmax_rows_vec4<4><<<blocks, kThreads, 0, stream>>>(x, y, a.row_begin, a.row_end, a.cols);
-    else if (chunks <= 8) softmax_rows_vec4<8><<<blocks, kThreads, 0, stream>>>(x, y, a.row_begin, a.row_end, a.cols);
-    else softmax_rows_vec4<16><<<blocks, kThreads, 0, stream>>>(x, y, a.row_begin, a.row_end, a.cols);
-    return cudaGetLastError();
+    PdlLaunch launch(blocks, kThreads, 0, stream);
+    if (chunks <= 1) return launch(softmax_rows_vec4<1>, x, y, a.row_begin, a.row_end, a.cols);
+    if (chunks <= 2) return launch(softmax_rows_vec4<2>, x, y, a.row_begin, a.row_end, a.cols);
+    if (chunks <= 4) return launch(softmax_rows_vec4<4>, x, y, a.row_begin, a.row_end, a.cols);
+    if (chunks <= 8) return launch(softmax_rows_vec4<8>, x, y, a.row_begin, a.row_end, a.cols);
+    return launch(softmax_rows_vec4<16>, x, y, a.row_begin, a.row_end, a.cols);
   }
   const int64_t pl = (a.cols + 31) / 32;
-  if (pl <= 1) rows_program<1><<<blocks, kThreads, 0, stream>>>(a);
-  else if (pl <= 2) rows_program<2><<<blocks, kThreads, 0, stream>>>(a);
-  else if (pl <= 4) rows_program<4><<<blocks, kThreads, 0, stream>>>(a);
-  else if (pl <= 8) rows_program<8><<<blocks, kThreads, 0, stream>>>(a);
-  else if (pl <= 16) rows_program<16><<<blocks, kThreads, 0, stream>>>(a);
-  else if (pl <= 32) rows_program<32><<<blocks, kThreads, 0, stream>>>(a);
-  else return cudaErrorInvalidValue;  // the planner admits rows up to 1024
-  return cudaGetLastError();
+  PdlLaunch launch(blocks, kThreads, 0, stream);
+  if (pl <= 1) return launch(rows_program<1>, a);
+  if (pl <= 2) return launch(rows_program<2>, a);
+  if (pl <= 4) return launch(rows_program<4>, a);
+  if (pl <= 8) return launch(rows_program<8>, a);
+  if (pl <= 16) return launch(rows_program<16>, a);
+  if (pl <= 32) return launch(rows_program<32>, a);
+  return cudaErrorInvalidValue;  // the planner admits rows up to 1024
 }
 
 }  // namespace dev

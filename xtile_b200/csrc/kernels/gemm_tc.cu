@@ -28,6 +28,7 @@
 #include <atomic>
 
 #include "../kernels.h"
+#include "pdl.cuh"
 #include "sm100.cuh"
 
 namespace xt {
@@ -210,6 +211,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   cluster_sync();  // both CTAs' barriers initialised before any cross-CTA arrive or load
   tc_fence_after();
+  // set-up done: the next launch may be scheduled; global memory only after
+  // the previous one has completed
+  griddep_launch_dependents();
+  griddep_wait();
   const uint32_t tmem_base = *tmem_slot;
   const Abort ab{abort_flag, p.error_word};
   const int num_items = p.num_items;
@@ -491,19 +496,7 @@ cudaError_t launch_pair(const GemmArgs& a, cudaStream_t stream) {
     p.tail_begin = tiles - tail;
     p.num_items = tiles + tail;
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * pairs);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = kPSmemBytes;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_pair<AB>, ma, mb, mc, p);
+  return PdlLaunch(dim3(2 * pairs), dim3(kThreads), kPSmemBytes, stream, 2)(gemm_pair<AB>, ma, mb, mc, p);
 }
 
 }  // namespace
