@@ -43,6 +43,14 @@ L2_BYTES = 126 * 2 ** 20
 # beside the GEMM at all (it waited for the GEMM to finish); 32 did.
 GATHER_SMS = 32
 GATHER_CHANNELS = 16
+# Rank 0's share of the sharded GEMM when the other ranks store their rows into
+# its memory: rank 0's NVLink ingress, not compute, bounds the step at 4 and 8
+# GPUs, and rank 0's own rows never cross NVLink.  The share balances rank 0's
+# compute against that ingress using two rates measured on B200s: the rows the
+# other ranks' kernels deliver into rank 0 while it computes (640-680 GB/s at
+# 4 and 8 GPUs) and the single-GPU rate of this GEMM (about 1450 TFLOP/s).
+PEER_INGEST_GBS = 680.0
+SHARDED_GEMM_TFLOPS = 1450.0
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 # DRAM bytes per launch of the dominant kernel from one ncu capture
@@ -166,10 +174,17 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=self.file, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
-        time.sleep(0.25)
+        # nvidia-smi takes a while to start (longer with 8 GPUs visible): wait
+        # for its first row, so the samples cover the timed region that follows
+        t0 = time.monotonic()
+        while self.proc is not None and time.monotonic() - t0 < 10.0:
+            if self.proc.poll() is not None or os.path.getsize(self.file.name) > 0:
+                break
+            time.sleep(0.02)
+        time.sleep(0.06)
         return self
 
     def __exit__(self, *exc):
@@ -241,9 +256,40 @@ def cpu_baseline(w: dict, xt, torch, budget_s: float = 12.0) -> dict:
             "sample": f"{done} of {len(order)} Blocks in {dt:.1f} s (numpy oracle, BLAS threads={threads})"}
 
 
-def bid0_share(grid0: int, world: int, rank: int) -> tuple[int, int]:
-    """Blocks [lo, hi) along bid0 that ``rank`` of ``world`` computes."""
-    return rank * grid0 // world, (rank + 1) * grid0 // world
+def bid0_share(grid0: int, world: int, rank: int, root_share: float | None = None) -> tuple[int, int]:
+    """Blocks [lo, hi) along bid0 that ``rank`` of ``world`` computes.
+
+    Contiguous ranges in rank order.  With ``root_share`` None every rank gets
+    an equal range; otherwise rank 0 gets that fraction of the Grid (at least
+    one Block, leaving at least one per other rank) and the other ranks split
+    the rest equally.
+    """
+    if root_share is None or world == 1:
+        return rank * grid0 // world, (rank + 1) * grid0 // world
+    if grid0 < world:
+        raise ValueError(f"grid0={grid0} has fewer Blocks than the {world} ranks")
+    b0 = min(grid0 - (world - 1), max(1, round(root_share * grid0)))
+    if rank == 0:
+        return 0, b0
+    rest = grid0 - b0
+    return b0 + (rank - 1) * rest // (world - 1), b0 + rank * rest // (world - 1)
+
+
+def gather_root_share(world: int, flops: float, out_bytes: float, tflops: float = SHARDED_GEMM_TFLOPS,
+                      ingest_gbs: float = PEER_INGEST_GBS) -> float:
+    """Rank 0's fraction of the Grid when rank 0 receives every other rank's rows.
+
+    Rank 0 computes f of the work (time f*T) while it takes in (1 - f) of the
+    output (time (1 - f)*R); each other rank computes (1 - f)/(world - 1) of
+    it.  The step ends when the slowest of the three does; with
+    m = max(R, T/(world - 1)) the best f is m / (T + m).
+    """
+    if world == 1:
+        return 1.0
+    t = flops / (tflops * 1e12)
+    r = out_bytes / (ingest_gbs * 1e9)
+    m = max(r, t / (world - 1))
+    return m / (t + m)
 
 
 def nccl_gather(out, rows_per_rank, world, rank, dist):
@@ -268,6 +314,8 @@ def main() -> None:
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="sharded_matmul on N>1 GPUs: ranks store their rows straight into rank 0's output "
                          "over NVLink (peer), or compute locally and gather with NCCL")
+    ap.add_argument("--root-share", type=float, default=None,
+                    help="peer gather: rank 0's fraction of the Grid (default: balanced against its NVLink ingress)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
@@ -306,7 +354,16 @@ def main() -> None:
         w["config"]["parallelism"] = f"{world} independent replicas"
     if sharded and (grid0 % world or w["out_shape"][0] % grid0):
         raise SystemExit(f"bench: grid0={grid0} does not split evenly over {world} ranks")
-    lo, hi = bid0_share(grid0, world, rank) if sharded else (0, grid0)
+    peer = sharded and world > 1 and args.gather == "peer"
+    # equal ranges: compute-only scaling (output left in place) and the NCCL gather
+    even_lo, even_hi = bid0_share(grid0, world, rank) if sharded else (0, grid0)
+    root_share = None
+    if peer:
+        out_bytes = w["out_shape"][0] * w["out_shape"][1] * 4
+        root_share = args.root_share if args.root_share is not None else gather_root_share(
+            world, plan["flops"], out_bytes)
+    lo, hi = bid0_share(grid0, world, rank, root_share) if sharded else (0, grid0)
+    rows_per_block = w["out_shape"][0] // grid0
     rows_per_rank = w["out_shape"][0] // world if sharded else 0
 
     # device-resident inputs; rotate enough sets to defeat the 126 MB L2
@@ -327,12 +384,13 @@ def main() -> None:
     # peer gather: every rank's kernel stores its rows into rank 0's output
     # arrays (mapped over NVLink with CUDA IPC); a one-element all-reduce per
     # step is the GPU-side barrier after which rank 0 holds all rows
-    peer = sharded and world > 1 and args.gather == "peer"
     targets = [o for _, o in sets]
     flag = torch.zeros(1, device=dev)
     if peer:
-        w["config"]["parallelism"] = (f"bid0 split over {world} GPUs; each rank's kernel stores its C rows "
-                                      f"into rank 0's output over NVLink (CUDA IPC)")
+        b0 = bid0_share(grid0, world, 0, root_share)[1]
+        w["config"]["parallelism"] = (f"bid0 split over {world} GPUs, rank 0 {b0} of {grid0} Blocks, the others "
+                                      f"{(grid0 - b0) // (world - 1)}-{-(-(grid0 - b0) // (world - 1))}; each "
+                                      f"rank's kernel stores its C rows into rank 0's output over NVLink (CUDA IPC)")
         handles = [xt.export_array(o) for o in targets] if rank == 0 else None
         box = [handles]
         dist.broadcast_object_list(box, src=0)
@@ -342,9 +400,9 @@ def main() -> None:
     computed = [torch.cuda.Event() for _ in range(n_sets)]
     gathered = [torch.cuda.Event() for _ in range(n_sets)]
 
-    def step(i):
+    def step(i, rng=(lo, hi)):
         ins, o = sets[i % n_sets]
-        xt.launch(mod, *ins, o, bid0_range=(lo, hi))
+        xt.launch(mod, *ins, o, bid0_range=rng)
 
     def sharded_step(i, start=None, end=None):
         if peer:
@@ -447,7 +505,7 @@ def main() -> None:
         dist.barrier()
         c0.record(stream)
         for i in range(args.steps):
-            step(i)
+            step(i, (even_lo, even_hi))
         c1.record(stream)
         torch.cuda.synchronize()
         t = torch.tensor([c0.elapsed_time(c1) / args.steps], device=dev)
@@ -459,8 +517,7 @@ def main() -> None:
     if not args.no_e2e:
         host_in = [t.pin_memory() for t in w["inputs"]]
         if sharded:
-            rows = w["inputs"][0].shape[0] // world
-            host_in[0] = host_in[0][rank * rows:(rank + 1) * rows]
+            host_in[0] = host_in[0][lo * rows_per_block:hi * rows_per_block]
         host_out = torch.empty(w["out_shape"] if (rank == 0 or not sharded) else (0,), dtype=w["out_dtype"]).pin_memory()
         ins, o = sets[0]
         h2d = sum(t.numel() * t.element_size() for t in host_in)
@@ -469,8 +526,7 @@ def main() -> None:
 
         def e2e_step():
             if sharded:
-                ins[0][lo * (w["out_shape"][0] // grid0):hi * (w["out_shape"][0] // grid0)].copy_(
-                    host_in[0], non_blocking=True)
+                ins[0][lo * rows_per_block:hi * rows_per_block].copy_(host_in[0], non_blocking=True)
                 ins[1].copy_(host_in[1], non_blocking=True)
             else:
                 for d, h in zip(ins, host_in):
@@ -575,7 +631,7 @@ def main() -> None:
         line["compute_only"] = {"ms_per_step": round(compute, 4),
                                 "value": round(work / (compute * 1e-3) / scale, 3)}
         line["gather"] = {"ms_per_step": round(ms_per_step - compute, 4),
-                          "bytes": (world - 1) * rows_per_rank * w["out_shape"][1] * 4}
+                          "bytes": (w["out_shape"][0] - (hi - lo) * rows_per_block) * w["out_shape"][1] * 4}
     if e2e is not None:
         e_ms, h2d, d2h = e2e
         line["e2e"] = {"value": round(job_units / (e_ms * 1e-3) / scale, 3), "unit": w["unit"],

@@ -88,3 +88,33 @@ def test_bid0_share_partitions_the_grid():
             spans = [bench.bid0_share(grid0, world, r) for r in range(world)]
             assert spans[0][0] == 0 and spans[-1][1] == grid0
             assert all(spans[r][1] == spans[r + 1][0] for r in range(world - 1))
+
+
+def test_bid0_share_with_root_share_partitions_the_grid():
+    for grid0 in (8, 13, 128):
+        for world in (2, 3, 8):
+            if grid0 < world:
+                continue
+            for f in (0.0, 0.1, 0.342, 0.9, 1.0):
+                spans = [bench.bid0_share(grid0, world, r, f) for r in range(world)]
+                assert spans[0][0] == 0 and spans[-1][1] == grid0
+                assert all(spans[r][1] == spans[r + 1][0] for r in range(world - 1))
+                assert all(hi > lo for lo, hi in spans)  # every rank gets at least one Block
+                sizes = [hi - lo for lo, hi in spans[1:]]
+                assert max(sizes) - min(sizes) <= 1  # the other ranks split the rest evenly
+
+
+def test_gather_root_share_balances_compute_and_ingress():
+    flops, out_bytes = 2.0 * 32768 * 8192 * 8192, 32768 * 8192 * 4
+    assert bench.gather_root_share(1, flops, out_bytes) == 1.0
+    # two GPUs: rank 1's compute, not rank 0's ingress, bounds the step
+    assert abs(bench.gather_root_share(2, flops, out_bytes) - 0.5) < 1e-12
+    for world in (4, 8):
+        f = bench.gather_root_share(world, flops, out_bytes)
+        t = flops / (bench.SHARDED_GEMM_TFLOPS * 1e12)
+        r = out_bytes / (bench.PEER_INGEST_GBS * 1e9)
+        # rank 0's compute equals its ingress, and the other ranks finish first
+        assert abs(f * t - (1 - f) * r) < 1e-12
+        assert (1 - f) / (world - 1) * t <= f * t
+    # slower links give rank 0 more of the Grid
+    assert bench.gather_root_share(8, flops, out_bytes, ingest_gbs=300.0) > bench.gather_root_share(8, flops, out_bytes)
