@@ -132,7 +132,8 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
         cfg = {"workload": name, "M": M, "N": N, "K": K, "block_tile": [tm, tn], "k_step": tk,
                "grid": list(grid)}
         if name == "sharded_matmul":
-            cfg["parallelism"] = f"bid0 split over {world} GPU(s), NCCL gather of C rows to rank 0"
+            cfg["parallelism"] = ("one GPU, the whole Grid" if world == 1 else
+                                  f"bid0 split over {world} GPUs, NCCL gather of C rows to rank 0")
         return dict(module=mod, inputs=[a, b], out_shape=(M, N), out_dtype=torch.float32,
                     unit="TFLOP/s", dtype="bf16", config=cfg, sharded=name == "sharded_matmul")
     if name == "conv2d":
@@ -159,18 +160,55 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons during the timed region."""
+    """Samples SM clocks, power and clock-event (throttle) reasons during the timed region.
+
+    NVML is read from a thread every 10 ms, so even a timed region of a few tens
+    of milliseconds gets samples; without NVML, ``nvidia-smi -lms 50`` is used.
+    Reading is all either does: no clock or power setting is changed.
+    """
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits (nvmlClocksEventReason*)
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
 
     def __init__(self, gpu_id: str):
         self.gpu = gpu_id
         self.proc = None
-        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.thread = None
+        self.rows: list[tuple[float, float, float, int]] = []
+        self.file = None
+
+    def _nvml_loop(self, nvml, handle, stop):
+        max_sm = float(nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM))
+        while not stop.is_set():
+            try:
+                sm = float(nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM))
+                reasons = int(nvml.nvmlDeviceGetCurrentClocksEventReasons(handle))
+                power = nvml.nvmlDeviceGetPowerUsage(handle) / 1000.0
+                self.rows.append((sm, max_sm, power, reasons))
+            except Exception:  # noqa: BLE001 - a failed read just drops the sample
+                pass
+            stop.wait(0.01)
 
     def __enter__(self):
+        import threading
+        try:
+            import pynvml as nvml
+            nvml.nvmlInit()
+            handle = nvml.nvmlDeviceGetHandleByUUID(self.gpu)
+            self.stop = threading.Event()
+            self.thread = threading.Thread(target=self._nvml_loop, args=(nvml, handle, self.stop), daemon=True)
+            self.thread.start()
+            t0 = time.monotonic()
+            while not self.rows and time.monotonic() - t0 < 5.0:
+                time.sleep(0.005)
+            return self
+        except Exception:  # noqa: BLE001 - no NVML: fall back to nvidia-smi
+            self.thread = None
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -188,6 +226,9 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -196,20 +237,29 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self) -> dict:
-        self.file.flush()
         rows = []
-        for line in Path(self.file.name).read_text().splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
-                rows.append(parts)
-        os.unlink(self.file.name)
+        if self.file is not None:
+            self.file.flush()
+            for line in Path(self.file.name).read_text().splitlines():
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                    bits = 0
+                    for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                                        "sw_power_cap"), parts[5:9]):
+                        if v.lower() == "active":
+                            bits |= self.REASON_BITS[name]
+                    power = float(parts[3]) if parts[3][:1].isdigit() else 0.0
+                    rows.append((float(parts[1]), float(parts[2]), power, bits))
+            os.unlink(self.file.name)
+        else:
+            rows = list(self.rows)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
-        sm = [float(r[1]) for r in rows]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
-                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3][0].isdigit())}
+        reasons = sorted({n for r in rows for n, bit in self.REASON_BITS.items() if r[3] & bit})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_min_mhz": min(r[0] for r in rows),
+                "sm_max_mhz": rows[0][1], "reasons": reasons, "samples": len(rows),
+                "power_w_max": max(r[2] for r in rows),
+                "source": "nvml, 10 ms" if self.file is None else "nvidia-smi, 50 ms"}
 
 
 # ---------------------------------------------------------------- helpers
@@ -300,6 +350,42 @@ def nccl_gather(out, rows_per_rank, world, rank, dist):
         dist.gather(mine, gather_list=[out[r * rows_per_rank:(r + 1) * rows_per_rank] for r in range(world)], dst=0)
     else:
         dist.gather(mine, dst=0)
+
+
+def roofline_line(plan: dict, share: float, kernel_ms: float, peaks: dict, peak_kind: str) -> dict:
+    """The ``roofline`` object for one launch of ``share`` of the Grid taking ``kernel_ms``.
+
+    The binding roofline is the one whose floor (work / peak) is longer: a
+    TFLOP/s workload below the ridge point (FLOP per byte < tensor peak / HBM
+    peak) is bound by HBM, not by the tensor pipe.  The denominator is the
+    burst peak: every workload here is timed alone, over a few tens of
+    milliseconds.  For tensor-bound launches of a millisecond or more the
+    fraction of the sustained GEMM peak (a seconds-long cuBLAS loop under the
+    1000 W power cap) is given beside it, for steps long enough to reach the cap.
+    """
+    launch_bytes = plan["bytes"] * share
+    launch_flops = plan["flops"] * share
+    secs = kernel_ms * 1e-3
+    hbm_floor = launch_bytes / (peaks["hbm_gbs"] * 1e9)
+    tensor_floor = launch_flops / (peaks["bf16_tflops"] * 1e12)
+    bound = "hbm" if hbm_floor >= tensor_floor else "tensor"
+    out = {"bound": bound}
+    if bound == "hbm":
+        achieved, peak, unit = launch_bytes / secs / 1e9, peaks["hbm_gbs"], "GB/s"
+    else:
+        achieved, peak, unit = launch_flops / secs / 1e12, peaks["bf16_tflops"], "TFLOP/s"
+    kind = f"{peak_kind} (burst)"
+    extra = {}
+    if launch_flops > 0:  # the non-binding roofline's fraction, for reference
+        if bound == "hbm":
+            extra["tensor_frac"] = round(launch_flops / secs / 1e12 / peaks["bf16_tflops"], 4)
+        else:
+            extra["hbm_frac"] = round(launch_bytes / secs / 1e9 / peaks["hbm_gbs"], 4)
+    if bound == "tensor" and kernel_ms >= 1.0 and "bf16_tflops_sustained" in peaks:
+        extra["frac_sustained"] = round(achieved / peaks["bf16_tflops_sustained"], 4)
+    out.update({"achieved": round(achieved, 2), "peak": peak, "unit": unit, "frac": round(achieved / peak, 4),
+                "peak_kind": kind, "traffic": None, "kernel_ms": round(kernel_ms, 4), **extra})
+    return out
 
 
 # ---------------------------------------------------------------- main
@@ -523,6 +609,46 @@ def main() -> None:
         h2d = sum(t.numel() * t.element_size() for t in host_in)
         d2h = host_out.numel() * host_out.element_size()
         e_steps = max(3, min(args.steps, 10))
+        e_note = "one stream: each step's copies in, launch and copy out in sequence"
+        # One GPU: a three-stage pipeline over two buffer sets.  One stream only
+        # copies inputs in, one only launches, one only copies results out, so
+        # step j + 1's host-to-device copies run while step j's result is copied
+        # back (PCIe carries both directions at once).  Events per buffer set
+        # keep a copy-in from overwriting inputs a kernel still reads and a
+        # kernel from overwriting a result still being copied out.  Every step
+        # moves all of its inputs in and its whole result out.
+        e_streams = [torch.cuda.Stream(dev) for _ in range(3)] if world == 1 else None
+        if e_streams:
+            e_note = ("three streams (copy in, launch, copy out) over two buffer sets: step j+1's "
+                      "host-to-device copies overlap step j's device-to-host copy")
+            e_sets = [sets[0], ([torch.empty_like(t) for t in ins], torch.empty_like(o))]
+            host_outs = [host_out, torch.empty_like(host_out).pin_memory()]
+            ev_in, ev_k, ev_out = ([torch.cuda.Event() for _ in range(2)] for _ in range(3))
+
+        def e2e_step_pipe(j):
+            b = j % 2
+            e_ins, e_o = e_sets[b]
+            s_in, s_k, s_out = e_streams
+            with torch.cuda.stream(s_in):
+                if j >= 2:
+                    s_in.wait_event(ev_k[b])  # step j - 2's kernel has read these inputs
+                if sharded:
+                    e_ins[0][lo * rows_per_block:hi * rows_per_block].copy_(host_in[0], non_blocking=True)
+                    e_ins[1].copy_(host_in[1], non_blocking=True)
+                else:
+                    for d, h in zip(e_ins, host_in):
+                        d.copy_(h, non_blocking=True)
+                ev_in[b].record(s_in)
+            with torch.cuda.stream(s_k):
+                s_k.wait_event(ev_in[b])
+                if j >= 2:
+                    s_k.wait_event(ev_out[b])  # step j - 2's result has been copied out
+                xt.launch(mod, *e_ins, e_o, bid0_range=(lo, hi))
+                ev_k[b].record(s_k)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_k[b])
+                host_outs[b].copy_(e_o, non_blocking=True)
+                ev_out[b].record(s_out)
 
         def e2e_step():
             if sharded:
@@ -541,15 +667,27 @@ def main() -> None:
             if host_out.numel():
                 host_out.copy_(o, non_blocking=True)
 
-        e2e_step()
+        if e_streams:
+            e2e_step_pipe(0)
+            e2e_step_pipe(1)
+        else:
+            e2e_step()
         torch.cuda.synchronize()
         if dist:
             dist.barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(e_steps):
-            e2e_step()
+        if e_streams:
+            for es in e_streams:
+                es.wait_stream(stream)
+            for j in range(2, 2 + e_steps):
+                e2e_step_pipe(j)
+            for es in e_streams:
+                stream.wait_stream(es)
+        else:
+            for _ in range(e_steps):
+                e2e_step()
         e1.record(stream)
         torch.cuda.synchronize()
         e_ms = e0.elapsed_time(e1) / e_steps
@@ -557,7 +695,7 @@ def main() -> None:
             t = torch.tensor([e_ms], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e_ms = t.item()
-        e2e = (e_ms, h2d, d2h)
+        e2e = (e_ms, h2d, d2h, e_note)
 
     if dist:
         dist.barrier()
@@ -575,30 +713,8 @@ def main() -> None:
     job_units = work if (sharded or world == 1) else work * world
     ms_per_step = total_ms / args.steps
     value = job_units / (ms_per_step * 1e-3) / scale
-    # One launch processes this rank's share of the Grid.  The binding
-    # roofline is the one whose floor (work / peak) is longer: a TFLOP/s
-    # workload below the ridge point (FLOP per byte < tensor peak / HBM peak)
-    # is bound by HBM, not by the tensor pipe.
-    launch_bytes = plan["bytes"] * (hi - lo) / grid0
-    launch_flops = plan["flops"] * (hi - lo) / grid0
-    hbm_floor = launch_bytes / (peaks["hbm_gbs"] * 1e9)
-    tensor_floor = launch_flops / (peaks["bf16_tflops"] * 1e12)
-    bound = "hbm" if hbm_floor >= tensor_floor else "tensor"
-    if bound == "hbm":
-        peak = peaks["hbm_gbs"]
-        achieved_r = launch_bytes / (kernel_ms * 1e-3) / 1e9
-        roof_unit = "GB/s"
-    else:
-        peak = peaks["bf16_tflops"]
-        achieved_r = launch_flops / (kernel_ms * 1e-3) / 1e12
-        roof_unit = "TFLOP/s"
-    other = None
-    if launch_flops > 0:
-        # the non-binding roofline's fraction, for reference
-        if bound == "hbm":
-            other = {"tensor_frac": round(launch_flops / (kernel_ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4)}
-        else:
-            other = {"hbm_frac": round(launch_bytes / (kernel_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4)}
+    roofline = roofline_line(plan, (hi - lo) / grid0, kernel_ms, peaks, peak_kind)
+    roofline["traffic"] = NCU_TRAFFIC_BYTES.get(args.workload)
     line = {
         "metric": METRIC,
         "value": round(value, 3),
@@ -615,14 +731,11 @@ def main() -> None:
         "config": {**w["config"], "l2": f"{n_sets} rotating input/output sets" if n_sets > 1
                    else "working set larger than L2",
                    "timing": ("CUDA-graph replay of K launches, events recorded inside the graph"
-                              if not sharded else
+                              if not sharded else "eager launches, events around each launch" if world == 1 else
                               ("eager launches; rows stored into rank 0's output over NVLink, one-element "
                                "all-reduce per step" if peer else
                                "eager launches; step i's NCCL gather overlaps step i+1's compute"))},
-        "roofline": {"bound": bound, "achieved": round(achieved_r, 2), "peak": peak, "unit": roof_unit,
-                     "frac": round(achieved_r / peak, 4), "peak_kind": f"{peak_kind} (burst)",
-                     "traffic": NCU_TRAFFIC_BYTES.get(args.workload),
-                     "kernel_ms": round(kernel_ms, 4), **(other or {})},
+        "roofline": roofline,
         "clocks": clock,
         "gpu_launches": args.steps,
         "device_error": err,
@@ -633,9 +746,10 @@ def main() -> None:
         line["gather"] = {"ms_per_step": round(ms_per_step - compute, 4),
                           "bytes": (w["out_shape"][0] - (hi - lo) * rows_per_block) * w["out_shape"][1] * 4}
     if e2e is not None:
-        e_ms, h2d, d2h = e2e
+        e_ms, h2d, d2h, e_note = e2e
         line["e2e"] = {"value": round(job_units / (e_ms * 1e-3) / scale, 3), "unit": w["unit"],
-                       "ms_per_step": round(e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+                       "ms_per_step": round(e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                       "pipelining": e_note}
     if not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(w, xt, torch)
     print(json.dumps(line), flush=True)

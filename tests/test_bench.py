@@ -1,0 +1,51 @@
+"""Host-side pieces of ``bench.py``: the roofline object and the clock summary.
+
+These run on the CPU; the timings themselves need a B200 (``bench.py``).
+"""
+import bench
+
+PEAKS = {"hbm_gbs": 6544.7, "bf16_tflops": 1634.5, "bf16_tflops_sustained": 1385.9}
+
+
+def test_matmul_is_tensor_bound_against_the_burst_peak():
+    plan = {"flops": 2.0 * 4096 ** 3, "bytes": 134_217_728.0}
+    r = bench.roofline_line(plan, 1.0, 0.1, PEAKS, "measured")
+    assert r["bound"] == "tensor" and r["unit"] == "TFLOP/s" and r["peak"] == 1634.5
+    assert abs(r["achieved"] - plan["flops"] / 1e-4 / 1e12) < 0.01
+    assert abs(r["frac"] - r["achieved"] / 1634.5) < 1e-4
+    assert "hbm_frac" in r and "frac_burst" not in r and r["peak_kind"] == "measured (burst)"
+
+
+def test_conv_below_the_ridge_is_hbm_bound():
+    plan = {"flops": 7_398_752_256.0, "bytes": 38_608_896.0}
+    r = bench.roofline_line(plan, 1.0, 0.014, PEAKS, "measured")
+    assert r["bound"] == "hbm" and r["unit"] == "GB/s" and r["peak"] == 6544.7
+    assert abs(r["achieved"] - 38_608_896.0 / 14e-6 / 1e9) < 0.01
+    assert abs(r["tensor_frac"] - plan["flops"] / 14e-6 / 1e12 / 1634.5) < 1e-4
+
+
+def test_elementwise_has_no_tensor_fraction():
+    r = bench.roofline_line({"flops": 0.0, "bytes": 50_331_648.0}, 1.0, 0.009, PEAKS, "measured")
+    assert r["bound"] == "hbm" and "tensor_frac" not in r and "hbm_frac" not in r
+
+
+def test_long_tensor_launches_also_report_the_sustained_fraction():
+    plan = {"flops": 2.0 * 32768 * 8192 * 8192, "bytes": 1.6e9}
+    r = bench.roofline_line(plan, 1.0, 3.2, PEAKS, "measured")
+    assert r["bound"] == "tensor" and r["peak"] == 1634.5 and r["peak_kind"] == "measured (burst)"
+    assert abs(r["frac_sustained"] - r["achieved"] / 1385.9) < 1e-4
+    # a share of the Grid scales the work, not the time
+    half = bench.roofline_line(plan, 0.5, 3.2, PEAKS, "measured")
+    assert abs(half["achieved"] - r["achieved"] / 2) < 0.02
+
+
+def test_clock_summary_from_nvml_samples():
+    c = bench.ClockSampler("GPU-test")
+    c.rows = [(1965.0, 1965.0, 700.0, 0), (1800.0, 1965.0, 990.0, 0x4), (1965.0, 1965.0, 800.0, 0)]
+    s = c.summary()
+    assert s["sm_mhz"] == 1965.0 and s["sm_min_mhz"] == 1800.0 and s["samples"] == 3
+    assert s["reasons"] == ["sw_power_cap"] and s["power_w_max"] == 990.0
+
+
+def test_clock_summary_without_samples_is_marked_unavailable():
+    assert bench.ClockSampler("GPU-test").summary()["reasons"] == ["unavailable"]
