@@ -396,7 +396,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="sharded_matmul",
                     choices=["add", "softmax", "matmul", "conv2d", "sharded_matmul"])
-    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference", "torch"],
+                    help="b200: this backend; reference: the reference's CPU path; torch: the vendor library "
+                         "(cuBLAS, cuDNN) through PyTorch on one GPU, for context")
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="sharded_matmul on N>1 GPUs: ranks store their rows straight into rank 0's output "
                          "over NVLink (peer), or compute locally and gather with NCCL")
@@ -413,6 +415,10 @@ def main() -> None:
 
     if args.impl == "reference":
         run_reference(args, world, rank, torch)
+        return
+    if args.impl == "torch":
+        if rank == 0:
+            run_torch_library(args, torch)
         return
 
     import xtile as xt
@@ -755,6 +761,66 @@ def main() -> None:
     print(json.dumps(line), flush=True)
     if dist:
         dist.destroy_process_group()
+
+
+def run_torch_library(args, torch) -> None:
+    """Times the workload through PyTorch's CUDA libraries on one GPU, for context.
+
+    add and softmax run torch's own kernels, matmul cuBLAS (``torch.mm`` with
+    an f32 output), conv2d cuDNN on channels-last bf16 tensors (its output is
+    bf16, half the bytes of this backend's f32 output).  The same inputs,
+    rotating buffer sets and graph-replay timing as the b200 arm.
+    """
+    import xtile as xt
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    w = build_workload(args.workload, xt, torch, 1, 0)
+    plan = w["module"].plan()
+    name = args.workload
+    ins = [t.to(dev) for t in w["inputs"]]
+    if name == "conv2d":
+        x, f = ins
+        ins = [x.permute(0, 3, 1, 2), f.permute(3, 2, 0, 1).contiguous(memory_format=torch.channels_last)]
+    ws = sum(t.numel() * t.element_size() for t in ins) + 2 * torch.Size(w["out_shape"]).numel() * 4
+    n_sets = 1 if ws > 3 * L2_BYTES else int(-(-3 * L2_BYTES // ws)) + 1
+    sets = [ins] + [[t.clone(memory_format=torch.preserve_format) for t in ins] for _ in range(n_sets - 1)]
+    outs = [torch.empty(w["out_shape"], dtype=torch.float32, device=dev) for _ in range(n_sets)]
+    if name == "add":
+        lib = "torch.add (out=)"
+        fn = lambda i: torch.add(*sets[i % n_sets], out=outs[i % n_sets])  # noqa: E731
+    elif name == "softmax":
+        lib = "torch.softmax"
+        fn = lambda i: torch.softmax(sets[i % n_sets][0], -1)  # noqa: E731
+    elif name in ("matmul", "sharded_matmul"):
+        lib = "cuBLAS via torch.mm(out_dtype=float32, out=)"
+        fn = lambda i: torch.mm(*sets[i % n_sets], out_dtype=torch.float32, out=outs[i % n_sets])  # noqa: E731
+    else:
+        lib = "cuDNN via torch.nn.functional.conv2d, channels-last bf16 in, bf16 out"
+        fn = lambda i: torch.nn.functional.conv2d(sets[i % n_sets][0], sets[i % n_sets][1], padding=1)  # noqa: E731
+    for i in range(args.warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    g_begin = torch.cuda.Event(enable_timing=True, external=True)
+    g_end = torch.cuda.Event(enable_timing=True, external=True)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        cap = torch.cuda.current_stream(dev)
+        g_begin.record(cap)
+        for i in range(args.steps):
+            fn(i)
+        g_end.record(cap)
+    graph.replay()
+    torch.cuda.synchronize()
+    graph.replay()
+    torch.cuda.synchronize()
+    ms = g_begin.elapsed_time(g_end) / args.steps
+    work = plan["flops"] if w["unit"] == "TFLOP/s" else plan["bytes"]
+    scale = 1e12 if w["unit"] == "TFLOP/s" else 1e9
+    print(json.dumps({"metric": METRIC, "impl": "torch", "library": lib, "value": round(work / (ms * 1e-3) / scale, 3),
+                      "unit": w["unit"], "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": round(ms, 4), "higher_is_better": True,
+                      "config": {**w["config"], "l2": f"{n_sets} rotating input/output sets"}}), flush=True)
 
 
 def run_reference(args, world: int, rank: int, torch) -> None:
