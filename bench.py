@@ -62,6 +62,7 @@ NCU_TRAFFIC_BYTES: dict[str, float] = {
     "conv2d": 12_956_416 + 256,
     "add": 33_561_088 + 10_496,
     "softmax": 33_567_488 + 498_432,
+    "sharded_matmul": 8_320_000_000 + 1_060_000_000,
 }
 
 
