@@ -453,6 +453,15 @@ __global__ void __launch_bounds__(kWinThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 32 && blockIdx.x < p.num_tiles) {
+    // Start this CTA's first window on its way from HBM into L2 while the
+    // previous launch on the stream drains (programmatic dependent launch):
+    // the window's TMA loads, issued after griddepcontrol.wait, then hit L2.
+    int n, w0, f0;
+    win_tile(p, blockIdx.x, n, w0, f0);
+    for (int c = 0; c < p.kc; ++c)
+      tma_prefetch_l2_4d(&tma_in, c * T::kCh, w0 - p.pad_l, f0 / p.Wp - p.pad_t, p.n_begin + n);
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&full[s], 1);

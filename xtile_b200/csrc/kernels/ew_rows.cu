@@ -74,10 +74,17 @@ __global__ void __launch_bounds__(kThreads) ew_binary_f32(const float* __restric
   // array (the loop only runs again past the grid-size limit): every load is
   // issued at kernel start, which measured faster on this HBM-bound op than
   // a persistent grid-stride loop with two vectors in flight per thread.
-  griddep_launch_dependents();
-  griddep_wait();
   const float4* a4 = reinterpret_cast<const float4*>(a);
   const float4* b4 = reinterpret_cast<const float4*>(b);
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * kThreads;
+  if (threadIdx.x == 0 && first < n4) {
+    // this CTA's first vectors of both operands into L2 while the previous launch drains
+    const uint32_t bytes = static_cast<uint32_t>((n4 - first < kThreads ? n4 - first : kThreads) * 16);
+    prefetch_l2(a4 + first, bytes);
+    prefetch_l2(b4 + first, bytes);
+  }
+  griddep_launch_dependents();
+  griddep_wait();
   float4* c4 = reinterpret_cast<float4*>(c);
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n4; i += stride) {
@@ -159,6 +166,8 @@ __global__ void __launch_bounds__(kThreads) softmax_rows_vec4(const float* __res
                                                                int64_t row_end, int64_t cols) {
   const int lane = threadIdx.x & 31;
   const int64_t row = row_begin + static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5);
+  if (lane == 0 && row < row_end && (cols & 3) == 0)
+    prefetch_l2(x + row * cols, static_cast<uint32_t>(cols * 4));  // this warp's row into L2 (see pdl.cuh)
   griddep_launch_dependents();
   if (row >= row_end) return;
   griddep_wait();

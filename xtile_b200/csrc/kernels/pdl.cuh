@@ -13,6 +13,7 @@
 
 #include <cuda_runtime.h>
 
+#include <cstdint>
 #include <utility>
 
 namespace xt {
@@ -26,6 +27,14 @@ __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wa
 // grid is still waiting for an SM.
 __device__ __forceinline__ void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Fetches [p, p + bytes) into L2 (16-byte aligned address, size a multiple of
+// 16).  L2 is the point of coherence, so this may run before griddep_wait():
+// a later load still sees every store the previous grid makes to those lines.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)), "r"(bytes)
+               : "memory");
 }
 
 // Launch attributes: programmatic serialization, plus an optional cluster.

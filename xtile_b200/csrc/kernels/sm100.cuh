@@ -155,6 +155,17 @@ __device__ __forceinline__ void tma_prefetch(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// Fetches a 4D box into L2 only (no shared memory, no barrier).  L2 is the
+// point of coherence, so this may run before griddepcontrol.wait: a later
+// load sees any store the previous grid makes to the same lines.
+__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap* map, int32_t c0, int32_t c1, int32_t c2,
+                                                   int32_t c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t x,
                                             int32_t y) {
   asm volatile(
