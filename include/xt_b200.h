@@ -45,8 +45,10 @@ enum {
   XT_EDEVICE = 8       /* a kernel reported an error word (bounded wait ran out) */
 };
 
-/* Kernel families a Block program maps onto. */
-enum { XT_FAMILY_EW = 1, XT_FAMILY_ROWS = 2, XT_FAMILY_GEMM = 3, XT_FAMILY_CONV = 4 };
+/* Kernel families a Block program maps onto.  XT_FAMILY_TILE runs any other
+ * Block program (reshape / transpose / permute, reductions along any axis,
+ * broadcasting binaries, tensor constants) one CTA per Block in shared memory. */
+enum { XT_FAMILY_EW = 1, XT_FAMILY_ROWS = 2, XT_FAMILY_GEMM = 3, XT_FAMILY_CONV = 4, XT_FAMILY_TILE = 5 };
 
 typedef struct xt_plan_info {
   int family;           /* XT_FAMILY_* */

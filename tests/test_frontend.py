@@ -222,9 +222,20 @@ def test_unsupported_programs_explain_why():
     m = xt.convert(case[1], args=case[2], grid=case[3], double_buffering=case[4])
     with pytest.raises(RuntimeError, match="bf16 or i8 operands"):
         m.plan()
+    # a column reduction is no elementwise map or row program: the tile family takes it
     case = {c[0]: c for c in build_cases(dsl)}["column_reduce"]
     m = xt.convert(case[1], args=case[2], grid=case[3], double_buffering=case[4])
-    with pytest.raises(RuntimeError, match="no B200 kernel family"):
+    assert m.plan()["family"] == "tile"
+
+    # every Block of a (4, 1, 1) grid storing the same tile: no family can run it
+    # without the result depending on Block order
+    @xt.kernel
+    def same_tile(x, y):
+        t = xt.load(x, index=(xt.bid(0), 0), shape=(8, 8))
+        xt.store(y, index=(0, 0), tile=xt.sum(t, axis=0))
+
+    m = xt.convert(same_tile, args=(xt.Array((32, 8), xt.float32), xt.Array((1, 8), xt.float32)), grid=(4, 1, 1))
+    with pytest.raises(RuntimeError, match="no B200 kernel family.*would store the same tile"):
         m.plan()
 
 

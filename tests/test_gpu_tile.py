@@ -1,0 +1,176 @@
+"""GPU parity of the tile family against the CPU oracle, through the public API.
+
+Tolerances: bit-exact for everything but f32 sums (f64 accumulation in both,
+in different orders, then one rounding to f32: |gpu - ref| <= 1e-6 |ref| + 1e-6).
+"""
+import numpy as np
+import pytest
+import torch
+
+import xtile as xt
+from oracle import xt_oracle
+from tests.test_tile import col_sums, transpose3
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0") if torch.cuda.is_available() else None
+A = xt.Array
+f32 = xt.float32
+
+
+def gen(seed):
+    return torch.Generator().manual_seed(seed)
+
+
+def host(t):
+    return t.detach().cpu().numpy()
+
+
+def oracle(module, arrays):
+    outs = [np.array(host(a)) for a in arrays]
+    xt_oracle.run(xt._module_asm(module), outs)
+    return outs
+
+
+@pytest.fixture(autouse=True)
+def no_device_errors():
+    yield
+    assert xt.device_error() == 0
+
+
+def test_transpose_rank3_ragged_bit_exact():
+    x = torch.randn(2, 96, 200, generator=gen(1))
+    y = torch.full((2, 200, 96), float("nan"), device=DEV)
+    m = xt.run(transpose3, args=(x.to(DEV), y, 32, 64), grid=(2, 3, 4))
+    assert m.plan()["family"] == "tile"
+    ref = oracle(m, [x, torch.zeros(2, 200, 96)])[1]
+    assert np.array_equal(host(y), ref)
+    assert np.array_equal(ref, np.swapaxes(host(x), 1, 2))
+
+
+def test_transpose_bid0_shards_match_full_launch():
+    x = torch.randn(4, 64, 64, generator=gen(2)).to(DEV)
+    full = torch.empty(4, 64, 64, device=DEV)
+    parts = torch.full((4, 64, 64), float("nan"), device=DEV)
+    m = xt.run(transpose3, args=(x, full, 32, 32), grid=(4, 2, 2))
+    for lo, hi in [(0, 1), (1, 3), (3, 4)]:
+        xt.launch(m, x, parts, bid0_range=(lo, hi))
+    assert torch.equal(full, parts)
+
+
+@xt.kernel
+def reshape_tiles(x, y, tm, tn):
+    i, j = xt.bid(0), xt.bid(1)
+    t = xt.load(x, index=(i, j), shape=(tm, tn))
+    xt.store(y, index=(i, j), tile=xt.reshape(t, shape=(tn, tm)))
+
+
+def test_reshape_bit_exact():
+    x = torch.randn(64, 128, generator=gen(3))
+    y = torch.empty(128, 64, device=DEV)
+    m = xt.run(reshape_tiles, args=(x.to(DEV), y, 16, 32), grid=(4, 4, 1))
+    assert m.plan()["family"] == "tile"
+    ref = oracle(m, [x, torch.zeros(128, 64)])[1]
+    assert np.array_equal(host(y), ref)
+
+
+@xt.kernel
+def col_stats(x, s, mx, tm, tn):
+    i, j = xt.bid(0), xt.bid(1)
+    t = xt.load(x, index=(i, j), shape=(tm, tn))
+    xt.store(s, index=(i, j), tile=xt.sum(t, axis=0))
+    xt.store(mx, index=(i, j), tile=xt.max(t, axis=0))
+
+
+def test_axis0_reductions():
+    x = torch.randn(256, 96, generator=gen(4)) * 3
+    s = torch.empty(4, 96, device=DEV)
+    mx = torch.empty(4, 96, device=DEV)
+    m = xt.run(col_stats, args=(x.to(DEV), s, mx, 64, 32), grid=(4, 3, 1))
+    assert m.plan()["family"] == "tile"
+    _, ref_s, ref_m = oracle(m, [x, torch.zeros(4, 96), torch.zeros(4, 96)])
+    assert np.array_equal(host(mx), ref_m)
+    got = host(s)
+    assert np.all(np.abs(got - ref_s) <= 1e-6 * np.abs(ref_s) + 1e-6)
+
+
+def test_axis0_sums_ragged_tiles():
+    # 100 rows in tiles of 64: the second tile's rows past the edge load zero
+    x = torch.randn(100, 40, generator=gen(5))
+    y = torch.empty(2, 40, device=DEV)
+    m = xt.run(col_sums, args=(x.to(DEV), y, 64, 40), grid=(2, 1, 1))
+    ref = oracle(m, [x, torch.zeros(2, 40)])[1]
+    got = host(y)
+    assert np.all(np.abs(got - ref) <= 1e-6 * np.abs(ref) + 1e-6)
+
+
+@xt.kernel
+def row_vector_ops(x, v, y, tm, tn):
+    i = xt.bid(0)
+    t = xt.load(x, index=(i, 0), shape=(tm, tn))
+    r = xt.load(v, index=(0, 0), shape=(1, tn), shared=1)
+    xt.store(y, index=(i, 0), tile=xt.sigmoid(t * r - r))
+
+
+def test_row_vector_broadcast_bit_exact():
+    x = torch.randn(128, 64, generator=gen(6))
+    v = torch.randn(1, 64, generator=gen(7))
+    y = torch.empty(128, 64, device=DEV)
+    m = xt.run(row_vector_ops, args=(x.to(DEV), v.to(DEV), y, 32, 64), grid=(4, 1, 1))
+    assert m.plan()["family"] == "tile"
+    ref = oracle(m, [x, v, torch.zeros(128, 64)])[2]
+    # sigmoid: CUDA expf against numpy's f64 exp, within a few ulp
+    np.testing.assert_allclose(host(y), ref, rtol=1e-6, atol=1e-7)
+
+
+def _text_case(body_op: str, out_shape: str, result_tensor: str):
+    return f"""func.func @p(%x: memref<4x3x5xf32>, %y: memref<{out_shape}xf32>) attributes {{xt.grid = array<i32: 2, 1, 1>}} {{
+  %bid:3 = xt.get_tile_block_id : i32, i32, i32
+  %zero = arith.constant 0 : i32
+  %t = xt.load(%x, %bid#0, %zero, %zero) : (memref<4x3x5xf32>, i32, i32, i32) -> tensor<2x3x5xf32>
+  {body_op}
+  xt.store(%u, %y, %bid#0, %zero, %zero) : ({result_tensor}, memref<{out_shape}xf32>, i32, i32, i32) -> ()
+  func.return
+}}"""
+
+
+def test_permute_bit_exact():
+    text = _text_case("%u = xt.permute(%t) {permutation = [2, 0, 1]} : tensor<2x3x5xf32> -> tensor<5x2x3xf32>",
+                      "10x2x3", "tensor<5x2x3xf32>")
+    m = xt.parse(text)
+    assert m.plan()["family"] == "tile"
+    x = torch.randn(4, 3, 5, generator=gen(8))
+    y = torch.empty(10, 2, 3, device=DEV)
+    xt.launch(m, x.to(DEV), y)
+    ref = oracle(m, [x, torch.zeros(10, 2, 3)])[1]
+    assert np.array_equal(host(y), ref)
+
+
+def test_splat_constant_bit_exact():
+    text = _text_case("%c = arith.constant dense<1.250000e-01> : tensor<2x3x5xf32>\n"
+                      "  %u = xt.mul(%t, %c) : tensor<2x3x5xf32>, tensor<2x3x5xf32> -> tensor<2x3x5xf32>",
+                      "4x3x5", "tensor<2x3x5xf32>")
+    m = xt.parse(text)
+    assert m.plan()["family"] == "tile"
+    x = torch.randn(4, 3, 5, generator=gen(9))
+    y = torch.empty(4, 3, 5, device=DEV)
+    xt.launch(m, x.to(DEV), y)
+    ref = oracle(m, [x, torch.zeros(4, 3, 5)])[1]
+    assert np.array_equal(host(y), ref)
+
+
+@xt.kernel
+def i8_wrap(a, b, y, tm, tn):
+    i, j = xt.bid(0), xt.bid(1)
+    s = xt.load(a, index=(i, j), shape=(tm, tn)) + xt.load(b, index=(0, j), shape=(1, tn))
+    xt.store(y, index=(i, j), tile=s * s)
+
+
+def test_int8_arithmetic_wraps_bit_exact():
+    g = gen(10)
+    a = torch.randint(-128, 128, (64, 64), generator=g, dtype=torch.int8)
+    b = torch.randint(-128, 128, (1, 64), generator=g, dtype=torch.int8)
+    y = torch.zeros(64, 64, dtype=torch.int8, device=DEV)
+    m = xt.run(i8_wrap, args=(a.to(DEV), b.to(DEV), y, 16, 32), grid=(4, 2, 1))
+    assert m.plan()["family"] == "tile"
+    ref = oracle(m, [a, b, torch.zeros(64, 64, dtype=torch.int8)])[2]
+    assert np.array_equal(host(y), ref)

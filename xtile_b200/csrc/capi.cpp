@@ -252,6 +252,25 @@ int launch_plan(const xt::Plan& p, void* const* args, int64_t b0, int64_t b1, cu
       err = dev::launch_conv(a, stream);
       return err == cudaSuccess ? XT_OK : cuda_fail(err, "conv kernel launch");
     }
+    case Family::Tile: {
+      const TilePlan& t = p.tile;
+      dev::TileArgs a{};
+      for (int i = 0; i < t.n_args; ++i) {
+        a.arr[i] = args[t.arg[i]];
+        a.elem[i] = elem_code(t.arg_elem[i]);
+        for (int d = 0; d < kTileRank; ++d) a.shape[i][d] = t.arg_shape[i][d];
+      }
+      for (size_t i = 0; i < t.vals.size(); ++i) a.vals[i] = t.vals[i];
+      for (size_t i = 0; i < t.ops.size(); ++i) a.ops[i] = t.ops[i];
+      a.n_ops = static_cast<int>(t.ops.size());
+      a.smem_floats = t.smem_floats;
+      for (int k = 0; k < 3; ++k) a.grid[k] = p.grid[k];
+      a.bid0_begin = clamp64(b0, 0, g0);
+      a.bid0_end = clamp64(b1, 0, g0);
+      if (a.bid0_end <= a.bid0_begin) return XT_OK;
+      cudaError_t err = dev::launch_tile(a, stream);
+      return err == cudaSuccess ? XT_OK : cuda_fail(err, "tile kernel launch");
+    }
   }
   return fail(XT_EUNSUPPORTED, "unknown kernel family");
 }
@@ -430,6 +449,18 @@ int xt_plan(const xt_module* module, const char* func, xt_plan_info* out) {
         out->flops = 2.0 * out->m * out->n * out->k;
         const double eb = xt::elem_bytes(c.elem);
         out->bytes = eb * (double(c.N) * c.H * c.W * c.C + double(c.KH) * c.KW * c.C * c.KO) + 4.0 * out->m * c.OC;
+        break;
+      }
+      case xt::Family::Tile: {
+        // every Block's loaded and stored tiles, as the program addresses them
+        const xt::TilePlan& t = p->tile;
+        double per_block = 0;
+        for (const xt::TileOp& op : t.ops) {
+          if (op.kind != xt::kTLoad && op.kind != xt::kTStore) continue;
+          const xt::TileVal& v = t.vals[op.kind == xt::kTLoad ? op.dst : op.a];
+          per_block += xt::elem_bytes(t.arg_elem[op.arg]) * static_cast<double>(v.numel);
+        }
+        out->bytes = per_block * static_cast<double>(p->grid[0] * p->grid[1] * p->grid[2]);
         break;
       }
     }

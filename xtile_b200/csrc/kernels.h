@@ -40,6 +40,20 @@ struct RowArgs {
 };
 cudaError_t launch_rows(const RowArgs& a, cudaStream_t stream);
 
+// ---------------------------------------------------------------- tile
+struct TileArgs {
+  void* arr[kTileMaxArgs];
+  uint8_t elem[kTileMaxArgs];
+  int32_t shape[kTileMaxArgs][kTileRank];
+  TileVal vals[kTileMaxVals];
+  TileOp ops[kTileMaxOps];
+  int n_ops;
+  int32_t smem_floats;
+  int64_t grid[3];
+  int64_t bid0_begin, bid0_end;  // Blocks [bid0_begin, bid0_end) along xt.bid(0)
+};
+cudaError_t launch_tile(const TileArgs& a, cudaStream_t stream);
+
 // ---------------------------------------------------------------- gemm
 struct GemmArgs {
   const void* A;           // [M, lda] row-major (bf16 or i8)

@@ -23,6 +23,7 @@ const char* family_name(Family f) {
     case Family::Rows: return "rows";
     case Family::Gemm: return "gemm";
     case Family::Conv: return "conv";
+    case Family::Tile: return "tile";
   }
   return "?";
 }
@@ -129,8 +130,16 @@ class Classifier {
       } catch (const Error& e) {
         rows_why = e.what();
       }
+      std::string tile_why;
+      try {
+        p.tile = plan_tile();
+        p.family = Family::Tile;
+        return p;
+      } catch (const Error& e) {
+        tile_why = e.what();
+      }
       throw Error(kUnsupported, "no B200 kernel family matches @" + f_.name + ": as an elementwise map: " +
-                                    ew_why + "; as a row program: " + rows_why);
+                                    ew_why + "; as a row program: " + rows_why + "; as a tile program: " + tile_why);
     }
     return p;
   }
@@ -197,6 +206,197 @@ class Classifier {
   std::pair<int64_t, int64_t> covered(const Coord& c, int64_t tile, int64_t dim) const {
     if (c.bid) return {0, std::min(grid_[c.dim] * tile, dim)};
     return {std::min(c.value * tile, dim), std::min((c.value + 1) * tile, dim)};
+  }
+
+  // ------------------------------------------------------------------ tile
+  // Any Block program of loads, stores, elementwise ops with broadcasting,
+  // reductions, reshape / transpose / permute and tensor constants.  Values
+  // live in shared memory as f32 (int8 values are exact there and wrap on
+  // add/sub/mul like the reference's int8 arithmetic).
+  TilePlan plan_tile() {
+    TilePlan p;
+    std::map<int, int> val_of;  // SSA value id -> tile value index
+    auto padded = [&](const std::vector<int64_t>& shape, int32_t (&out)[kTileRank]) {
+      if (shape.size() > static_cast<size_t>(kTileRank)) unsupported("tile programs use rank <= 4 tiles");
+      const int lead = kTileRank - static_cast<int>(shape.size());
+      for (int d = 0; d < kTileRank; ++d) {
+        const int64_t v = d < lead ? 1 : shape[d - lead];
+        if (v <= 0 || v > (int64_t{1} << 30)) unsupported("tile and array dims must be in [1, 2^30]");
+        out[d] = static_cast<int32_t>(v);
+      }
+      return lead;
+    };
+    auto new_val = [&](int vid, const Type& t) -> uint8_t {
+      if (p.vals.size() == static_cast<size_t>(kTileMaxVals)) unsupported("the program has more than 16 tiles");
+      if (t.elem != Elem::F32 && t.elem != Elem::I8 && t.elem != Elem::BF16) unsupported("unsupported element type");
+      TileVal v{};
+      padded(t.shape, v.shape);
+      // rows padded to an odd length, so column walks (transpose, axis-0
+      // reductions) touch distinct shared-memory banks
+      const int64_t inner = v.shape[3] % 2 == 0 ? v.shape[3] + 1 : v.shape[3];
+      const int64_t s2 = inner, s1 = s2 * v.shape[2], s0 = s1 * v.shape[1];
+      const int64_t floats = s0 * v.shape[0];
+      const int64_t offset = (static_cast<int64_t>(p.smem_floats) + 3) & ~int64_t{3};
+      if (offset + floats > kTileSmemFloats) unsupported("the program's tiles exceed 192 KiB of shared memory");
+      v.stride[3] = 1;
+      v.stride[2] = static_cast<int32_t>(s2);
+      v.stride[1] = static_cast<int32_t>(s1);
+      v.stride[0] = static_cast<int32_t>(s0);
+      v.numel = v.shape[0] * v.shape[1] * v.shape[2] * v.shape[3];
+      v.offset = static_cast<int32_t>(offset);
+      v.i8 = t.elem == Elem::I8;
+      p.smem_floats = static_cast<int32_t>(offset + floats);
+      val_of[vid] = static_cast<int>(p.vals.size());
+      p.vals.push_back(v);
+      return static_cast<uint8_t>(p.vals.size() - 1);
+    };
+    auto val = [&](int vid) -> uint8_t {
+      auto it = val_of.find(vid);
+      if (it == val_of.end()) unsupported("a tile operand is not a tile value of the program");
+      return static_cast<uint8_t>(it->second);
+    };
+    auto slot_of = [&](const Access& a) -> uint8_t {
+      for (int i = 0; i < p.n_args; ++i)
+        if (p.arg[i] == a.arg) return static_cast<uint8_t>(i);
+      if (p.n_args == kTileMaxArgs) unsupported("the program addresses more than 8 arrays");
+      if (a.array.elem != Elem::F32 && a.array.elem != Elem::I8 && a.array.elem != Elem::BF16)
+        unsupported("unsupported array element type");
+      const int i = p.n_args++;
+      p.arg[i] = a.arg;
+      p.arg_elem[i] = a.array.elem;
+      padded(a.array.shape, p.arg_shape[i]);
+      return static_cast<uint8_t>(i);
+    };
+    auto set_coords = [&](TileOp& t, const Access& a) {
+      if (a.idx.size() != a.array.shape.size() || a.tile.size() != a.array.shape.size())
+        unsupported("a tile's rank must match its array's rank");
+      const int lead = kTileRank - static_cast<int>(a.idx.size());
+      for (int d = 0; d < kTileRank; ++d) {
+        t.coord_bid[d] = -1;
+        t.coord[d] = 0;
+        if (d < lead) continue;
+        const Coord& c = a.idx[d - lead];
+        if (c.bid) {
+          t.coord_bid[d] = static_cast<int8_t>(c.dim);
+        } else {
+          if (c.value < 0 || c.value > (int64_t{1} << 30)) unsupported("tile coordinates must be in [0, 2^30]");
+          t.coord[d] = static_cast<int32_t>(c.value);
+        }
+      }
+    };
+    std::map<int, const Access*> store_at;
+    for (const Access& a : stores_) store_at[a.op] = &a;
+    static const std::map<std::string, uint8_t> kUn = {
+        {"xt.exp", kExp}, {"xt.cos", kCos}, {"xt.sin", kSin}, {"xt.reciprocal", kRecip}, {"xt.rsqrt", kRsqrt},
+        {"xt.sigmoid", kSigmoid}, {"xt.tanh", kTanh}, {"xt.silu", kSilu}};
+    static const std::map<std::string, uint8_t> kBin = {{"xt.add", kAdd}, {"xt.sub", kSub}, {"xt.mul", kMul}};
+    for (size_t i = 0; i < f_.ops.size(); ++i) {
+      const Op& op = f_.ops[i];
+      const std::string& n = op.name;
+      if (n == "xt.get_tile_block_id" || n == "func.return" || n == "return") continue;
+      TileOp t{};
+      if (n == "arith.constant") {
+        if (op.result_types[0].kind != Type::Tensor) continue;  // a scalar tile coordinate
+        if (!op.is_dense) unsupported("tensor constants must be dense splats");
+        t.kind = kTConst;
+        t.value = static_cast<float>(op.fvalue);
+        t.dst = new_val(op.results[0], op.result_types[0]);
+      } else if (n == "xt.load") {
+        const Access& a = loads_.at(op.results[0]);
+        t.kind = kTLoad;
+        t.arg = slot_of(a);
+        set_coords(t, a);
+        t.dst = new_val(op.results[0], op.result_types[0]);
+      } else if (n == "xt.store") {
+        const Access& a = *store_at.at(static_cast<int>(i));
+        t.kind = kTStore;
+        t.a = val(op.operands[0]);
+        t.arg = slot_of(a);
+        set_coords(t, a);
+      } else if (kUn.count(n) || n == "xt.itof" || n == "xt.ftoi") {
+        if (op.operand_types[0].shape != op.result_types[0].shape) unsupported("'" + n + "' changes the tile shape");
+        if (n == "xt.itof" && op.operand_types[0].elem != Elem::I8) unsupported("itof expects i8");
+        if (n == "xt.ftoi" && op.result_types[0].elem != Elem::I8) unsupported("ftoi produces i8");
+        if (kUn.count(n) && op.operand_types[0].elem != Elem::F32) unsupported("'" + n + "' expects an f32 tile");
+        t.kind = kTUnary;
+        t.code = n == "xt.itof" ? kItof : n == "xt.ftoi" ? kFtoi : kUn.at(n);
+        t.a = val(op.operands[0]);
+        t.dst = new_val(op.results[0], op.result_types[0]);
+      } else if (kBin.count(n)) {
+        t.kind = kTBinary;
+        t.code = kBin.at(n);
+        t.a = val(op.operands[0]);
+        t.b = val(op.operands[1]);
+        t.dst = new_val(op.results[0], op.result_types[0]);
+        const TileVal &va = p.vals[t.a], &vb = p.vals[t.b], &vd = p.vals[t.dst];
+        for (int d = 0; d < kTileRank; ++d)
+          if ((va.shape[d] != vd.shape[d] && va.shape[d] != 1) || (vb.shape[d] != vd.shape[d] && vb.shape[d] != 1))
+            unsupported("'" + n + "' operands do not broadcast to its result");
+      } else if (n == "xt.reduce_max" || n == "xt.reduce_sum") {
+        if (op.operand_types[0].elem != Elem::F32) unsupported("reductions are supported on f32 tiles");
+        const Attr* ax = find_attr(op.attrs, "axis");
+        const int rank = static_cast<int>(op.operand_types[0].shape.size());
+        const int64_t axis = ax ? ax->i : rank - 1;
+        if (axis < 0 || axis >= rank) unsupported("reduction axis out of range");
+        t.kind = kTReduce;
+        t.code = n == "xt.reduce_sum" ? 1 : 0;
+        t.axis = static_cast<uint8_t>(kTileRank - rank + axis);
+        t.a = val(op.operands[0]);
+        t.dst = new_val(op.results[0], op.result_types[0]);
+        for (int d = 0; d < kTileRank; ++d)
+          if (p.vals[t.dst].shape[d] != (d == t.axis ? 1 : p.vals[t.a].shape[d]))
+            unsupported("a reduction keeps every dim but the reduced one, which becomes 1");
+      } else if (n == "xt.reshape") {
+        t.kind = kTReshape;
+        t.a = val(op.operands[0]);
+        t.dst = new_val(op.results[0], op.result_types[0]);
+        if (p.vals[t.a].numel != p.vals[t.dst].numel) unsupported("reshape must keep the element count");
+      } else if (n == "xt.transpose" || n == "xt.permute") {
+        const int rank = static_cast<int>(op.operand_types[0].shape.size());
+        std::vector<int64_t> perm;
+        if (n == "xt.transpose") {
+          if (rank != 3) unsupported("transpose takes rank-3 tiles");
+          perm = {0, 2, 1};
+        } else {
+          const Attr* pa = find_attr(op.attrs, "permutation");
+          if (!pa) unsupported("permute needs a permutation");
+          perm = pa->arr;
+        }
+        if (static_cast<int>(perm.size()) != rank) unsupported("the permutation must list every dim");
+        std::vector<int64_t> sorted = perm;
+        std::sort(sorted.begin(), sorted.end());
+        for (int d = 0; d < rank; ++d)
+          if (sorted[d] != d) unsupported("the permutation must use every dim once");
+        t.kind = kTPermute;
+        const int lead = kTileRank - rank;
+        for (int d = 0; d < kTileRank; ++d)
+          t.perm[d] = static_cast<uint8_t>(d < lead ? d : lead + perm[d - lead]);
+        t.a = val(op.operands[0]);
+        t.dst = new_val(op.results[0], op.result_types[0]);
+        for (int d = 0; d < kTileRank; ++d)
+          if (p.vals[t.dst].shape[d] != p.vals[t.a].shape[t.perm[d]])
+            unsupported("the result shape must be the operand shape permuted");
+      } else {
+        unsupported("'" + n + "' is not supported in tile programs");
+      }
+      if (p.ops.size() == static_cast<size_t>(kTileMaxOps)) unsupported("the program has more than 32 tile ops");
+      p.ops.push_back(t);
+    }
+    // Every Block stores tiles of its own: Blocks differing along any grid
+    // axis must store to different tiles, or the result would depend on the
+    // order in which Blocks run.
+    for (const Access& a : stores_) {
+      std::set<int> used;
+      for (const Coord& c : a.idx)
+        if (c.bid) {
+          if (used.count(c.dim)) unsupported("a block axis may index only one dim of a stored tile");
+          used.insert(c.dim);
+        }
+      for (int k = 0; k < static_cast<int>(grid_.size()); ++k)
+        if (grid_[k] > 1 && !used.count(k))
+          unsupported("Blocks along grid axis " + std::to_string(k) + " would store the same tile");
+    }
+    return p;
   }
 
   // ------------------------------------------------------------------ ew
@@ -723,6 +923,11 @@ std::string describe_plan(const Plan& p, int stage) {
         os << "  //   xt_to_nova -> conv: implicit GEMM M " << p.conv.ON * p.conv.OH * p.conv.OW << " N "
            << p.conv.OC << " K " << p.conv.KH * p.conv.KW * p.conv.C << ", pad [" << p.conv.pad_t << ", "
            << p.conv.pad_l << "]\n";
+        break;
+      case Family::Tile:
+        os << "  //   xt_to_nova -> tile: one CTA per Block, " << p.tile.vals.size() << " tiles in "
+           << (p.tile.smem_floats * 4 + 1023) / 1024 << " KiB of shared memory, " << p.tile.ops.size()
+           << " tile ops\n";
         break;
     }
   }

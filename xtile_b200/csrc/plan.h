@@ -12,6 +12,10 @@
 //          row or scalar scale and bias and an optional int8 cast
 //          (tcgen05 + TMEM + TMA)
 //   conv   load_conv2d as an implicit GEMM (tcgen05 + TMEM + TMA)
+//   tile   any other Block program (reshape / transpose / permute,
+//          reductions along any axis, broadcasting binaries, tensor
+//          constants): one CTA per Block interprets the tile ops on f32 tiles
+//          held in shared memory
 #pragma once
 
 #include <cstdint>
@@ -22,7 +26,7 @@
 
 namespace xt {
 
-enum class Family { Ew = 1, Rows = 2, Gemm = 3, Conv = 4 };
+enum class Family { Ew = 1, Rows = 2, Gemm = 3, Conv = 4, Tile = 5 };
 
 // --- elementwise --------------------------------------------------------------
 // Register programs shared by the ew and rows kernels.  ``dst``/``a``/``b``
@@ -98,6 +102,47 @@ struct ConvPlan {
   int n_axis = 0;                            // bid axis of the batch tile
 };
 
+// --- tile -----------------------------------------------------------------------
+// Shapes are padded with leading 1s to rank 4 (tile and array rank agree).
+enum TileOpKind : uint8_t {
+  kTLoad = 1, kTStore, kTConst, kTUnary, kTBinary, kTReduce, kTReshape, kTPermute,
+};
+constexpr int kTileRank = 4;
+constexpr int kTileMaxVals = 16;
+constexpr int kTileMaxOps = 32;
+constexpr int kTileMaxArgs = 8;
+constexpr int kTileSmemFloats = 48 * 1024;  // 192 KiB of shared memory per Block
+
+struct TileVal {               // one tile value, f32 elements in shared memory
+  int32_t shape[kTileRank];
+  int32_t stride[kTileRank];   // shared-memory strides in floats (rows padded to an odd length)
+  int32_t offset;              // first float
+  int32_t numel;
+  uint8_t i8;                  // int8 value: add/sub/mul results wrap modulo 256
+};
+
+struct TileOp {
+  uint8_t kind;                // TileOpKind
+  uint8_t code;                // unary / binary: Opcode (kExp.., kAdd.., kItof, kFtoi); reduce: 0 max, 1 sum
+  uint8_t dst, a, b;           // value indices (store: ``a`` is the stored value)
+  uint8_t arg;                 // load / store: argument slot
+  uint8_t axis;                // reduce: the reduced dim
+  uint8_t perm[kTileRank];     // permute: dst dim d is src dim perm[d]
+  int8_t coord_bid[kTileRank]; // load / store tile coordinate per dim: bid axis, or -1 for ``coord``
+  int32_t coord[kTileRank];
+  float value;                 // constant splat
+};
+
+struct TilePlan {
+  int n_args = 0;
+  int arg[kTileMaxArgs];                 // function argument of each slot
+  Elem arg_elem[kTileMaxArgs];
+  int32_t arg_shape[kTileMaxArgs][kTileRank];
+  std::vector<TileVal> vals;
+  std::vector<TileOp> ops;
+  int32_t smem_floats = 0;
+};
+
 struct Plan {
   Family family = Family::Ew;
   std::string func;
@@ -109,6 +154,7 @@ struct Plan {
   RowPlan rows;
   GemmPlan gemm;
   ConvPlan conv;
+  TilePlan tile;
 };
 
 // Classifies ``f`` (throws Error(kUnsupported) with the reason otherwise).

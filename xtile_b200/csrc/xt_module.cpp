@@ -87,7 +87,7 @@ py::dict plan(py::object module, py::object func) {
   xt_plan_info info;
   int st = xt_plan(unwrap(module), fname, &info);
   if (st != XT_OK) raise_status(st, "plan");
-  static const char* kFamilies[] = {"", "ew", "rows", "gemm", "conv"};
+  static const char* kFamilies[] = {"", "ew", "rows", "gemm", "conv", "tile"};
   py::dict d;
   d["family"] = kFamilies[info.family];
   d["n_args"] = info.n_args;
