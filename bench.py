@@ -156,6 +156,21 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
                     unit="TFLOP/s", dtype="bf16",
                     config={"workload": "conv2d", "input": [32, 56, 56, 64], "filter": [3, 3, 64, 64],
                             "pad": 1, "block_tile": [1, 8, 56, 64], "grid": [32, 7, 1]})
+    if name == "transpose":
+        # not a BASELINE configuration: the tile family on an HBM-bound program
+        @xt.kernel
+        def transpose3(inp, out, tm, tn):
+            b, i, j = xt.bid(0), xt.bid(1), xt.bid(2)
+            t = xt.load(inp, index=(b, i, j), shape=(1, tm, tn))
+            xt.store(out, index=(b, j, i), tile=xt.transpose(t))
+
+        x = torch.randn(8, 2048, 2048, generator=g(5))
+        mod = xt.convert(transpose3, args=(A((8, 2048, 2048), xt.float32), A((8, 2048, 2048), xt.float32), 32, 64),
+                         grid=(8, 64, 32), double_buffering=True)
+        return dict(module=mod, inputs=[x], out_shape=(8, 2048, 2048), out_dtype=torch.float32,
+                    unit="GB/s", dtype="f32",
+                    config={"workload": "transpose", "shape": [8, 2048, 2048], "block_tile": [1, 32, 64],
+                            "grid": [8, 64, 32]})
     raise SystemExit(f"unknown workload {name}")
 
 
@@ -396,7 +411,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="sharded_matmul",
-                    choices=["add", "softmax", "matmul", "conv2d", "sharded_matmul"])
+                    choices=["add", "softmax", "matmul", "conv2d", "sharded_matmul", "transpose"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference", "torch"],
                     help="b200: this backend; reference: the reference's CPU path; torch: the vendor library "
                          "(cuBLAS, cuDNN) through PyTorch on one GPU, for context")
@@ -796,6 +811,9 @@ def run_torch_library(args, torch) -> None:
     elif name in ("matmul", "sharded_matmul"):
         lib = "cuBLAS via torch.mm(out_dtype=float32, out=)"
         fn = lambda i: torch.mm(*sets[i % n_sets], out_dtype=torch.float32, out=outs[i % n_sets])  # noqa: E731
+    elif name == "transpose":
+        lib = "torch copy_ of a transposed view"
+        fn = lambda i: outs[i % n_sets].copy_(sets[i % n_sets][0].transpose(1, 2))  # noqa: E731
     else:
         lib = "cuDNN via torch.nn.functional.conv2d, channels-last bf16 in, bf16 out"
         fn = lambda i: torch.nn.functional.conv2d(sets[i % n_sets][0], sets[i % n_sets][1], padding=1)  # noqa: E731

@@ -264,6 +264,7 @@ int launch_plan(const xt::Plan& p, void* const* args, int64_t b0, int64_t b1, cu
       for (size_t i = 0; i < t.ops.size(); ++i) a.ops[i] = t.ops[i];
       a.n_ops = static_cast<int>(t.ops.size());
       a.smem_floats = t.smem_floats;
+      a.rows = t.rows ? 1 : 0;
       for (int k = 0; k < 3; ++k) a.grid[k] = p.grid[k];
       a.bid0_begin = clamp64(b0, 0, g0);
       a.bid0_end = clamp64(b1, 0, g0);

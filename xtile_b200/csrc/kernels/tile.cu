@@ -41,92 +41,298 @@ __device__ __forceinline__ void unravel(int e, const int32_t (&s)[kTileRank], in
   i[0] = e / s[1];
 }
 
-__device__ __forceinline__ int slot(const TileVal& v, const int (&i)[kTileRank]) {
-  return v.offset + i[0] * v.stride[0] + i[1] * v.stride[1] + i[2] * v.stride[2] + i[3];
+// Walks the multi-indices of elements e = t, t + kTileThreads, ... of a
+// rank-4 shape: one unravel per thread, then a mixed-radix add of the stride's
+// digits with one carry per dim (no division per element).
+struct Walker {
+  int i[kTileRank];
+  int step[kTileRank];
+  int s[kTileRank];
+  __device__ __forceinline__ Walker(int t, const int (&shape)[kTileRank]) {
+    int32_t sh[kTileRank];
+#pragma unroll
+    for (int k = 0; k < kTileRank; ++k) s[k] = sh[k] = shape[k];
+    unravel(t, sh, i);
+    unravel(kTileThreads, sh, step);
+  }
+  __device__ __forceinline__ void next() {
+    int c = 0;
+#pragma unroll
+    for (int k = kTileRank - 1; k >= 0; --k) {
+      i[k] += step[k] + c;
+      c = i[k] >= s[k];
+      i[k] -= c ? s[k] : 0;
+    }
+  }
+};
+
+// A tile value's layout, copied once from the kernel parameters into registers.
+struct TV {
+  int shape[kTileRank], stride[kTileRank];
+  int offset, numel;
+  bool i8;
+  __device__ __forceinline__ explicit TV(const TileVal& v) {
+#pragma unroll
+    for (int k = 0; k < kTileRank; ++k) {
+      shape[k] = v.shape[k];
+      stride[k] = v.stride[k];
+    }
+    offset = v.offset;
+    numel = v.numel;
+    i8 = v.i8 != 0;
+  }
+  __device__ __forceinline__ int at(const int (&i)[kTileRank]) const {
+    return offset + i[0] * stride[0] + i[1] * stride[1] + i[2] * stride[2] + i[3];
+  }
+};
+
+// A tile whose two leading dims are 1 is R x C (R = shape[2], C = shape[3]).
+// When C divides the CTA width, each thread keeps one column and steps whole
+// rows: every offset then advances by a constant, with no index arithmetic.
+__device__ __forceinline__ bool rows_of(const TV& v) {
+  return v.shape[0] == 1 && v.shape[1] == 1 && kTileThreads % v.shape[3] == 0;
 }
 
 __device__ __forceinline__ float wrap_i8(float x) {
   return static_cast<float>(static_cast<int8_t>(static_cast<int>(x)));
 }
 
-__global__ void __launch_bounds__(kTileThreads) tile_program(const __grid_constant__ TileArgs p) {
+// Load or store of one tile: elements past the array edge load 0 / are skipped.
+template <bool LOAD, bool ROWS>
+__device__ __forceinline__ void move_tile(float* sm, const TileArgs& p, const TileOp& op, const TV& v,
+                                          const int64_t (&bid)[3]) {
+  int64_t astride[kTileRank];
+  int lim[kTileRank];
+  int64_t base = 0;
+  int64_t run = 1;
+#pragma unroll
+  for (int d = kTileRank - 1; d >= 0; --d) {
+    const int64_t ext = p.shape[op.arg][d];
+    const int cb = op.coord_bid[d];
+    const int64_t c = cb == 0 ? bid[0] : cb == 1 ? bid[1] : cb == 2 ? bid[2] : op.coord[d];
+    const int64_t start = c * static_cast<int64_t>(v.shape[d]);
+    astride[d] = run;
+    base += start * run;
+    run *= ext;
+    const int64_t left = ext - start;  // elements of this dim inside the array
+    lim[d] = left <= 0 ? 0 : (left > v.shape[d] ? v.shape[d] : static_cast<int>(left));
+  }
+  void* arr = p.arr[op.arg];
+  const uint8_t elem = p.elem[op.arg];
+  constexpr int kBatch = 8;
+  if ((ROWS || rows_of(v)) && elem == kF32 && v.shape[3] % 4 == 0 && lim[3] % 4 == 0 && base % 4 == 0 &&
+      astride[2] % 4 == 0 && (reinterpret_cast<uintptr_t>(arr) & 15) == 0) {
+    constexpr int kVecBatch = 4;  // float4s in flight per thread
+    // f32 rows of a multiple of 4 elements at 16-byte aligned global offsets:
+    // one float4 per thread per access (shared memory stays scalar: its rows
+    // are padded to an odd length)
+    const int C4 = v.shape[3] / 4, R = v.shape[2];
+    const int c = (threadIdx.x % C4) * 4, rs = kTileThreads / C4;
+    const bool col_in = c < lim[3] && lim[0] > 0 && lim[1] > 0;
+    const int r_lim = lim[2];
+    float4* g = reinterpret_cast<float4*>(arr);
+    for (int r = threadIdx.x / C4; r < R; r += kVecBatch * rs) {
+      if (LOAD) {
+        float4 val[kVecBatch];
+#pragma unroll
+        for (int u = 0; u < kVecBatch; ++u) {
+          const int ru = r + u * rs;
+          val[u] = (col_in && ru < r_lim) ? __ldg(g + (base + ru * astride[2] + c) / 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < kVecBatch; ++u) {
+          const int ru = r + u * rs;
+          if (ru < R) {
+            float* d = sm + v.offset + ru * v.stride[2] + c;
+            d[0] = val[u].x;
+            d[1] = val[u].y;
+            d[2] = val[u].z;
+            d[3] = val[u].w;
+          }
+        }
+      } else if (col_in) {
+#pragma unroll
+        for (int u = 0; u < kVecBatch; ++u) {
+          const int ru = r + u * rs;
+          if (ru < r_lim) {
+            const float* s4 = sm + v.offset + ru * v.stride[2] + c;
+            g[(base + ru * astride[2] + c) / 4] = make_float4(s4[0], s4[1], s4[2], s4[3]);
+          }
+        }
+      }
+    }
+    return;
+  }
+  if (ROWS || rows_of(v)) {
+    const int C = v.shape[3], R = v.shape[2];
+    const int c = threadIdx.x % C, rs = kTileThreads / C;
+    const bool col_in = c < lim[3] && lim[0] > 0 && lim[1] > 0;
+    const int r_lim = lim[2];
+    const int64_t gstep = rs * astride[2];
+    const int sstep = rs * v.stride[2];
+    int r = threadIdx.x / C;
+    int64_t goff = base + r * astride[2] + c;
+    int soff = v.offset + r * v.stride[2] + c;
+    if (LOAD) {
+      for (; r < R; r += kBatch * rs) {
+        float val[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          const int ru = r + u * rs;
+          val[u] = (col_in && ru < r_lim) ? load_elem(arr, elem, goff + u * gstep) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u)
+          if (r + u * rs < R) sm[soff + u * sstep] = val[u];
+        goff += kBatch * gstep;
+        soff += kBatch * sstep;
+      }
+    } else if (col_in) {
+      for (; r < r_lim; r += rs, goff += gstep, soff += sstep) store_elem(arr, elem, goff, sm[soff]);
+    }
+    return;
+  }
+  if constexpr (ROWS) return;
+  Walker w(threadIdx.x, v.shape);
+  if (LOAD) {
+    // kBatch independent loads in flight per thread before their shared-memory
+    // stores: one HBM round trip per kBatch elements, not per element
+    for (int e0 = threadIdx.x; e0 < v.numel; e0 += kBatch * kTileThreads) {
+      float val[kBatch];
+      int dst[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const bool live = e0 + u * kTileThreads < v.numel;
+        const bool in = live && w.i[0] < lim[0] && w.i[1] < lim[1] && w.i[2] < lim[2] && w.i[3] < lim[3];
+        const int64_t off = base + w.i[0] * astride[0] + w.i[1] * astride[1] + w.i[2] * astride[2] + w.i[3];
+        val[u] = in ? load_elem(arr, elem, off) : 0.0f;
+        dst[u] = live ? v.at(w.i) : -1;
+        w.next();
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u)
+        if (dst[u] >= 0) sm[dst[u]] = val[u];
+    }
+  } else {
+    for (int e = threadIdx.x; e < v.numel; e += kTileThreads, w.next()) {
+      const bool in = w.i[0] < lim[0] && w.i[1] < lim[1] && w.i[2] < lim[2] && w.i[3] < lim[3];
+      const int64_t off = base + w.i[0] * astride[0] + w.i[1] * astride[1] + w.i[2] * astride[2] + w.i[3];
+      if (in) store_elem(arr, elem, off, sm[v.at(w.i)]);
+    }
+  }
+}
+
+// ROWS: every tile of the program is R x C with C dividing the CTA width (the
+// planner checks), so only the row paths are compiled: fewer registers, more
+// CTAs per SM.
+template <bool ROWS>
+__global__ void __launch_bounds__(kTileThreads, ROWS ? 5 : 1) tile_program(const __grid_constant__ TileArgs p) {
   extern __shared__ float sm[];
   griddep_launch_dependents();
   griddep_wait();
   const int64_t bid[3] = {p.bid0_begin + blockIdx.x, blockIdx.y, blockIdx.z};
-  for (int o = 0; o < p.n_ops; ++o) {
+  const int n_ops = p.n_ops;
+  for (int o = 0; o < n_ops; ++o) {
     const TileOp& op = p.ops[o];
-    switch (op.kind) {
+    const uint8_t kind = op.kind, code = op.code;
+    switch (kind) {
       case kTLoad:
-      case kTStore: {
-        const bool load = op.kind == kTLoad;
-        const TileVal& v = p.vals[load ? op.dst : op.a];
-        const int32_t(&as)[kTileRank] = p.shape[op.arg];
-        int64_t start[kTileRank];
-#pragma unroll
-        for (int d = 0; d < kTileRank; ++d)
-          start[d] = (op.coord_bid[d] >= 0 ? bid[op.coord_bid[d]] : op.coord[d]) * static_cast<int64_t>(v.shape[d]);
-        for (int e = threadIdx.x; e < v.numel; e += kTileThreads) {
-          int i[kTileRank];
-          unravel(e, v.shape, i);
-          bool in = true;
-          int64_t off = 0;
-#pragma unroll
-          for (int d = 0; d < kTileRank; ++d) {
-            const int64_t g = start[d] + i[d];
-            in = in && g < as[d];
-            off = off * as[d] + g;
-          }
-          if (load)
-            sm[slot(v, i)] = in ? load_elem(p.arr[op.arg], p.elem[op.arg], off) : 0.0f;
-          else if (in)
-            store_elem(p.arr[op.arg], p.elem[op.arg], off, sm[slot(v, i)]);
-        }
+        move_tile<true, ROWS>(sm, p, op, TV(p.vals[op.dst]), bid);
         break;
-      }
+      case kTStore:
+        move_tile<false, ROWS>(sm, p, op, TV(p.vals[op.a]), bid);
+        break;
       case kTConst: {
-        const TileVal& d = p.vals[op.dst];
-        for (int e = threadIdx.x; e < d.numel; e += kTileThreads) {
-          int i[kTileRank];
-          unravel(e, d.shape, i);
-          sm[slot(d, i)] = op.value;
+        const TV d(p.vals[op.dst]);
+        const float value = op.value;
+        if (ROWS || rows_of(d)) {
+          const int C = d.shape[3], c = threadIdx.x % C, rs = kTileThreads / C;
+          for (int r = threadIdx.x / C; r < d.shape[2]; r += rs) sm[d.offset + r * d.stride[2] + c] = value;
+          break;
+        }
+        if constexpr (!ROWS) {
+          Walker w(threadIdx.x, d.shape);
+          for (int e = threadIdx.x; e < d.numel; e += kTileThreads, w.next()) sm[d.at(w.i)] = value;
         }
         break;
       }
       case kTUnary: {
-        const TileVal &d = p.vals[op.dst], &a = p.vals[op.a];
-        for (int e = threadIdx.x; e < d.numel; e += kTileThreads) {
-          int i[kTileRank];
-          unravel(e, d.shape, i);
-          sm[slot(d, i)] = unary_op(op.code, sm[slot(a, i)]);
+        const TV d(p.vals[op.dst]), a(p.vals[op.a]);
+        if (ROWS || rows_of(d)) {
+          const int C = d.shape[3], c = threadIdx.x % C, rs = kTileThreads / C;
+          for (int r = threadIdx.x / C; r < d.shape[2]; r += rs)
+            sm[d.offset + r * d.stride[2] + c] = unary_op(code, sm[a.offset + r * a.stride[2] + c]);
+          break;
+        }
+        if constexpr (!ROWS) {
+          Walker w(threadIdx.x, d.shape);
+          for (int e = threadIdx.x; e < d.numel; e += kTileThreads, w.next())
+            sm[d.at(w.i)] = unary_op(code, sm[a.at(w.i)]);
         }
         break;
       }
       case kTBinary: {
-        const TileVal &d = p.vals[op.dst], &a = p.vals[op.a], &b = p.vals[op.b];
-        for (int e = threadIdx.x; e < d.numel; e += kTileThreads) {
-          int i[kTileRank], ia[kTileRank], ib[kTileRank];
-          unravel(e, d.shape, i);
+        const TV d(p.vals[op.dst]), a(p.vals[op.a]), b(p.vals[op.b]);
+        // broadcast dims (size 1) contribute no stride
+        int sa[kTileRank], sb[kTileRank];
 #pragma unroll
-          for (int k = 0; k < kTileRank; ++k) {
-            ia[k] = a.shape[k] == 1 ? 0 : i[k];
-            ib[k] = b.shape[k] == 1 ? 0 : i[k];
+        for (int k = 0; k < kTileRank; ++k) {
+          sa[k] = a.shape[k] == 1 ? 0 : a.stride[k];
+          sb[k] = b.shape[k] == 1 ? 0 : b.stride[k];
+        }
+        if (ROWS || rows_of(d)) {
+          const int C = d.shape[3], c = threadIdx.x % C, rs = kTileThreads / C;
+          for (int r = threadIdx.x / C; r < d.shape[2]; r += rs) {
+            const float x = sm[a.offset + r * sa[2] + c * sa[3]];
+            const float y = sm[b.offset + r * sb[2] + c * sb[3]];
+            const float v = binary_op(code, x, y);
+            sm[d.offset + r * d.stride[2] + c] = d.i8 ? wrap_i8(v) : v;
           }
-          float r = binary_op(op.code, sm[slot(a, ia)], sm[slot(b, ib)]);
-          sm[slot(d, i)] = d.i8 ? wrap_i8(r) : r;
+          break;
+        }
+        if constexpr (!ROWS) {
+          Walker w(threadIdx.x, d.shape);
+          for (int e = threadIdx.x; e < d.numel; e += kTileThreads, w.next()) {
+            const int(&i)[kTileRank] = w.i;
+            const float x = sm[a.offset + i[0] * sa[0] + i[1] * sa[1] + i[2] * sa[2] + i[3] * sa[3]];
+            const float y = sm[b.offset + i[0] * sb[0] + i[1] * sb[1] + i[2] * sb[2] + i[3] * sb[3]];
+            const float r = binary_op(code, x, y);
+            sm[d.at(i)] = d.i8 ? wrap_i8(r) : r;
+          }
         }
         break;
       }
       case kTReduce: {
-        const TileVal &d = p.vals[op.dst], &a = p.vals[op.a];
-        const int n = a.shape[op.axis];
-        const int step = a.stride[op.axis];
-        for (int e = threadIdx.x; e < d.numel; e += kTileThreads) {
-          int i[kTileRank];
-          unravel(e, d.shape, i);
-          const float* src = sm + slot(a, i);  // the reduced dim's index is 0 in i
+        const TV d(p.vals[op.dst]), a(p.vals[op.a]);
+        const int n = p.vals[op.a].shape[op.axis];  // parameter reads: no runtime index into registers
+        const int step = p.vals[op.a].stride[op.axis];
+        if constexpr (ROWS) {
+          // rows mode: d is R x C with the reduced dim (2 or 3) of size 1
+          const int C = d.shape[3];
+          for (int e = threadIdx.x; e < d.numel; e += kTileThreads) {
+            const int r = e / C, c = e - (e / C) * C;
+            const float* src = sm + a.offset + r * a.stride[2] + c;
+            float v;
+            if (code == 0) {
+              v = src[0];
+              for (int j = 1; j < n; ++j) {
+                const float x = src[j * step];
+                if (x != x || x > v) v = x;
+              }
+            } else {
+              double acc = 0.0;
+              for (int j = 0; j < n; ++j) acc += static_cast<double>(src[j * step]);
+              v = static_cast<float>(acc);
+            }
+            sm[d.offset + r * d.stride[2] + c] = v;
+          }
+          break;
+        }
+        Walker w(threadIdx.x, d.shape);
+        for (int e = threadIdx.x; e < d.numel; e += kTileThreads, w.next()) {
+          const float* src = sm + a.at(w.i);  // the reduced dim's index is 0 in w.i
           float r;
-          if (op.code == 0) {
+          if (code == 0) {
             r = src[0];
             for (int j = 1; j < n; ++j) {
               const float x = src[j * step];
@@ -137,28 +343,41 @@ __global__ void __launch_bounds__(kTileThreads) tile_program(const __grid_consta
             for (int j = 0; j < n; ++j) s += static_cast<double>(src[j * step]);
             r = static_cast<float>(s);
           }
-          sm[slot(d, i)] = r;
+          sm[d.at(w.i)] = r;
         }
         break;
       }
       case kTReshape: {
-        const TileVal &d = p.vals[op.dst], &a = p.vals[op.a];
-        for (int e = threadIdx.x; e < d.numel; e += kTileThreads) {
-          int i[kTileRank], j[kTileRank];
-          unravel(e, d.shape, i);
-          unravel(e, a.shape, j);
-          sm[slot(d, i)] = sm[slot(a, j)];
+        const TV d(p.vals[op.dst]), a(p.vals[op.a]);
+        if constexpr (ROWS) {
+          const int dc = d.shape[3], ac = a.shape[3];
+          for (int e = threadIdx.x; e < d.numel; e += kTileThreads)
+            sm[d.offset + (e / dc) * d.stride[2] + e % dc] = sm[a.offset + (e / ac) * a.stride[2] + e % ac];
+        } else {
+          Walker wd(threadIdx.x, d.shape), wa(threadIdx.x, a.shape);
+          for (int e = threadIdx.x; e < d.numel; e += kTileThreads, wd.next(), wa.next())
+            sm[d.at(wd.i)] = sm[a.at(wa.i)];
         }
         break;
       }
       case kTPermute: {
-        const TileVal &d = p.vals[op.dst], &a = p.vals[op.a];
-        for (int e = threadIdx.x; e < d.numel; e += kTileThreads) {
-          int i[kTileRank], j[kTileRank];
-          unravel(e, d.shape, i);
+        const TV d(p.vals[op.dst]), a(p.vals[op.a]);
+        // dst dim k is src dim perm[k]: the source offset walks the source strides in dst order
+        int ss[kTileRank];
 #pragma unroll
-          for (int k = 0; k < kTileRank; ++k) j[op.perm[k]] = i[k];
-          sm[slot(d, i)] = sm[slot(a, j)];
+        for (int k = 0; k < kTileRank; ++k) ss[k] = p.vals[op.a].stride[op.perm[k]];
+        if (ROWS || rows_of(d)) {
+          const int C = d.shape[3], c = threadIdx.x % C, rs = kTileThreads / C;
+          for (int r = threadIdx.x / C; r < d.shape[2]; r += rs)
+            sm[d.offset + r * d.stride[2] + c] = sm[a.offset + r * ss[2] + c * ss[3]];
+          break;
+        }
+        if constexpr (!ROWS) {
+          Walker w(threadIdx.x, d.shape);
+          for (int e = threadIdx.x; e < d.numel; e += kTileThreads, w.next()) {
+            const int(&i)[kTileRank] = w.i;
+            sm[d.at(i)] = sm[a.offset + i[0] * ss[0] + i[1] * ss[1] + i[2] * ss[2] + i[3] * ss[3]];
+          }
         }
         break;
       }
@@ -183,14 +402,16 @@ cudaError_t launch_tile(const TileArgs& a, cudaStream_t stream) {
     static std::atomic<uint64_t> attr_devices{0};
     const uint64_t bit = dev < 64 ? (uint64_t{1} << dev) : 0;
     if (!(attr_devices.load(std::memory_order_relaxed) & bit)) {
-      cudaError_t e = cudaFuncSetAttribute(tile_program, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           kTileSmemFloats * static_cast<int>(sizeof(float)));
-      if (e != cudaSuccess) return e;
+      for (auto k : {tile_program<true>, tile_program<false>}) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kTileSmemFloats * static_cast<int>(sizeof(float)));
+        if (e != cudaSuccess) return e;
+      }
       attr_devices.fetch_or(bit, std::memory_order_relaxed);
     }
   }
   return PdlLaunch(dim3(static_cast<unsigned>(gx), static_cast<unsigned>(a.grid[1]), static_cast<unsigned>(a.grid[2])),
-                   dim3(kTileThreads), smem, stream)(tile_program, a);
+                   dim3(kTileThreads), smem, stream)(a.rows ? tile_program<true> : tile_program<false>, a);
 }
 
 }  // namespace dev
