@@ -174,3 +174,68 @@ def test_int8_arithmetic_wraps_bit_exact():
     assert m.plan()["family"] == "tile"
     ref = oracle(m, [a, b, torch.zeros(64, 64, dtype=torch.int8)])[2]
     assert np.array_equal(host(y), ref)
+
+
+def test_rank4_permute_general_walker():
+    # rank-4 tiles with non-unit leading dims take the general (walker) path
+    text = """func.func @r(%x: memref<4x6x10x12xf32>, %y: memref<4x10x6x12xf32>) attributes {xt.grid = array<i32: 2, 1, 2>} {
+  %bid:3 = xt.get_tile_block_id : i32, i32, i32
+  %zero = arith.constant 0 : i32
+  %t = xt.load(%x, %bid#0, %zero, %bid#2, %zero) : (memref<4x6x10x12xf32>, i32, i32, i32, i32) -> tensor<2x6x5x12xf32>
+  %p = xt.permute(%t) {permutation = [0, 2, 1, 3]} : tensor<2x6x5x12xf32> -> tensor<2x5x6x12xf32>
+  %u = xt.mul(%p, %p) : tensor<2x5x6x12xf32>, tensor<2x5x6x12xf32> -> tensor<2x5x6x12xf32>
+  xt.store(%u, %y, %bid#0, %bid#2, %zero, %zero) : (tensor<2x5x6x12xf32>, memref<4x10x6x12xf32>, i32, i32, i32, i32) -> ()
+  func.return
+}"""
+    m = xt.parse(text)
+    assert m.plan()["family"] == "tile"
+    x = torch.randn(4, 6, 10, 12, generator=gen(11))
+    y = torch.full((4, 10, 6, 12), float("nan"), device=DEV)
+    xt.launch(m, x.to(DEV), y)
+    ref = oracle(m, [x, torch.zeros(4, 10, 6, 12)])[1]
+    assert np.array_equal(host(y), ref)
+    xh = host(x)
+    assert np.array_equal(ref, np.transpose(xh, (0, 2, 1, 3)) ** 2)
+
+
+def test_bf16_transpose_round_trip_bit_exact():
+    # bf16 loads widen exactly to f32 and stores round back: a transpose moves bits unchanged
+    x = torch.randn(2, 40, 70, generator=gen(14)).to(torch.bfloat16)
+    y = torch.zeros(2, 70, 40, dtype=torch.bfloat16, device=DEV)
+    m = xt.run(transpose3, args=(x.to(DEV), y, 16, 32), grid=(2, 3, 3))
+    assert m.plan()["family"] == "tile"
+    assert torch.equal(y.cpu(), x.transpose(1, 2))
+
+
+@xt.kernel
+def rank1_scale(x, y, t):
+    i = xt.bid(0)
+    v = xt.load(x, index=(i,), shape=(t,))
+    xt.store(y, index=(i,), tile=v * v)
+
+
+def test_rank1_ragged_stores_are_clipped():
+    # 1000 elements in tiles of 96: the last tile runs past the end; nothing past it is written
+    x = torch.randn(1000, generator=gen(12))
+    y = torch.full((1000,), float("nan"), device=DEV)
+    m = xt.run(rank1_scale, args=(x.to(DEV), y, 96), grid=(11, 1, 1))
+    ref = oracle(m, [x, torch.zeros(1000)])[1]
+    assert np.array_equal(host(y), ref)
+
+
+def test_permute_general_path_rank3_ragged():
+    text = """func.func @p(%x: memref<5x7x9xf32>, %y: memref<9x5x7xf32>) attributes {xt.grid = array<i32: 2, 1, 1>} {
+  %bid:3 = xt.get_tile_block_id : i32, i32, i32
+  %zero = arith.constant 0 : i32
+  %t = xt.load(%x, %bid#0, %zero, %zero) : (memref<5x7x9xf32>, i32, i32, i32) -> tensor<3x7x9xf32>
+  %u = xt.permute(%t) {permutation = [2, 0, 1]} : tensor<3x7x9xf32> -> tensor<9x3x7xf32>
+  xt.store(%u, %y, %zero, %bid#0, %zero) : (tensor<9x3x7xf32>, memref<9x5x7xf32>, i32, i32, i32) -> ()
+  func.return
+}"""
+    m = xt.parse(text)
+    x = torch.randn(5, 7, 9, generator=gen(13))
+    y = torch.full((9, 5, 7), float("nan"), device=DEV)
+    xt.launch(m, x.to(DEV), y)
+    ref = oracle(m, [x, torch.zeros(9, 5, 7)])[1]
+    assert np.array_equal(host(y), ref)
+    assert np.array_equal(ref, np.transpose(host(x), (2, 0, 1)))
