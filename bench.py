@@ -772,7 +772,7 @@ def main() -> None:
         line["e2e"] = {"value": round(job_units / (e_ms * 1e-3) / scale, 3), "unit": w["unit"],
                        "ms_per_step": round(e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                        "pipelining": e_note}
-    if not args.no_cpu:
+    if not args.no_cpu and world == 1:  # the host-core baseline is a 1-GPU figure
         line["cpu_baseline"] = cpu_baseline(w, xt, torch)
     print(json.dumps(line), flush=True)
     if dist:
