@@ -59,7 +59,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # the kernel ends are not in these figures (they are written back later).
 NCU_TRAFFIC_BYTES: dict[str, float] = {
     "matmul": 89_688_320 + 40_005_376,
-    "conv2d": 12_956_416 + 256,
+    "conv2d": 12_960_768 + 2_304,
     "add": 33_561_088 + 10_496,
     "softmax": 33_567_488 + 498_432,
     "sharded_matmul": 8_320_000_000 + 1_060_000_000,
