@@ -226,6 +226,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0, armed = 0, armed_phase = 0;
       bool ok = true;
+      // A's rows are reused by every N-tile of a rasterization group (kGroupM
+      // M-tiles, one wave after another): keep them in L2 ahead of B, which is
+      // shared within a wave, so A is not re-read from DRAM for each wave
+      const uint64_t pol_a = l2_policy_evict_last();
       for (int t = pair; t < num_items && ok; t += npairs) {
         const Item it = item_coords(p, t);
         const int32_t row0 = static_cast<int32_t>(p.m_begin + static_cast<int64_t>(it.mt) * 256 + rank * 128);
@@ -244,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
           }
           const uint32_t bar = full0 + static_cast<uint32_t>(stage) * 8u;
-          tma_load_2d_pair(sa + stage * kPAStage, &tma_a, bar, kb * T::kBK, row0);
+          tma_load_2d_pair_hint(sa + stage * kPAStage, &tma_a, bar, kb * T::kBK, row0, pol_a);
           for (int c = 0; c < chunks; ++c)
             tma_load_2d_pair(sb + stage * kPBStage + c * T::kChunkBytes, &tma_b, bar, col0 + c * T::kChunkN,
                              kb * T::kBK);
@@ -361,8 +365,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tma_c, buf, it.col0 + c * 32,
-                         static_cast<int32_t>(p.m_begin + static_cast<int64_t>(mt) * 256 + rank * 128 + q * 32));
+            // C is not read again by this kernel: its lines leave L2 first
+            tma_store_2d_hint(&tma_c, buf, it.col0 + c * 32,
+                              static_cast<int32_t>(p.m_begin + static_cast<int64_t>(mt) * 256 + rank * 128 + q * 32),
+                              l2_policy_evict_first());
             bulk_commit_group();
           }
           continue;
