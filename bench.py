@@ -10,7 +10,8 @@ Workloads are the BASELINE configurations (synthetic, seeded inputs):
   conv2d          NHWC bf16 [32,56,56,64] * [3,3,64,64], pad 1, fp32 out
   sharded_matmul  bf16 [32768,8192] x [8192,8192], fp32 out, 256x128 Block tiles,
                   grid (128,64) split along bid0 across ranks, output rows
-                  gathered to rank 0 over NCCL (the default workload)
+                  gathered to rank 0 over NVLink by peer stores from the GEMM
+                  (--gather nccl: an NCCL gather; the default workload)
 
 A step is one launch of the workload's Block program over its whole Grid
 (for sharded_matmul: every rank's share plus the gather).  ``value`` is the

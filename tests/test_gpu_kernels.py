@@ -257,6 +257,60 @@ def test_matmul_bid0_shards_match_full_launch():
     assert torch.equal(full, parts)
 
 
+def test_matmul_config5_shards_full_size():
+    """Config 5 at full size (A bf16 [32768,8192] x B bf16 [8192,8192], seed 4,
+    256x128 Blocks, grid (128,64)), built exactly as bench.py builds it.
+
+    * the bid0 splits bench.py uses (equal shares over 2, 4 and 8 ranks, and the
+      peer-gather split that gives rank 0 a larger share) each reproduce a
+      full launch bit for bit;
+    * three seeded Blocks in every one of the 8 equal shards (its first and
+      last bid0 and one inside: 768 rows per shard) against the oracle;
+    * the full rows on both sides of every shard boundary against float64 dot
+      products of the same bf16 inputs.
+    """
+    import bench
+
+    w = bench.build_workload("sharded_matmul", xt, torch, 1, 0)
+    m = w["module"]
+    a_h, b_h = w["inputs"]
+    a, b = a_h.to(DEV), b_h.to(DEV)
+    M, N = w["out_shape"]
+    grid0 = m.plan()["grid"][0]
+    full = torch.empty(M, N, device=DEV)
+    xt.launch(m, a, b, full)
+    parts = torch.empty(M, N, device=DEV)
+    splits = [(world, None) for world in (2, 4, 8)]
+    splits += [(world, bench.gather_root_share(world, 2.0 * M * N * 8192, M * N * 4.0)) for world in (4, 8)]
+    bounds = set()
+    for world, share in splits:
+        parts.fill_(float("nan"))
+        for r in range(world):
+            lo, hi = bench.bid0_share(grid0, world, r, share)
+            xt.launch(m, a, b, parts, bid0_range=(lo, hi))
+            bounds.add(lo)
+        assert torch.equal(full, parts), (world, share)
+    del parts
+
+    rng = np.random.default_rng(4)
+    blocks = []
+    for s in range(8):
+        lo, hi = bench.bid0_share(grid0, 8, s)
+        for x in (lo, int(rng.integers(lo + 1, hi - 1)), hi - 1):
+            blocks.append((x, int(rng.integers(0, 64)), 0))
+    ref = oracle(m, [a_h, b_h, torch.zeros(M, N)], blocks=blocks)[2]
+    got = host(full)
+    for x, y, _ in blocks:
+        sl = (slice(x * 256, x * 256 + 256), slice(y * 128, y * 128 + 128))
+        bf16_close(got[sl], ref[sl])
+
+    rows = sorted({r for lo in bounds if lo > 0 for r in (lo * 256 - 1, lo * 256)})
+    a64 = a_h[rows].double().numpy()
+    b64 = b_h.double().numpy()
+    bf16_close(got[rows], a64 @ b64)
+    torch.cuda.empty_cache()
+
+
 @xt.kernel
 def matmul_i8(lhs, rhs, res, scale, bias, tm, tn, tk):
     i, j = xt.bid(0), xt.bid(1)

@@ -239,3 +239,61 @@ def test_permute_general_path_rank3_ragged():
     ref = oracle(m, [x, torch.zeros(9, 5, 7)])[1]
     assert np.array_equal(host(y), ref)
     assert np.array_equal(ref, np.transpose(host(x), (2, 0, 1)))
+
+
+# Grids of thousands of Blocks, with ragged edge tiles and bid0 shards: every
+# CTA of the launch sees its own Block coordinates, tile starts past 2^16
+# elements, and edge tiles clipped in rows and in float4 columns.
+
+def test_large_grid_transpose_ragged_edges_bit_exact():
+    # grid (6, 33, 16) = 3168 Blocks; the last row tile holds 8 of 16 rows
+    # and the last column tile 20 of 32
+    x = torch.randn(6, 520, 500, generator=gen(21))
+    y = torch.full((6, 500, 520), float("nan"), device=DEV)
+    m = xt.run(transpose3, args=(x.to(DEV), y, 16, 32), grid=(6, 33, 16))
+    assert torch.equal(y.cpu(), x.transpose(1, 2))
+
+
+def test_large_grid_transpose_bid0_shards_match_full_launch():
+    # grid (160, 4, 4) launched whole and as the shards [0, 150) and [150, 160)
+    x = torch.randn(160, 64, 128, generator=gen(22)).to(DEV)
+    full = torch.empty(160, 128, 64, device=DEV)
+    parts = torch.full((160, 128, 64), float("nan"), device=DEV)
+    m = xt.run(transpose3, args=(x, full, 16, 32), grid=(160, 4, 4))
+    assert torch.equal(full, x.transpose(1, 2))
+    for lo, hi in [(0, 150), (150, 160)]:
+        xt.launch(m, x, parts, bid0_range=(lo, hi))
+    assert torch.equal(full, parts)
+
+
+def test_large_grid_axis0_reductions():
+    # 64 x 32 tiles over [4096, 1024]: grid (64, 32) = 2048 Blocks
+    x = torch.randn(4096, 1024, generator=gen(23)) * 3
+    s = torch.empty(64, 1024, device=DEV)
+    mx = torch.empty(64, 1024, device=DEV)
+    m = xt.run(col_stats, args=(x.to(DEV), s, mx, 64, 32), grid=(64, 32, 1))
+    xr = x.view(64, 64, 1024).double()
+    assert torch.equal(mx.cpu(), x.view(64, 64, 1024).amax(dim=1))
+    ref = xr.sum(dim=1).float().numpy()
+    got = host(s)
+    assert np.all(np.abs(got - ref) <= 1e-6 * np.abs(ref) + 1e-6)
+
+
+def test_large_grid_rank4_permute_general_path():
+    # rank-4 tiles with a non-unit leading dim (general walker path) on a grid
+    # of (40, 1, 80) = 3200 Blocks
+    text = """func.func @r(%x: memref<80x6x320x12xf32>, %y: memref<80x320x6x12xf32>) attributes {xt.grid = array<i32: 40, 1, 80>} {
+  %bid:3 = xt.get_tile_block_id : i32, i32, i32
+  %zero = arith.constant 0 : i32
+  %t = xt.load(%x, %bid#0, %zero, %bid#2, %zero) : (memref<80x6x320x12xf32>, i32, i32, i32, i32) -> tensor<2x6x4x12xf32>
+  %p = xt.permute(%t) {permutation = [0, 2, 1, 3]} : tensor<2x6x4x12xf32> -> tensor<2x4x6x12xf32>
+  %u = xt.mul(%p, %p) : tensor<2x4x6x12xf32>, tensor<2x4x6x12xf32> -> tensor<2x4x6x12xf32>
+  xt.store(%u, %y, %bid#0, %bid#2, %zero, %zero) : (tensor<2x4x6x12xf32>, memref<80x320x6x12xf32>, i32, i32, i32, i32) -> ()
+  func.return
+}"""
+    m = xt.parse(text)
+    assert m.plan()["family"] == "tile"
+    x = torch.randn(80, 6, 320, 12, generator=gen(24))
+    y = torch.full((80, 320, 6, 12), float("nan"), device=DEV)
+    xt.launch(m, x.to(DEV), y)
+    assert torch.equal(y.cpu(), x.permute(0, 2, 1, 3) ** 2)
