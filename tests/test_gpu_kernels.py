@@ -418,6 +418,9 @@ def test_conv_config4_bf16_sampled():
     ((1, 16, 16, 32), (5, 5, 32, 32), (16, 16), (2, 2), (1, 1)),  # window kernel, any-tap loop
     ((3, 16, 16, 32), (5, 5, 32, 32), (16, 16), (2, 2), (1, 1)),  # 5 stacked taps, 4 shifted rows
     ((1, 12, 20, 64), (3, 3, 64, 64), (4, 20), (2, 2), (2, 2)),   # stacked taps with dilation 2
+    ((3, 17, 45, 64), (3, 3, 64, 64), (6, 45), None, (1, 1)),     # window kernel, odd sizes
+    ((1, 14, 33, 64), (5, 3, 64, 64), (5, 33), (2, 1), (2, 1)),   # 5 x 3 filter, dilation 2 in H
+    ((1, 12, 20, 64), (3, 3, 64, 64), (4, 22), (2, 2), (1, 1)),   # pad 2: output wider than the input
 ])
 def test_conv_bf16_shapes(shape, kshape, tile, pad, dil):
     got, ref = conv_case(shape, kshape, tile, torch.bfloat16, 4, pad=pad, dil=dil)
