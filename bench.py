@@ -62,7 +62,7 @@ NCU_TRAFFIC_BYTES: dict[str, float] = {
     "matmul": 89_688_320 + 40_005_376,
     "conv2d": 12_960_768 + 2_304,
     "add": 33_561_088 + 10_496,
-    "softmax": 33_567_488 + 498_432,
+    "softmax": 33_566_464 + 343_552,
     "sharded_matmul": 6_210_000_000 + 1_060_000_000,
 }
 

@@ -297,3 +297,32 @@ def test_large_grid_rank4_permute_general_path():
     y = torch.full((80, 320, 6, 12), float("nan"), device=DEV)
     xt.launch(m, x.to(DEV), y)
     assert torch.equal(y.cpu(), x.permute(0, 2, 1, 3) ** 2)
+
+
+def test_permute_used_twice_and_permute_chains_bit_exact():
+    # the transposed tile feeds a store and a multiply (not folded into the
+    # store); a second program transposes twice (the first permute feeds the
+    # second, which is folded into the store)
+    from tests.test_tile import transpose_twice_used
+
+    x = torch.randn(2, 96, 200, generator=gen(25))
+    y = torch.full((2, 200, 96), float("nan"), device=DEV)
+    z = torch.full((2, 200, 96), float("nan"), device=DEV)
+    xt.run(transpose_twice_used, args=(x.to(DEV), y, z, 32, 64), grid=(2, 3, 4))
+    xt_ = x.transpose(1, 2)
+    assert torch.equal(y.cpu(), xt_)
+    assert torch.equal(z.cpu(), xt_ * xt_)
+    text = """func.func @pp(%x: memref<4x6x8xf32>, %y: memref<4x6x8xf32>) attributes {xt.grid = array<i32: 2, 1, 1>} {
+  %bid:3 = xt.get_tile_block_id : i32, i32, i32
+  %zero = arith.constant 0 : i32
+  %t = xt.load(%x, %bid#0, %zero, %zero) : (memref<4x6x8xf32>, i32, i32, i32) -> tensor<2x6x8xf32>
+  %u = xt.permute(%t) {permutation = [2, 0, 1]} : tensor<2x6x8xf32> -> tensor<8x2x6xf32>
+  %v = xt.permute(%u) {permutation = [1, 2, 0]} : tensor<8x2x6xf32> -> tensor<2x6x8xf32>
+  xt.store(%v, %y, %bid#0, %zero, %zero) : (tensor<2x6x8xf32>, memref<4x6x8xf32>, i32, i32, i32) -> ()
+  func.return
+}"""
+    m = xt.parse(text)
+    xs = torch.randn(4, 6, 8, generator=gen(26))
+    ys = torch.full((4, 6, 8), float("nan"), device=DEV)
+    xt.launch(m, xs.to(DEV), ys)
+    assert torch.equal(ys.cpu(), xs)

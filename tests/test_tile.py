@@ -58,3 +58,22 @@ def test_permute_must_match_its_result_shape():
   func.return
 }"""
     assert xt.parse(text).plan()["family"] == "tile"
+
+
+@xt.kernel
+def transpose_twice_used(x, y, z, tm, tn):
+    b, i, j = xt.bid(0), xt.bid(1), xt.bid(2)
+    t = xt.transpose(xt.load(x, index=(b, i, j), shape=(1, tm, tn)))
+    xt.store(y, index=(b, j, i), tile=t)
+    xt.store(z, index=(b, j, i), tile=t * t)
+
+
+def test_a_permute_feeding_only_a_store_is_folded_into_it():
+    # load + transpose + store plans as two tile ops: the store reads the
+    # loaded tile through the transposed strides
+    m = xt.convert(transpose3, args=(A((2, 96, 200), f32), A((2, 200, 96), f32), 32, 64), grid=(2, 3, 4))
+    assert "2 tile ops" in str(xt.xt_to_nova(xt.xt_serialize(m)))
+    # a transposed tile that is also multiplied keeps its permute op
+    m = xt.convert(transpose_twice_used, args=(A((2, 96, 200), f32), A((2, 200, 96), f32), A((2, 200, 96), f32),
+                                               32, 64), grid=(2, 3, 4))
+    assert "5 tile ops" in str(xt.xt_to_nova(xt.xt_serialize(m)))

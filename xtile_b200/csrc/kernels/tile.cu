@@ -17,7 +17,9 @@
 //                 in f64 and round once to f32;
 //   reshape       the same row-major element order in a new shape;
 //   permute       dims reordered (xt.transpose is the rank-3 swap of the last
-//                 two dims, XTOps.cpp:318-327).
+//                 two dims, XTOps.cpp:318-327).  A permute whose result only
+//                 feeds one store is folded into it by the planner: the
+//                 store reads the operand through the permuted strides.
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -97,10 +99,34 @@ __device__ __forceinline__ float wrap_i8(float x) {
   return static_cast<float>(static_cast<int8_t>(static_cast<int>(x)));
 }
 
+// Where a store reads its tile in shared memory: the stored value's own
+// slot, or, for a store with a folded permute (TileOp code 1), the permute's
+// operand through the permuted strides.
+struct SmemView {
+  int offset;
+  int stride[kTileRank];
+};
+
+__device__ __forceinline__ SmemView store_view(const TileArgs& p, const TileOp& op, const TV& v) {
+  SmemView rd;
+  if (op.code == 1) {
+    rd.offset = p.vals[op.b].offset;
+#pragma unroll
+    for (int k = 0; k < kTileRank; ++k) rd.stride[k] = p.vals[op.b].stride[op.perm[k]];
+  } else {
+    rd.offset = v.offset;
+#pragma unroll
+    for (int k = 0; k < kTileRank; ++k) rd.stride[k] = v.stride[k];
+  }
+  return rd;
+}
+
 // Load or store of one tile: elements past the array edge load 0 / are skipped.
+// A load writes the slot of ``v``; a store writes the tile ``v`` (its shape)
+// reading each element through ``rd``.
 template <bool LOAD, bool ROWS>
 __device__ __forceinline__ void move_tile(float* sm, const TileArgs& p, const TileOp& op, const TV& v,
-                                          const int64_t (&bid)[3]) {
+                                          const int64_t (&bid)[3], const SmemView& rd) {
   int64_t astride[kTileRank];
   int lim[kTileRank];
   int64_t base = 0;
@@ -151,12 +177,13 @@ __device__ __forceinline__ void move_tile(float* sm, const TileArgs& p, const Ti
           }
         }
       } else if (col_in) {
+        const int cs = rd.stride[3];
 #pragma unroll
         for (int u = 0; u < kVecBatch; ++u) {
           const int ru = r + u * rs;
           if (ru < r_lim) {
-            const float* s4 = sm + v.offset + ru * v.stride[2] + c;
-            g[(base + ru * astride[2] + c) / 4] = make_float4(s4[0], s4[1], s4[2], s4[3]);
+            const float* s4 = sm + rd.offset + ru * rd.stride[2] + c * cs;
+            g[(base + ru * astride[2] + c) / 4] = make_float4(s4[0], s4[cs], s4[2 * cs], s4[3 * cs]);
           }
         }
       }
@@ -188,7 +215,9 @@ __device__ __forceinline__ void move_tile(float* sm, const TileArgs& p, const Ti
         soff += kBatch * sstep;
       }
     } else if (col_in) {
-      for (; r < r_lim; r += rs, goff += gstep, soff += sstep) store_elem(arr, elem, goff, sm[soff]);
+      int roff = rd.offset + r * rd.stride[2] + c * rd.stride[3];
+      const int rstep = rs * rd.stride[2];
+      for (; r < r_lim; r += rs, goff += gstep, roff += rstep) store_elem(arr, elem, goff, sm[roff]);
     }
     return;
   }
@@ -217,7 +246,10 @@ __device__ __forceinline__ void move_tile(float* sm, const TileArgs& p, const Ti
     for (int e = threadIdx.x; e < v.numel; e += kTileThreads, w.next()) {
       const bool in = w.i[0] < lim[0] && w.i[1] < lim[1] && w.i[2] < lim[2] && w.i[3] < lim[3];
       const int64_t off = base + w.i[0] * astride[0] + w.i[1] * astride[1] + w.i[2] * astride[2] + w.i[3];
-      if (in) store_elem(arr, elem, off, sm[v.at(w.i)]);
+      if (in)
+        store_elem(arr, elem, off,
+                   sm[rd.offset + w.i[0] * rd.stride[0] + w.i[1] * rd.stride[1] + w.i[2] * rd.stride[2] +
+                      w.i[3] * rd.stride[3]]);
     }
   }
 }
@@ -236,12 +268,16 @@ __global__ void __launch_bounds__(kTileThreads, ROWS ? 5 : 1) tile_program(const
     const TileOp& op = p.ops[o];
     const uint8_t kind = op.kind, code = op.code;
     switch (kind) {
-      case kTLoad:
-        move_tile<true, ROWS>(sm, p, op, TV(p.vals[op.dst]), bid);
+      case kTLoad: {
+        const TV v(p.vals[op.dst]);
+        move_tile<true, ROWS>(sm, p, op, v, bid, SmemView{});
         break;
-      case kTStore:
-        move_tile<false, ROWS>(sm, p, op, TV(p.vals[op.a]), bid);
+      }
+      case kTStore: {
+        const TV v(p.vals[op.a]);
+        move_tile<false, ROWS>(sm, p, op, v, bid, store_view(p, op, v));
         break;
+      }
       case kTConst: {
         const TV d(p.vals[op.dst]);
         const float value = op.value;

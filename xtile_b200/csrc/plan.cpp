@@ -382,6 +382,35 @@ class Classifier {
       if (p.ops.size() == static_cast<size_t>(kTileMaxOps)) unsupported("the program has more than 32 tile ops");
       p.ops.push_back(t);
     }
+    // A permute whose result feeds nothing but one store is folded into that
+    // store: the store reads the permute's operand through the permuted
+    // strides (code 1, b = the operand, perm), which saves the kernel a pass
+    // over shared memory and a CTA barrier per Block.
+    {
+      std::vector<int> uses(p.vals.size(), 0);
+      for (const TileOp& t : p.ops) {
+        if (t.kind == kTStore || t.kind == kTUnary || t.kind == kTReduce || t.kind == kTReshape ||
+            t.kind == kTPermute || t.kind == kTBinary)
+          ++uses[t.a];
+        if (t.kind == kTBinary) ++uses[t.b];
+      }
+      std::vector<TileOp> ops;
+      for (size_t i = 0; i < p.ops.size(); ++i) {
+        const TileOp t = p.ops[i];
+        if (t.kind == kTPermute && uses[t.dst] == 1) {
+          auto st = std::find_if(p.ops.begin() + static_cast<std::ptrdiff_t>(i) + 1, p.ops.end(),
+                                 [&](const TileOp& o) { return o.kind == kTStore && o.a == t.dst; });
+          if (st != p.ops.end()) {
+            st->code = 1;
+            st->b = t.a;
+            for (int d = 0; d < kTileRank; ++d) st->perm[d] = t.perm[d];
+            continue;
+          }
+        }
+        ops.push_back(t);
+      }
+      p.ops = std::move(ops);
+    }
     // Every Block stores tiles of its own: Blocks differing along any grid
     // axis must store to different tiles, or the result would depend on the
     // order in which Blocks run.

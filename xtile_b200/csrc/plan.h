@@ -123,11 +123,12 @@ struct TileVal {               // one tile value, f32 elements in shared memory
 
 struct TileOp {
   uint8_t kind;                // TileOpKind
-  uint8_t code;                // unary / binary: Opcode (kExp.., kAdd.., kItof, kFtoi); reduce: 0 max, 1 sum
+  uint8_t code;                // unary / binary: Opcode (kExp.., kAdd.., kItof, kFtoi); reduce: 0 max, 1 sum;
+                               // store: 1 = value ``a`` is permute(``b``, perm), read from ``b`` (``a`` has no slot data)
   uint8_t dst, a, b;           // value indices (store: ``a`` is the stored value)
   uint8_t arg;                 // load / store: argument slot
   uint8_t axis;                // reduce: the reduced dim
-  uint8_t perm[kTileRank];     // permute: dst dim d is src dim perm[d]
+  uint8_t perm[kTileRank];     // permute (and store code 1): dst dim d is src dim perm[d]
   int8_t coord_bid[kTileRank]; // load / store tile coordinate per dim: bid axis, or -1 for ``coord``
   int32_t coord[kTileRank];
   float value;                 // constant splat
