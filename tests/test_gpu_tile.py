@@ -326,3 +326,20 @@ def test_permute_used_twice_and_permute_chains_bit_exact():
     ys = torch.full((4, 6, 8), float("nan"), device=DEV)
     xt.launch(m, xs.to(DEV), ys)
     assert torch.equal(ys.cpu(), xs)
+
+
+@xt.kernel
+def swap_tiles(x, y, tm, tn):
+    i, j = xt.bid(0), xt.bid(1)
+    xt.store(y, index=(j, i), tile=xt.load(x, index=(i, j), shape=(tm, tn)))
+
+
+def test_tile_copy_to_swapped_coordinates_ragged():
+    # a plain load + store (the data-movement path without a transpose): the
+    # tile at (i, j) of x lands at (j, i) of y; edge tiles load zeros past x's
+    # edge and are clipped at y's
+    x = torch.randn(90, 188, generator=gen(27))
+    y = torch.full((90, 188), float("nan"), device=DEV)
+    m = xt.run(swap_tiles, args=(x.to(DEV), y, 16, 32), grid=(6, 6, 1))
+    ref = oracle(m, [x, torch.full((90, 188), float("nan"))])[1]
+    assert np.array_equal(host(y), ref, equal_nan=True)

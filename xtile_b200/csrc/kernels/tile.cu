@@ -424,12 +424,184 @@ __global__ void __launch_bounds__(kTileThreads, ROWS ? 5 : 1) tile_program(const
   }
 }
 
+// ---------------------------------------------------------------------------
+// Pure data movement: the program is one f32 row-tile load and one store of
+// that tile, unchanged or transposed (a permute folded into the store).  The
+// interpreter above spends most of its issue slots on per-op set-up (64-bit
+// geometry, runtime divisions, op decoding) for 8 elements per thread; this
+// kernel takes the tile geometry precomputed on the host as per-axis
+// multipliers and power-of-two thread layouts.
+struct MoveGeom {
+  int64_t cst;          // first element of the tile for bid = (0, 0, 0)
+  int64_t mult[3];      // elements per unit of bid(k)
+  int64_t row;          // array row stride (elements)
+  int32_t r_cst, r_mult[3];  // first tile row, as an array row index
+  int32_t c_cst, c_mult[3];  // first tile column
+  int32_t ext_r, ext_c;      // array rows / columns
+};
+
+struct MoveArgs {
+  const float* in;
+  float* out;
+  MoveGeom g_in, g_out;
+  int32_t R, C;         // loaded tile rows x columns
+  int32_t lc4, lo4;     // log2 of float4s per loaded / stored tile row
+  int32_t sp;           // shared-memory row stride of the loaded tile (odd)
+  int64_t bid0_begin;
+};
+
+__device__ __forceinline__ void move_geom(const MoveGeom& g, const int64_t (&bid)[3], int rows, int cols,
+                                          int64_t& base, int& nr, int& nc) {
+  base = g.cst + bid[0] * g.mult[0] + bid[1] * g.mult[1] + bid[2] * g.mult[2];
+  const int64_t r0 = g.r_cst + bid[0] * g.r_mult[0] + bid[1] * g.r_mult[1] + bid[2] * g.r_mult[2];
+  const int64_t c0 = g.c_cst + bid[0] * g.c_mult[0] + bid[1] * g.c_mult[1] + bid[2] * g.c_mult[2];
+  const int64_t lr = g.ext_r - r0, lc = g.ext_c - c0;
+  nr = lr <= 0 ? 0 : (lr < rows ? static_cast<int>(lr) : rows);
+  nc = lc <= 0 ? 0 : (lc < cols ? static_cast<int>(lc) : cols);
+}
+
+template <bool TRANSPOSE>
+__global__ void __launch_bounds__(kTileThreads) tile_move(const __grid_constant__ MoveArgs p) {
+  extern __shared__ float sm[];
+  griddep_launch_dependents();
+  griddep_wait();
+  const int64_t bid[3] = {p.bid0_begin + blockIdx.x, blockIdx.y, blockIdx.z};
+  const int R = p.R, C = p.C, sp = p.sp;
+  int64_t base;
+  int nr, nc;
+  move_geom(p.g_in, bid, R, C, base, nr, nc);
+  {
+    // loaded tile: float4 column c4 of rows r, r + rs, ...; up to 4 in flight
+    const int c4 = threadIdx.x & ((1 << p.lc4) - 1);
+    const int rs = kTileThreads >> p.lc4;
+    const bool col_in = 4 * c4 < nc;
+    const float4* g = reinterpret_cast<const float4*>(p.in + base) + c4;
+    const int64_t row4 = p.g_in.row >> 2;
+    for (int r = threadIdx.x >> p.lc4; r < R; r += 4 * rs) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int ru = r + u * rs;
+        v[u] = (col_in && ru < nr) ? __ldg(g + ru * row4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int ru = r + u * rs;
+        if (ru < R) {
+          float* d = sm + ru * sp + 4 * c4;
+          d[0] = v[u].x;
+          d[1] = v[u].y;
+          d[2] = v[u].z;
+          d[3] = v[u].w;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const int OR = TRANSPOSE ? C : R, OC = TRANSPOSE ? R : C;
+  move_geom(p.g_out, bid, OR, OC, base, nr, nc);
+  const int c4 = threadIdx.x & ((1 << p.lo4) - 1);
+  if (4 * c4 >= nc) return;
+  const int rs = kTileThreads >> p.lo4;
+  float4* g = reinterpret_cast<float4*>(p.out + base) + c4;
+  const int64_t row4 = p.g_out.row >> 2;
+  for (int r = threadIdx.x >> p.lo4; r < nr; r += rs) {
+    float4 o;
+    if (TRANSPOSE) {
+      const float* s = sm + 4 * c4 * sp + r;  // output (r, 4 c4 + k) = loaded (4 c4 + k, r)
+      o = make_float4(s[0], s[sp], s[2 * sp], s[3 * sp]);
+    } else {
+      const float* s = sm + r * sp + 4 * c4;
+      o = make_float4(s[0], s[1], s[2], s[3]);
+    }
+    g[r * row4] = o;
+  }
+}
+
+// The move kernel's arguments when the program is a plain f32 row-tile load
+// and store (optionally transposed) that it can run; false otherwise.
+bool plan_move(const TileArgs& a, MoveArgs& m, bool& transpose) {
+  if (a.n_ops != 2 || a.ops[0].kind != kTLoad || a.ops[1].kind != kTStore) return false;
+  const TileOp &ld = a.ops[0], &st = a.ops[1];
+  const TileVal& v = a.vals[ld.dst];
+  const TileVal& o = a.vals[st.a];
+  const bool copy = st.code == 0 && st.a == ld.dst;
+  transpose = st.code == 1 && st.b == ld.dst && st.perm[0] == 0 && st.perm[1] == 1 && st.perm[2] == 3 &&
+              st.perm[3] == 2;
+  if (!copy && !transpose) return false;
+  if (a.elem[ld.arg] != kF32 || a.elem[st.arg] != kF32) return false;
+  if (v.shape[0] != 1 || v.shape[1] != 1 || o.shape[0] != 1 || o.shape[1] != 1) return false;
+  const int R = v.shape[2], C = v.shape[3];
+  const int OC = transpose ? R : C;
+  auto log2_of = [](int x) {
+    int l = 0;
+    while ((1 << l) < x) ++l;
+    return (1 << l) == x ? l : -1;
+  };
+  if (R % 4 || C % 4) return false;
+  const int lc4 = log2_of(C / 4), lo4 = log2_of(OC / 4);
+  if (lc4 < 0 || lo4 < 0 || C / 4 > kTileThreads || OC / 4 > kTileThreads) return false;
+  const int sp = C % 2 == 0 ? C + 1 : C;
+  if (static_cast<int64_t>(R) * sp > 12 * 1024) return false;  // 48 KiB of shared memory
+  if ((reinterpret_cast<uintptr_t>(a.arr[ld.arg]) | reinterpret_cast<uintptr_t>(a.arr[st.arg])) & 15) return false;
+  auto geom = [&](const TileOp& op, const TileVal& t, MoveGeom& g) {
+    const int32_t* ext = a.shape[op.arg];
+    if (ext[3] % 4) return false;  // rows of whole float4s
+    int64_t astride[kTileRank], run = 1;
+    for (int d = kTileRank - 1; d >= 0; --d) {
+      astride[d] = run;
+      run *= ext[d];
+    }
+    g = MoveGeom{};
+    g.row = astride[2];
+    g.ext_r = ext[2];
+    g.ext_c = ext[3];
+    for (int d = 0; d < kTileRank; ++d) {
+      const int cb = op.coord_bid[d];
+      // leading dims: tile extent 1; every Block's coordinate must lie inside the array
+      if (d < 2 && (cb >= 0 ? a.grid[cb] > ext[d] : op.coord[d] >= ext[d])) return false;
+      const int64_t step = static_cast<int64_t>(t.shape[d]);
+      if (cb >= 0) {
+        g.mult[cb] += step * astride[d];
+        if (d == 2) g.r_mult[cb] = static_cast<int32_t>(step);
+        if (d == 3) g.c_mult[cb] = static_cast<int32_t>(step);
+      } else {
+        g.cst += op.coord[d] * step * astride[d];
+        if (d == 2) g.r_cst = static_cast<int32_t>(op.coord[d] * step);
+        if (d == 3) g.c_cst = static_cast<int32_t>(op.coord[d] * step);
+      }
+    }
+    return true;
+  };
+  if (!geom(ld, v, m.g_in) || !geom(st, o, m.g_out)) return false;
+  m.in = static_cast<const float*>(a.arr[ld.arg]);
+  m.out = static_cast<float*>(a.arr[st.arg]);
+  m.R = R;
+  m.C = C;
+  m.lc4 = lc4;
+  m.lo4 = lo4;
+  m.sp = sp;
+  m.bid0_begin = a.bid0_begin;
+  return true;
+}
+
 }  // namespace
 
 cudaError_t launch_tile(const TileArgs& a, cudaStream_t stream) {
   const int64_t gx = a.bid0_end - a.bid0_begin;
   if (gx <= 0) return cudaSuccess;
   if (gx > 0x7fffffff || a.grid[1] > 65535 || a.grid[2] > 65535) return cudaErrorInvalidValue;
+  {
+    MoveArgs m;
+    bool transpose = false;
+    if (plan_move(a, m, transpose)) {
+      const size_t msmem = static_cast<size_t>(m.R) * m.sp * sizeof(float);
+      PdlLaunch launch(dim3(static_cast<unsigned>(gx), static_cast<unsigned>(a.grid[1]),
+                            static_cast<unsigned>(a.grid[2])),
+                       dim3(kTileThreads), msmem, stream);
+      return transpose ? launch(tile_move<true>, m) : launch(tile_move<false>, m);
+    }
+  }
   const size_t smem = static_cast<size_t>(a.smem_floats) * sizeof(float);
   if (smem > 48 * 1024) {
     // the opt-in to more than 48 KiB is per device; set it to the family's maximum once
