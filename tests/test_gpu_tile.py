@@ -343,3 +343,24 @@ def test_tile_copy_to_swapped_coordinates_ragged():
     m = xt.run(swap_tiles, args=(x.to(DEV), y, 16, 32), grid=(6, 6, 1))
     ref = oracle(m, [x, torch.full((90, 188), float("nan"))])[1]
     assert np.array_equal(host(y), ref, equal_nan=True)
+
+
+@pytest.mark.parametrize("dtype,shape,tile", [
+    (torch.bfloat16, (4, 64, 128), (32, 64)),
+    (torch.bfloat16, (3, 104, 120), (16, 32)),   # ragged rows and columns (whole 16-byte vectors)
+    (torch.int8, (2, 64, 192), (32, 64)),
+    (torch.int8, (2, 80, 176), (32, 32)),        # ragged rows and columns
+])
+def test_data_movement_transpose_bf16_int8_bit_exact(dtype, shape, tile):
+    # 16-byte vectors of 8 bf16 or 16 int8 elements; the values pass through
+    # f32 in shared memory and come back bit for bit
+    g = gen(28)
+    if dtype == torch.int8:
+        x = torch.randint(-128, 128, shape, generator=g, dtype=torch.int8)
+    else:
+        x = torch.randn(*shape, generator=g).to(dtype)
+    y = torch.zeros(shape[0], shape[2], shape[1], dtype=dtype, device=DEV)
+    tm, tn = tile
+    grid = (shape[0], -(-shape[1] // tm), -(-shape[2] // tn))
+    xt.run(transpose3, args=(x.to(DEV), y, tm, tn), grid=grid)
+    assert torch.equal(y.cpu(), x.transpose(1, 2))

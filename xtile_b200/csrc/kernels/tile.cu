@@ -425,12 +425,15 @@ __global__ void __launch_bounds__(kTileThreads, ROWS ? 5 : 1) tile_program(const
 }
 
 // ---------------------------------------------------------------------------
-// Pure data movement: the program is one f32 row-tile load and one store of
-// that tile, unchanged or transposed (a permute folded into the store).  The
-// interpreter above spends most of its issue slots on per-op set-up (64-bit
-// geometry, runtime divisions, op decoding) for 8 elements per thread; this
-// kernel takes the tile geometry precomputed on the host as per-axis
-// multipliers and power-of-two thread layouts.
+// Pure data movement: the program is one row-tile load and one store of that
+// tile, unchanged or transposed (a permute folded into the store), with both
+// arrays of one element type.  The interpreter above spends most of its issue
+// slots on per-op set-up (64-bit geometry, runtime divisions, op decoding)
+// for 8 elements per thread; this kernel takes the tile geometry
+// precomputed on the host as per-axis multipliers and moves 16 bytes per
+// thread access (4 f32, 8 bf16 or 16 int8 elements) with power-of-two thread
+// layouts.  Shared memory holds the tile as f32 values, which every f32,
+// bf16 and int8 value converts to and from exactly.
 struct MoveGeom {
   int64_t cst;          // first element of the tile for bid = (0, 0, 0)
   int64_t mult[3];      // elements per unit of bid(k)
@@ -441,13 +444,52 @@ struct MoveGeom {
 };
 
 struct MoveArgs {
-  const float* in;
-  float* out;
+  const void* in;
+  void* out;
   MoveGeom g_in, g_out;
   int32_t R, C;         // loaded tile rows x columns
-  int32_t lc4, lo4;     // log2 of float4s per loaded / stored tile row
+  int32_t lc, lo;       // log2 of 16-byte vectors per loaded / stored tile row
   int32_t sp;           // shared-memory row stride of the loaded tile (odd)
   int64_t bid0_begin;
+};
+
+// 16 bytes of elements of EB bytes each <-> f32 values.
+template <int EB>
+struct Vec16 {
+  static constexpr int n = 16 / EB;
+  static __device__ __forceinline__ void unpack(const uint4& u, float (&f)[n]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if constexpr (EB == 4) {
+        f[i] = __uint_as_float(w[i]);
+      } else if constexpr (EB == 2) {  // bf16: the high half of an f32
+        f[2 * i] = __uint_as_float(w[i] << 16);
+        f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+      } else {  // int8
+#pragma unroll
+        for (int k = 0; k < 4; ++k) f[4 * i + k] = static_cast<float>(static_cast<int8_t>(w[i] >> (8 * k)));
+      }
+    }
+  }
+  // exact for values that came from this element type
+  static __device__ __forceinline__ uint4 pack(const float (&f)[n]) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if constexpr (EB == 4) {
+        w[i] = __float_as_uint(f[i]);
+      } else if constexpr (EB == 2) {
+        w[i] = (__float_as_uint(f[2 * i]) >> 16) | (__float_as_uint(f[2 * i + 1]) & 0xffff0000u);
+      } else {
+        w[i] = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          w[i] |= static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(f[4 * i + k]))) << (8 * k);
+      }
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  }
 };
 
 __device__ __forceinline__ void move_geom(const MoveGeom& g, const int64_t (&bid)[3], int rows, int cols,
@@ -460,8 +502,10 @@ __device__ __forceinline__ void move_geom(const MoveGeom& g, const int64_t (&bid
   nc = lc <= 0 ? 0 : (lc < cols ? static_cast<int>(lc) : cols);
 }
 
-template <bool TRANSPOSE>
+template <int EB, bool TRANSPOSE>
 __global__ void __launch_bounds__(kTileThreads) tile_move(const __grid_constant__ MoveArgs p) {
+  using V = Vec16<EB>;
+  constexpr int kN = V::n;
   extern __shared__ float sm[];
   griddep_launch_dependents();
   griddep_wait();
@@ -471,28 +515,28 @@ __global__ void __launch_bounds__(kTileThreads) tile_move(const __grid_constant_
   int nr, nc;
   move_geom(p.g_in, bid, R, C, base, nr, nc);
   {
-    // loaded tile: float4 column c4 of rows r, r + rs, ...; up to 4 in flight
-    const int c4 = threadIdx.x & ((1 << p.lc4) - 1);
-    const int rs = kTileThreads >> p.lc4;
-    const bool col_in = 4 * c4 < nc;
-    const float4* g = reinterpret_cast<const float4*>(p.in + base) + c4;
-    const int64_t row4 = p.g_in.row >> 2;
-    for (int r = threadIdx.x >> p.lc4; r < R; r += 4 * rs) {
-      float4 v[4];
+    // loaded tile: vector column cv of rows r, r + rs, ...; up to 4 in flight
+    const int cv = threadIdx.x & ((1 << p.lc) - 1);
+    const int rs = kTileThreads >> p.lc;
+    const bool col_in = kN * cv < nc;
+    const uint4* g = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.in) + base * EB) + cv;
+    const int64_t rowv = p.g_in.row / kN;
+    for (int r = threadIdx.x >> p.lc; r < R; r += 4 * rs) {
+      uint4 v[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int ru = r + u * rs;
-        v[u] = (col_in && ru < nr) ? __ldg(g + ru * row4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[u] = (col_in && ru < nr) ? __ldg(g + ru * rowv) : make_uint4(0u, 0u, 0u, 0u);
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int ru = r + u * rs;
         if (ru < R) {
-          float* d = sm + ru * sp + 4 * c4;
-          d[0] = v[u].x;
-          d[1] = v[u].y;
-          d[2] = v[u].z;
-          d[3] = v[u].w;
+          float f[kN];
+          V::unpack(v[u], f);
+          float* d = sm + ru * sp + kN * cv;
+#pragma unroll
+          for (int k = 0; k < kN; ++k) d[k] = f[k];
         }
       }
     }
@@ -500,27 +544,29 @@ __global__ void __launch_bounds__(kTileThreads) tile_move(const __grid_constant_
   __syncthreads();
   const int OR = TRANSPOSE ? C : R, OC = TRANSPOSE ? R : C;
   move_geom(p.g_out, bid, OR, OC, base, nr, nc);
-  const int c4 = threadIdx.x & ((1 << p.lo4) - 1);
-  if (4 * c4 >= nc) return;
-  const int rs = kTileThreads >> p.lo4;
-  float4* g = reinterpret_cast<float4*>(p.out + base) + c4;
-  const int64_t row4 = p.g_out.row >> 2;
-  for (int r = threadIdx.x >> p.lo4; r < nr; r += rs) {
-    float4 o;
+  const int cv = threadIdx.x & ((1 << p.lo) - 1);
+  if (kN * cv >= nc) return;
+  const int rs = kTileThreads >> p.lo;
+  uint4* g = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) + base * EB) + cv;
+  const int64_t rowv = p.g_out.row / kN;
+  for (int r = threadIdx.x >> p.lo; r < nr; r += rs) {
+    float f[kN];
     if (TRANSPOSE) {
-      const float* s = sm + 4 * c4 * sp + r;  // output (r, 4 c4 + k) = loaded (4 c4 + k, r)
-      o = make_float4(s[0], s[sp], s[2 * sp], s[3 * sp]);
+      const float* s = sm + kN * cv * sp + r;  // output (r, kN cv + k) = loaded (kN cv + k, r)
+#pragma unroll
+      for (int k = 0; k < kN; ++k) f[k] = s[k * sp];
     } else {
-      const float* s = sm + r * sp + 4 * c4;
-      o = make_float4(s[0], s[1], s[2], s[3]);
+      const float* s = sm + r * sp + kN * cv;
+#pragma unroll
+      for (int k = 0; k < kN; ++k) f[k] = s[k];
     }
-    g[r * row4] = o;
+    g[r * rowv] = V::pack(f);
   }
 }
 
-// The move kernel's arguments when the program is a plain f32 row-tile load
-// and store (optionally transposed) that it can run; false otherwise.
-bool plan_move(const TileArgs& a, MoveArgs& m, bool& transpose) {
+// The move kernel's arguments when the program is a plain row-tile load and
+// store (optionally transposed) that it can run; false otherwise.
+bool plan_move(const TileArgs& a, MoveArgs& m, bool& transpose, int& eb) {
   if (a.n_ops != 2 || a.ops[0].kind != kTLoad || a.ops[1].kind != kTStore) return false;
   const TileOp &ld = a.ops[0], &st = a.ops[1];
   const TileVal& v = a.vals[ld.dst];
@@ -529,7 +575,9 @@ bool plan_move(const TileArgs& a, MoveArgs& m, bool& transpose) {
   transpose = st.code == 1 && st.b == ld.dst && st.perm[0] == 0 && st.perm[1] == 1 && st.perm[2] == 3 &&
               st.perm[3] == 2;
   if (!copy && !transpose) return false;
-  if (a.elem[ld.arg] != kF32 || a.elem[st.arg] != kF32) return false;
+  if (a.elem[ld.arg] != a.elem[st.arg]) return false;
+  eb = a.elem[ld.arg] == kF32 ? 4 : a.elem[ld.arg] == kBF16 ? 2 : 1;
+  const int vn = 16 / eb;  // elements per 16-byte vector
   if (v.shape[0] != 1 || v.shape[1] != 1 || o.shape[0] != 1 || o.shape[1] != 1) return false;
   const int R = v.shape[2], C = v.shape[3];
   const int OC = transpose ? R : C;
@@ -538,15 +586,15 @@ bool plan_move(const TileArgs& a, MoveArgs& m, bool& transpose) {
     while ((1 << l) < x) ++l;
     return (1 << l) == x ? l : -1;
   };
-  if (R % 4 || C % 4) return false;
-  const int lc4 = log2_of(C / 4), lo4 = log2_of(OC / 4);
-  if (lc4 < 0 || lo4 < 0 || C / 4 > kTileThreads || OC / 4 > kTileThreads) return false;
+  if (C % vn || OC % vn) return false;
+  const int lc = log2_of(C / vn), lo = log2_of(OC / vn);
+  if (lc < 0 || lo < 0 || C / vn > kTileThreads || OC / vn > kTileThreads) return false;
   const int sp = C % 2 == 0 ? C + 1 : C;
   if (static_cast<int64_t>(R) * sp > 12 * 1024) return false;  // 48 KiB of shared memory
   if ((reinterpret_cast<uintptr_t>(a.arr[ld.arg]) | reinterpret_cast<uintptr_t>(a.arr[st.arg])) & 15) return false;
   auto geom = [&](const TileOp& op, const TileVal& t, MoveGeom& g) {
     const int32_t* ext = a.shape[op.arg];
-    if (ext[3] % 4) return false;  // rows of whole float4s
+    if (ext[3] % vn) return false;  // rows of whole 16-byte vectors
     int64_t astride[kTileRank], run = 1;
     for (int d = kTileRank - 1; d >= 0; --d) {
       astride[d] = run;
@@ -574,12 +622,12 @@ bool plan_move(const TileArgs& a, MoveArgs& m, bool& transpose) {
     return true;
   };
   if (!geom(ld, v, m.g_in) || !geom(st, o, m.g_out)) return false;
-  m.in = static_cast<const float*>(a.arr[ld.arg]);
-  m.out = static_cast<float*>(a.arr[st.arg]);
+  m.in = a.arr[ld.arg];
+  m.out = a.arr[st.arg];
   m.R = R;
   m.C = C;
-  m.lc4 = lc4;
-  m.lo4 = lo4;
+  m.lc = lc;
+  m.lo = lo;
   m.sp = sp;
   m.bid0_begin = a.bid0_begin;
   return true;
@@ -594,12 +642,15 @@ cudaError_t launch_tile(const TileArgs& a, cudaStream_t stream) {
   {
     MoveArgs m;
     bool transpose = false;
-    if (plan_move(a, m, transpose)) {
+    int eb = 4;
+    if (plan_move(a, m, transpose, eb)) {
       const size_t msmem = static_cast<size_t>(m.R) * m.sp * sizeof(float);
       PdlLaunch launch(dim3(static_cast<unsigned>(gx), static_cast<unsigned>(a.grid[1]),
                             static_cast<unsigned>(a.grid[2])),
                        dim3(kTileThreads), msmem, stream);
-      return transpose ? launch(tile_move<true>, m) : launch(tile_move<false>, m);
+      if (eb == 4) return transpose ? launch(tile_move<4, true>, m) : launch(tile_move<4, false>, m);
+      if (eb == 2) return transpose ? launch(tile_move<2, true>, m) : launch(tile_move<2, false>, m);
+      return transpose ? launch(tile_move<1, true>, m) : launch(tile_move<1, false>, m);
     }
   }
   const size_t smem = static_cast<size_t>(a.smem_floats) * sizeof(float);
