@@ -64,6 +64,7 @@ NCU_TRAFFIC_BYTES: dict[str, float] = {
     "add": 33_561_088 + 10_496,
     "softmax": 33_566_464 + 343_552,
     "sharded_matmul": 6_210_000_000 + 1_060_000_000,
+    "transpose": 134_227_712 + 88_921_088,
 }
 
 
