@@ -124,6 +124,37 @@ def test_ew_interpreter_program():
     np.testing.assert_allclose(host(d), ref[3], rtol=2e-6, atol=1e-6)
 
 
+@xt.kernel
+def ew_int8(q, r, y, yq, trow, col):
+    i = xt.bid(0)
+    a = xt.astype(xt.load(q, index=(i, 0), shape=(trow, col)), dtype=xt.float32)
+    b = xt.load(r, index=(i, 0), shape=(trow, col))
+    t = a * b + a
+    xt.store(y, index=(i, 0), tile=t)
+    xt.store(yq, index=(i, 0), tile=xt.astype(t, dtype=xt.int8))
+
+
+def test_ew_interpreter_int8_casts_tail_and_shards_bit_exact():
+    # 7 x 13 = 91 elements: 22 groups of four (4-byte int8 and 16-byte f32
+    # accesses) and a tail of 3; a bid0 shard starting at element 13 runs the
+    # one-element interpreter.  ftoi rounds half to even and saturates.
+    g = gen(29)
+    q = torch.randint(-128, 128, (7, 13), generator=g, dtype=torch.int8)
+    r = torch.randn(7, 13, generator=g) * 3
+    y = torch.empty(7, 13, device=DEV)
+    yq = torch.zeros(7, 13, dtype=torch.int8, device=DEV)
+    m = xt.run(ew_int8, args=(q.to(DEV), r.to(DEV), y, yq, 1, 13), grid=(7, 1, 1))
+    assert m.plan()["family"] == "ew"
+    ref = oracle(m, [q, r, torch.zeros(7, 13), torch.zeros(7, 13, dtype=torch.int8)])
+    assert np.array_equal(host(y).view(np.uint32), ref[2].view(np.uint32))
+    assert np.array_equal(host(yq), ref[3])
+    y2 = torch.full((7, 13), float("nan"), device=DEV)
+    yq2 = torch.zeros(7, 13, dtype=torch.int8, device=DEV)
+    for lo, hi in [(0, 1), (1, 7)]:
+        xt.launch(m, q.to(DEV), r.to(DEV), y2, yq2, bid0_range=(lo, hi))
+    assert torch.equal(y, y2) and torch.equal(yq, yq2)
+
+
 # --------------------------------------------------------------- softmax
 @xt.kernel
 def softmax_rows(inp, out, trow, col):
@@ -166,13 +197,16 @@ def row_stats(x, y, mx, trow, col):
     xt.store(mx, index=(i, 0), tile=xt.reciprocal(xt.sum(t, axis=1)))
 
 
-def test_row_program_interpreter():
-    x = torch.randn(96, 200, generator=gen(4)) + 3
-    y = torch.empty(96, 200, device=DEV)
-    mx = torch.empty(96, 1, device=DEV)
-    m = xt.run(row_stats, args=(x.to(DEV), y, mx, 32, 200), grid=(3, 1, 1))
+@pytest.mark.parametrize("rows,cols", [(96, 200), (64, 1024), (50, 37), (33, 128)])
+def test_row_program_interpreter(rows, cols):
+    # cols a multiple of 4: row registers in shared memory, float4 accesses;
+    # 37 columns: the one-value-per-lane interpreter
+    x = torch.randn(rows, cols, generator=gen(4)) + 3
+    y = torch.empty(rows, cols, device=DEV)
+    mx = torch.empty(rows, 1, device=DEV)
+    m = xt.run(row_stats, args=(x.to(DEV), y, mx, 32, cols), grid=((rows + 31) // 32, 1, 1))
     assert m.plan()["family"] == "rows"
-    ref = oracle(m, [x, torch.zeros(96, 200), torch.zeros(96, 1)])
+    ref = oracle(m, [x, torch.zeros(rows, cols), torch.zeros(rows, 1)])
     np.testing.assert_array_equal(host(y), ref[1])
     np.testing.assert_allclose(host(mx), ref[2], rtol=1e-5)
 

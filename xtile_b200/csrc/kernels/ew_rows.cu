@@ -84,28 +84,137 @@ __device__ __forceinline__ void put(float (&r)[N], int idx, float v) {
   for (int k = 0; k < N; ++k) r[k] = (k == idx) ? v : r[k];
 }
 
+// The program for element i, registers held by predicated selection.
+__device__ __forceinline__ void ew_element(const EwArgs& p, int64_t i) {
+  float r[kEwRegs];
+#pragma unroll
+  for (int k = 0; k < kEwRegs; ++k) r[k] = 0.0f;
+  for (int pc = 0; pc < p.n_code; ++pc) {
+    const Instr ins = p.code[pc];
+    if (ins.op == kLoad) {
+      put(r, ins.dst, load_elem(p.in[ins.a], p.in_elem[ins.a], i));
+    } else if (ins.op == kStore) {
+      store_elem(p.out[ins.dst], p.out_elem[ins.dst], i, pick(r, ins.a));
+    } else if (ins.op == kAdd || ins.op == kSub || ins.op == kMul) {
+      put(r, ins.dst, binary_op(ins.op, pick(r, ins.a), pick(r, ins.b)));
+    } else {
+      put(r, ins.dst, unary_op(ins.op, pick(r, ins.a)));
+    }
+  }
+}
+
+// One element per thread: any alignment.
 __global__ void __launch_bounds__(kThreads) ew_program(const __grid_constant__ EwArgs p) {
   griddep_launch_dependents();
   griddep_wait();
   int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
   for (int64_t i = p.begin + static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < p.end;
-       i += stride) {
-    float r[kEwRegs];
+       i += stride)
+    ew_element(p, i);
+}
+
+// Four consecutive elements of an array as f32 values: one 16-, 8- or 4-byte
+// load (the array holds whole groups of four at 4-element aligned offsets).
+__device__ __forceinline__ float4 load4(const void* p, uint8_t e, int64_t i) {
+  if (e == kF32) return __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p) + i));
+  if (e == kBF16) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p) + i));
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                       __uint_as_float(u.y & 0xffff0000u));
+  }
+  const uint32_t w = __ldg(reinterpret_cast<const unsigned int*>(static_cast<const int8_t*>(p) + i));
+  return make_float4(static_cast<float>(static_cast<int8_t>(w)), static_cast<float>(static_cast<int8_t>(w >> 8)),
+                     static_cast<float>(static_cast<int8_t>(w >> 16)), static_cast<float>(static_cast<int8_t>(w >> 24)));
+}
+
+// store_elem's conversions for four consecutive elements, one store.
+__device__ __forceinline__ void store4(void* p, uint8_t e, int64_t i, float4 v) {
+  if (e == kF32) {
+    *reinterpret_cast<float4*>(static_cast<float*>(p) + i) = v;
+  } else if (e == kBF16) {
+    auto b = [](float x) { return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(x))); };
+    *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p) + i) =
+        make_uint2(b(v.x) | (b(v.y) << 16), b(v.z) | (b(v.w) << 16));
+  } else {
+    auto c = [](float x) { return static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(static_cast<int>(x)))); };
+    *reinterpret_cast<unsigned int*>(static_cast<int8_t*>(p) + i) =
+        c(v.x) | (c(v.y) << 8) | (c(v.z) << 16) | (c(v.w) << 24);
+  }
+}
+
+template <uint8_t OP>
+__device__ __forceinline__ float4 unary4_of(float4 x) {
+  return make_float4(unary_op(OP, x.x), unary_op(OP, x.y), unary_op(OP, x.z), unary_op(OP, x.w));
+}
+
+// unary_op on four values with one dispatch on the (warp-uniform) opcode
+__device__ __forceinline__ float4 unary4(uint8_t op, float4 x) {
+  switch (op & 0x7f) {
+    case kExp: return unary4_of<kExp>(x);
+    case kCos: return unary4_of<kCos>(x);
+    case kSin: return unary4_of<kSin>(x);
+    case kRecip: return unary4_of<kRecip>(x);
+    case kRsqrt: return unary4_of<kRsqrt>(x);
+    case kSigmoid: return unary4_of<kSigmoid>(x);
+    case kTanh: return unary4_of<kTanh>(x);
+    case kSilu: return unary4_of<kSilu>(x);
+    case kFtoi: return unary4_of<kFtoi>(x);
+    default: return x;
+  }
+}
+
+template <uint8_t OP>
+__device__ __forceinline__ float4 binary4_of(float4 x, float4 y) {
+  return make_float4(binary_op(OP, x.x, y.x), binary_op(OP, x.y, y.y), binary_op(OP, x.z, y.z),
+                     binary_op(OP, x.w, y.w));
+}
+
+__device__ __forceinline__ float4 binary4(uint8_t op, float4 x, float4 y) {
+  switch (op & 0x7f) {
+    case kAdd: case kBcastAdd: return binary4_of<kAdd>(x, y);
+    case kSub: case kBcastSub: return binary4_of<kSub>(x, y);
+    default: return binary4_of<kMul>(x, y);
+  }
+}
+
+// Four elements per thread per pass, for arrays whose range starts at a
+// multiple of 4 elements on aligned pointers.  The program's registers live
+// in shared memory, one float4 slot per register and thread, so an operand is
+// one 16-byte shared load at a computed address instead of a predicated
+// selection over every register.  The program's leading loads (n_lead of
+// them) are all issued before any of them is written to its register, so a
+// thread has every input's 16 bytes in flight at once.  The last n % 4
+// elements run through ew_element.
+__global__ void __launch_bounds__(kThreads) ew_program_v4(const __grid_constant__ EwArgs p, int n_lead) {
+  __shared__ float4 rf[kEwRegs * kThreads];
+  float4* my = rf + threadIdx.x;  // register k of this thread: my[k * kThreads]
+  griddep_launch_dependents();
+  griddep_wait();
+  const int64_t n4 = (p.end - p.begin) / 4;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; v < n4; v += stride) {
+    const int64_t i = p.begin + 4 * v;
+    float4 t[kMaxSlots];
 #pragma unroll
-    for (int k = 0; k < kEwRegs; ++k) r[k] = 0.0f;
-    for (int pc = 0; pc < p.n_code; ++pc) {
+    for (int j = 0; j < kMaxSlots; ++j)
+      if (j < n_lead) t[j] = load4(p.in[p.code[j].a], p.in_elem[p.code[j].a], i);
+#pragma unroll
+    for (int j = 0; j < kMaxSlots; ++j)
+      if (j < n_lead) my[p.code[j].dst * kThreads] = t[j];
+    for (int pc = n_lead; pc < p.n_code; ++pc) {
       const Instr ins = p.code[pc];
       if (ins.op == kLoad) {
-        put(r, ins.dst, load_elem(p.in[ins.a], p.in_elem[ins.a], i));
+        my[ins.dst * kThreads] = load4(p.in[ins.a], p.in_elem[ins.a], i);
       } else if (ins.op == kStore) {
-        store_elem(p.out[ins.dst], p.out_elem[ins.dst], i, pick(r, ins.a));
+        store4(p.out[ins.dst], p.out_elem[ins.dst], i, my[ins.a * kThreads]);
       } else if (ins.op == kAdd || ins.op == kSub || ins.op == kMul) {
-        put(r, ins.dst, binary_op(ins.op, pick(r, ins.a), pick(r, ins.b)));
+        my[ins.dst * kThreads] = binary4(ins.op, my[ins.a * kThreads], my[ins.b * kThreads]);
       } else {
-        put(r, ins.dst, unary_op(ins.op, pick(r, ins.a)));
+        my[ins.dst * kThreads] = unary4(ins.op, my[ins.a * kThreads]);
       }
     }
   }
+  if (blockIdx.x == 0 && threadIdx.x < (p.end - p.begin) - 4 * n4) ew_element(p, p.begin + 4 * n4 + threadIdx.x);
 }
 
 // ---------------------------------------------------------------------------
@@ -292,6 +401,87 @@ __global__ void __launch_bounds__(kThreads) rows_program(const __grid_constant__
   }
 }
 
+// Row programs on rows of a multiple of 4 columns at 16-byte aligned rows:
+// one warp per row as above, lane l holding float4 chunks l, l + 32, ... of
+// each row register, but the row registers live in shared memory (one float4
+// slot per chunk, lane and register), so an operand is read at a computed
+// address rather than selected out of every register, and the kernel needs
+// few registers: the interpreter above holds up to 3 x 32 row values plus
+// temporaries per lane (224 registers at 1024 columns, one CTA per SM).
+// Scalar registers stay in registers.  Four rows per CTA; the launch bound
+// asks for four CTAs per SM (without a minimum ptxas held the 8-chunk kernel
+// to 32 registers and spilled).
+constexpr int kRowV4Threads = 128;
+
+template <int PL4>  // float4 chunks per lane: row length <= 128 * PL4
+__global__ void __launch_bounds__(kRowV4Threads, 4) rows_program_v4(const __grid_constant__ RowArgs p) {
+  extern __shared__ float4 row_rf[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t row = p.row_begin + static_cast<int64_t>(blockIdx.x) * (kRowV4Threads / 32) + warp;
+  griddep_launch_dependents();
+  if (row >= p.row_end) return;
+  griddep_wait();
+  float4* rf = row_rf + warp * (p.n_vregs * PL4 * 32) + lane;  // register k, chunk j: rf[(k * PL4 + j) * 32]
+  const int64_t c4n = p.cols >> 2;
+  float s[kRowS];
+#pragma unroll
+  for (int k = 0; k < kRowS; ++k) s[k] = 0.0f;
+  for (int pc = 0; pc < p.n_code; ++pc) {
+    const Instr ins = p.code[pc];
+    const uint8_t op = ins.op & 0x7f;
+    const bool scalar = ins.op & 0x80;
+    if (op == kLoad) {
+      const float4* src = reinterpret_cast<const float4*>(p.in[ins.a] + row * p.cols);
+      float4 t[PL4];
+#pragma unroll
+      for (int j = 0; j < PL4; ++j) {
+        const int c = j * 32 + lane;
+        t[j] = c < c4n ? __ldg(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int j = 0; j < PL4; ++j) rf[(ins.dst * PL4 + j) * 32] = t[j];
+    } else if (op == kLoadScalar) {
+      put(s, ins.dst, __ldg(p.in[ins.a] + row));
+    } else if (op == kStore) {
+      float4* dst = reinterpret_cast<float4*>(p.out[ins.dst] + row * p.cols);
+#pragma unroll
+      for (int j = 0; j < PL4; ++j) {
+        const int c = j * 32 + lane;
+        if (c < c4n) dst[c] = rf[(ins.a * PL4 + j) * 32];
+      }
+    } else if (op == kStoreScalar) {
+      if (lane == 0) p.out[ins.dst][row] = pick(s, ins.a);
+    } else if (op == kRowMax || op == kRowSum) {
+      float acc = op == kRowMax ? -INFINITY : 0.0f;
+#pragma unroll
+      for (int j = 0; j < PL4; ++j) {
+        if (j * 32 + lane < c4n) {
+          const float4 x = rf[(ins.a * PL4 + j) * 32];
+          acc = op == kRowMax ? fmaxf(fmaxf(fmaxf(acc, x.x), fmaxf(x.y, x.z)), x.w)
+                              : __fadd_rn(acc, __fadd_rn(__fadd_rn(x.x, x.y), __fadd_rn(x.z, x.w)));
+        }
+      }
+      put(s, ins.dst, op == kRowMax ? warp_max(acc) : warp_sum(acc));
+    } else if (scalar) {
+      const float a = pick(s, ins.a);
+      put(s, ins.dst, (op == kAdd || op == kSub || op == kMul) ? binary_op(op, a, pick(s, ins.b))
+                                                               : unary_op(op, a));
+    } else if (op == kBcastAdd || op == kBcastSub || op == kBcastMul) {
+      const float b = pick(s, ins.b);
+      const float4 b4 = make_float4(b, b, b, b);
+#pragma unroll
+      for (int j = 0; j < PL4; ++j) rf[(ins.dst * PL4 + j) * 32] = binary4(op, rf[(ins.a * PL4 + j) * 32], b4);
+    } else if (op == kAdd || op == kSub || op == kMul) {
+#pragma unroll
+      for (int j = 0; j < PL4; ++j)
+        rf[(ins.dst * PL4 + j) * 32] = binary4(op, rf[(ins.a * PL4 + j) * 32], rf[(ins.b * PL4 + j) * 32]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < PL4; ++j) rf[(ins.dst * PL4 + j) * 32] = unary4(op, rf[(ins.a * PL4 + j) * 32]);
+    }
+  }
+}
+
 int grid_for(int64_t work_items, int per_block, int max_blocks) {
   int64_t b = (work_items + per_block - 1) / per_block;
   if (b < 1) b = 1;
@@ -335,6 +525,19 @@ cudaError_t launch_ew(const EwArgs& a, cudaStream_t stream) {
       }
     }
   }
+  // vectorised interpreter: a range starting at a multiple of 4 elements on
+  // pointers aligned to 4 elements of their type
+  bool v4 = a.begin % 4 == 0 && a.n_code <= kMaxInstr;
+  for (int k = 0; k < a.n_in && v4; ++k)
+    v4 = reinterpret_cast<uintptr_t>(a.in[k]) % (a.in_elem[k] == kF32 ? 16 : a.in_elem[k] == kBF16 ? 8 : 4) == 0;
+  for (int k = 0; k < a.n_out && v4; ++k)
+    v4 = reinterpret_cast<uintptr_t>(a.out[k]) % (a.out_elem[k] == kF32 ? 16 : a.out_elem[k] == kBF16 ? 8 : 4) == 0;
+  if (v4) {
+    int n_lead = 0;
+    while (n_lead < a.n_code && n_lead < kMaxSlots && a.code[n_lead].op == kLoad) ++n_lead;
+    const int64_t n4 = n / 4;
+    return PdlLaunch(grid_for(n4 > 0 ? n4 : 1, kThreads, max_blocks), kThreads, 0, stream)(ew_program_v4, a, n_lead);
+  }
   return PdlLaunch(grid_for(n, kThreads, max_blocks), kThreads, 0, stream)(ew_program, a);
 }
 
@@ -359,6 +562,24 @@ cudaError_t launch_rows(const RowArgs& a, cudaStream_t stream) {
     if (chunks <= 4) return go(softmax_rows_vec4<4, true>, softmax_rows_vec4<4, false>, 4);
     if (chunks <= 8) return go(softmax_rows_vec4<8, true>, softmax_rows_vec4<8, false>, 8);
     return go(softmax_rows_vec4<16, true>, softmax_rows_vec4<16, false>, 16);
+  }
+  bool v4 = a.cols % 4 == 0 && a.n_vregs >= 1;
+  for (int k = 0; k < kMaxSlots && v4; ++k) {
+    if (a.in[k] && !a.in_scalar[k]) v4 = (reinterpret_cast<uintptr_t>(a.in[k]) & 15) == 0;
+    if (v4 && a.out[k] && !a.out_scalar[k]) v4 = (reinterpret_cast<uintptr_t>(a.out[k]) & 15) == 0;
+  }
+  if (v4) {
+    const int64_t pl4 = (a.cols / 4 + 31) / 32;
+    const int rpb = kRowV4Threads / 32;
+    const int vblocks = static_cast<int>((rows + rpb - 1) / rpb);
+    auto go = [&](auto kernel, int pl4c) {
+      const size_t smem = static_cast<size_t>(rpb) * a.n_vregs * pl4c * 32 * sizeof(float4);
+      return PdlLaunch(vblocks, kRowV4Threads, smem, stream)(kernel, a);
+    };
+    if (pl4 <= 1) return go(rows_program_v4<1>, 1);
+    if (pl4 <= 2) return go(rows_program_v4<2>, 2);
+    if (pl4 <= 4) return go(rows_program_v4<4>, 4);
+    if (pl4 <= 8) return go(rows_program_v4<8>, 8);
   }
   const int64_t pl = (a.cols + 31) / 32;
   PdlLaunch launch(blocks, kThreads, 0, stream);
