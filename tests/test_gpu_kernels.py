@@ -197,10 +197,10 @@ def row_stats(x, y, mx, trow, col):
     xt.store(mx, index=(i, 0), tile=xt.reciprocal(xt.sum(t, axis=1)))
 
 
-@pytest.mark.parametrize("rows,cols", [(96, 200), (64, 1024), (50, 37), (33, 128)])
+@pytest.mark.parametrize("rows,cols", [(96, 200), (64, 1024), (50, 37), (33, 128), (40, 2048), (20, 1531)])
 def test_row_program_interpreter(rows, cols):
-    # cols a multiple of 4: row registers in shared memory, float4 accesses;
-    # 37 columns: the one-value-per-lane interpreter
+    # cols a multiple of 4: float4 accesses; 37 and 1531 columns: element
+    # accesses with a guard per element (partial last chunk of every row)
     x = torch.randn(rows, cols, generator=gen(4)) + 3
     y = torch.empty(rows, cols, device=DEV)
     mx = torch.empty(rows, 1, device=DEV)

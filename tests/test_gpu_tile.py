@@ -364,3 +364,38 @@ def test_data_movement_transpose_bf16_int8_bit_exact(dtype, shape, tile):
     grid = (shape[0], -(-shape[1] // tm), -(-shape[2] // tn))
     xt.run(transpose3, args=(x.to(DEV), y, tm, tn), grid=grid)
     assert torch.equal(y.cpu(), x.transpose(1, 2))
+
+
+@xt.kernel
+def row_stats_tiles(x, s, mx, tm, tn):
+    i, j = xt.bid(0), xt.bid(1)
+    t = xt.load(x, index=(i, j), shape=(tm, tn))
+    xt.store(s, index=(i, j), tile=xt.sum(t, axis=1))
+    xt.store(mx, index=(i, j), tile=xt.max(t, axis=1))
+
+
+def test_tile_reductions_both_axes_with_nans():
+    # 16 x 64 tiles reduced along each axis; a NaN in a column or row makes
+    # its max NaN and its sum NaN, as in the oracle
+    x = torch.randn(128, 256, generator=gen(30)) * 2
+    x[5, 7] = float("nan")
+    x[70, 200] = float("nan")
+    s = torch.empty(128, 4, device=DEV)
+    mx = torch.empty(128, 4, device=DEV)
+    m = xt.run(row_stats_tiles, args=(x.to(DEV), s, mx, 16, 64), grid=(8, 4, 1))
+    assert m.plan()["family"] == "tile"
+    _, ref_s, ref_m = oracle(m, [x, torch.zeros(128, 4), torch.zeros(128, 4)])
+    assert np.array_equal(host(mx), ref_m, equal_nan=True)
+    got = host(s)
+    assert np.array_equal(np.isnan(got), np.isnan(ref_s))
+    ok = ~np.isnan(ref_s)
+    assert np.all(np.abs(got[ok] - ref_s[ok]) <= 1e-6 * np.abs(ref_s[ok]) + 1e-6)
+    cs = torch.empty(8, 256, device=DEV)
+    cm = torch.empty(8, 256, device=DEV)
+    m = xt.run(col_stats, args=(x.to(DEV), cs, cm, 16, 64), grid=(8, 4, 1))
+    _, ref_s, ref_m = oracle(m, [x, torch.zeros(8, 256), torch.zeros(8, 256)])
+    assert np.array_equal(host(cm), ref_m, equal_nan=True)
+    got = host(cs)
+    ok = ~np.isnan(ref_s)
+    assert np.array_equal(np.isnan(got), ~ok)
+    assert np.all(np.abs(got[ok] - ref_s[ok]) <= 1e-6 * np.abs(ref_s[ok]) + 1e-6)

@@ -298,131 +298,35 @@ __global__ void __launch_bounds__(kThreads, CHUNKS <= 8 ? 1 : 3) softmax_rows_ve
 }
 
 // ---------------------------------------------------------------------------
-// rows: register-program interpreter.  Row registers hold PER_LANE values per
-// lane (element j*32 + lane); scalar registers hold one value per row.
+// rows: register-program interpreter
 // ---------------------------------------------------------------------------
-constexpr int kRowV = 3;
 constexpr int kRowS = 8;
 
-template <int PL>
-__device__ __forceinline__ void get_row(const float (&v)[kRowV][PL], int idx, float (&out)[PL]) {
-#pragma unroll
-  for (int k = 0; k < kRowV; ++k) {
-    const bool hit = k == idx;
-#pragma unroll
-    for (int j = 0; j < PL; ++j) out[j] = hit ? v[k][j] : out[j];
-  }
-}
+// One warp per row; lane l holds the float4 chunks l, l + 32, ... (elements
+// 4c .. 4c + 3 of chunk c) of each row register.  The row registers live in
+// shared memory, one float4 slot per register, chunk and lane, so an operand
+// is read at a computed address rather than selected out of every register;
+// scalar registers (one value per row) stay in registers.  VEC: rows of a
+// multiple of 4 columns at 16-byte aligned addresses, accessed as float4;
+// otherwise element by element with a guard on each element.  A first form
+// held the row registers in registers (3 x 32 values per lane at 1024
+// columns, 224 registers, one CTA per SM) and measured 684 GB/s on a
+// max-centre-square program over 128 MiB; this one 4297 GB/s.  The launch
+// bound asks for four CTAs per SM (without a minimum ptxas held the 8-chunk
+// kernel to 32 registers and spilled).
+constexpr int kRowMaxThreads = 128;
 
-template <int PL>
-__device__ __forceinline__ void set_row(float (&v)[kRowV][PL], int idx, const float (&in)[PL]) {
-#pragma unroll
-  for (int k = 0; k < kRowV; ++k) {
-    const bool hit = k == idx;
-#pragma unroll
-    for (int j = 0; j < PL; ++j) v[k][j] = hit ? in[j] : v[k][j];
-  }
-}
-
-template <int PL>
-__global__ void __launch_bounds__(kThreads) rows_program(const __grid_constant__ RowArgs p) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = p.row_begin + static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5);
-  griddep_launch_dependents();
-  if (row >= p.row_end) return;
-  griddep_wait();
-  float v[kRowV][PL];
-  float s[kRowS];
-#pragma unroll
-  for (int k = 0; k < kRowV; ++k)
-#pragma unroll
-    for (int j = 0; j < PL; ++j) v[k][j] = 0.0f;
-#pragma unroll
-  for (int k = 0; k < kRowS; ++k) s[k] = 0.0f;
-
-  for (int pc = 0; pc < p.n_code; ++pc) {
-    const Instr ins = p.code[pc];
-    const uint8_t op = ins.op & 0x7f;
-    const bool scalar = ins.op & 0x80;
-    float t[PL], u[PL];
-#pragma unroll
-    for (int j = 0; j < PL; ++j) t[j] = u[j] = 0.0f;
-    if (op == kLoad) {
-      const float* src = p.in[ins.a] + row * p.cols;
-#pragma unroll
-      for (int j = 0; j < PL; ++j) {
-        int64_t c = static_cast<int64_t>(j) * 32 + lane;
-        t[j] = c < p.cols ? __ldg(src + c) : 0.0f;
-      }
-      set_row(v, ins.dst, t);
-    } else if (op == kLoadScalar) {
-      put(s, ins.dst, __ldg(p.in[ins.a] + row));
-    } else if (op == kStore) {
-      float* dst = p.out[ins.dst] + row * p.cols;
-      get_row(v, ins.a, t);
-#pragma unroll
-      for (int j = 0; j < PL; ++j) {
-        int64_t c = static_cast<int64_t>(j) * 32 + lane;
-        if (c < p.cols) dst[c] = t[j];
-      }
-    } else if (op == kStoreScalar) {
-      if (lane == 0) p.out[ins.dst][row] = pick(s, ins.a);
-    } else if (op == kRowMax || op == kRowSum) {
-      get_row(v, ins.a, t);
-      float acc = op == kRowMax ? -INFINITY : 0.0f;
-#pragma unroll
-      for (int j = 0; j < PL; ++j) {
-        int64_t c = static_cast<int64_t>(j) * 32 + lane;
-        if (c < p.cols) acc = op == kRowMax ? fmaxf(acc, t[j]) : __fadd_rn(acc, t[j]);
-      }
-      put(s, ins.dst, op == kRowMax ? warp_max(acc) : warp_sum(acc));
-    } else if (scalar) {
-      const float a = pick(s, ins.a);
-      put(s, ins.dst, (op == kAdd || op == kSub || op == kMul) ? binary_op(op, a, pick(s, ins.b))
-                                                               : unary_op(op, a));
-    } else if (op == kBcastAdd || op == kBcastSub || op == kBcastMul) {
-      get_row(v, ins.a, t);
-      const float b = pick(s, ins.b);
-#pragma unroll
-      for (int j = 0; j < PL; ++j) t[j] = binary_op(op, t[j], b);
-      set_row(v, ins.dst, t);
-    } else if (op == kAdd || op == kSub || op == kMul) {
-      get_row(v, ins.a, t);
-      get_row(v, ins.b, u);
-#pragma unroll
-      for (int j = 0; j < PL; ++j) t[j] = binary_op(op, t[j], u[j]);
-      set_row(v, ins.dst, t);
-    } else {
-      get_row(v, ins.a, t);
-#pragma unroll
-      for (int j = 0; j < PL; ++j) t[j] = unary_op(op, t[j]);
-      set_row(v, ins.dst, t);
-    }
-  }
-}
-
-// Row programs on rows of a multiple of 4 columns at 16-byte aligned rows:
-// one warp per row as above, lane l holding float4 chunks l, l + 32, ... of
-// each row register, but the row registers live in shared memory (one float4
-// slot per chunk, lane and register), so an operand is read at a computed
-// address rather than selected out of every register, and the kernel needs
-// few registers: the interpreter above holds up to 3 x 32 row values plus
-// temporaries per lane (224 registers at 1024 columns, one CTA per SM).
-// Scalar registers stay in registers.  Four rows per CTA; the launch bound
-// asks for four CTAs per SM (without a minimum ptxas held the 8-chunk kernel
-// to 32 registers and spilled).
-constexpr int kRowV4Threads = 128;
-
-template <int PL4>  // float4 chunks per lane: row length <= 128 * PL4
-__global__ void __launch_bounds__(kRowV4Threads, 4) rows_program_v4(const __grid_constant__ RowArgs p) {
+template <int PL4, bool VEC>  // float4 chunks per lane: row length <= 128 * PL4
+__global__ void __launch_bounds__(kRowMaxThreads, 4) rows_program(const __grid_constant__ RowArgs p) {
   extern __shared__ float4 row_rf[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t row = p.row_begin + static_cast<int64_t>(blockIdx.x) * (kRowV4Threads / 32) + warp;
+  const int64_t row = p.row_begin + static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + warp;
   griddep_launch_dependents();
   if (row >= p.row_end) return;
   griddep_wait();
   float4* rf = row_rf + warp * (p.n_vregs * PL4 * 32) + lane;  // register k, chunk j: rf[(k * PL4 + j) * 32]
-  const int64_t c4n = p.cols >> 2;
+  const int64_t cols = p.cols, c4n = (cols + 3) >> 2;
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
   float s[kRowS];
 #pragma unroll
   for (int k = 0; k < kRowS; ++k) s[k] = 0.0f;
@@ -431,37 +335,62 @@ __global__ void __launch_bounds__(kRowV4Threads, 4) rows_program_v4(const __grid
     const uint8_t op = ins.op & 0x7f;
     const bool scalar = ins.op & 0x80;
     if (op == kLoad) {
-      const float4* src = reinterpret_cast<const float4*>(p.in[ins.a] + row * p.cols);
+      const float* src = p.in[ins.a] + row * cols;
       float4 t[PL4];
 #pragma unroll
       for (int j = 0; j < PL4; ++j) {
-        const int c = j * 32 + lane;
-        t[j] = c < c4n ? __ldg(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const int64_t c = j * 32 + lane;
+        if (VEC) {
+          t[j] = c < c4n ? __ldg(reinterpret_cast<const float4*>(src) + c) : zero;
+        } else {
+          const int64_t e = 4 * c;
+          t[j] = make_float4(e < cols ? __ldg(src + e) : 0.f, e + 1 < cols ? __ldg(src + e + 1) : 0.f,
+                             e + 2 < cols ? __ldg(src + e + 2) : 0.f, e + 3 < cols ? __ldg(src + e + 3) : 0.f);
+        }
       }
 #pragma unroll
       for (int j = 0; j < PL4; ++j) rf[(ins.dst * PL4 + j) * 32] = t[j];
     } else if (op == kLoadScalar) {
       put(s, ins.dst, __ldg(p.in[ins.a] + row));
     } else if (op == kStore) {
-      float4* dst = reinterpret_cast<float4*>(p.out[ins.dst] + row * p.cols);
+      float* dst = p.out[ins.dst] + row * cols;
 #pragma unroll
       for (int j = 0; j < PL4; ++j) {
-        const int c = j * 32 + lane;
-        if (c < c4n) dst[c] = rf[(ins.a * PL4 + j) * 32];
+        const int64_t c = j * 32 + lane;
+        if (c >= c4n) continue;
+        const float4 v = rf[(ins.a * PL4 + j) * 32];
+        if (VEC) {
+          reinterpret_cast<float4*>(dst)[c] = v;
+        } else {
+          const int64_t e = 4 * c;
+          dst[e] = v.x;
+          if (e + 1 < cols) dst[e + 1] = v.y;
+          if (e + 2 < cols) dst[e + 2] = v.z;
+          if (e + 3 < cols) dst[e + 3] = v.w;
+        }
       }
     } else if (op == kStoreScalar) {
       if (lane == 0) p.out[ins.dst][row] = pick(s, ins.a);
     } else if (op == kRowMax || op == kRowSum) {
-      float acc = op == kRowMax ? -INFINITY : 0.0f;
+      const bool mx = op == kRowMax;
+      const float pad = mx ? -INFINITY : 0.0f;  // elements past the row end
+      float acc = pad;
 #pragma unroll
       for (int j = 0; j < PL4; ++j) {
-        if (j * 32 + lane < c4n) {
-          const float4 x = rf[(ins.a * PL4 + j) * 32];
-          acc = op == kRowMax ? fmaxf(fmaxf(fmaxf(acc, x.x), fmaxf(x.y, x.z)), x.w)
-                              : __fadd_rn(acc, __fadd_rn(__fadd_rn(x.x, x.y), __fadd_rn(x.z, x.w)));
+        const int64_t c = j * 32 + lane;
+        if (c < c4n) {
+          float4 x = rf[(ins.a * PL4 + j) * 32];
+          if (!VEC) {
+            const int64_t e = 4 * c;
+            if (e + 1 >= cols) x.y = pad;
+            if (e + 2 >= cols) x.z = pad;
+            if (e + 3 >= cols) x.w = pad;
+          }
+          acc = mx ? fmaxf(fmaxf(fmaxf(acc, x.x), fmaxf(x.y, x.z)), x.w)
+                   : __fadd_rn(acc, __fadd_rn(__fadd_rn(x.x, x.y), __fadd_rn(x.z, x.w)));
         }
       }
-      put(s, ins.dst, op == kRowMax ? warp_max(acc) : warp_sum(acc));
+      put(s, ins.dst, mx ? warp_max(acc) : warp_sum(acc));
     } else if (scalar) {
       const float a = pick(s, ins.a);
       put(s, ins.dst, (op == kAdd || op == kSub || op == kMul) ? binary_op(op, a, pick(s, ins.b))
@@ -563,33 +492,27 @@ cudaError_t launch_rows(const RowArgs& a, cudaStream_t stream) {
     if (chunks <= 8) return go(softmax_rows_vec4<8, true>, softmax_rows_vec4<8, false>, 8);
     return go(softmax_rows_vec4<16, true>, softmax_rows_vec4<16, false>, 16);
   }
-  bool v4 = a.cols % 4 == 0 && a.n_vregs >= 1;
-  for (int k = 0; k < kMaxSlots && v4; ++k) {
-    if (a.in[k] && !a.in_scalar[k]) v4 = (reinterpret_cast<uintptr_t>(a.in[k]) & 15) == 0;
-    if (v4 && a.out[k] && !a.out_scalar[k]) v4 = (reinterpret_cast<uintptr_t>(a.out[k]) & 15) == 0;
+  bool vec = a.cols % 4 == 0;
+  for (int k = 0; k < kMaxSlots && vec; ++k) {
+    if (a.in[k] && !a.in_scalar[k]) vec = (reinterpret_cast<uintptr_t>(a.in[k]) & 15) == 0;
+    if (vec && a.out[k] && !a.out_scalar[k]) vec = (reinterpret_cast<uintptr_t>(a.out[k]) & 15) == 0;
   }
-  if (v4) {
-    const int64_t pl4 = (a.cols / 4 + 31) / 32;
-    const int rpb = kRowV4Threads / 32;
+  const int64_t pl4 = ((a.cols + 3) / 4 + 31) / 32;
+  const int nv = a.n_vregs > 0 ? a.n_vregs : 1;
+  auto go = [&](auto vec_kernel, auto any_kernel, int pl4c) {
+    // rows per CTA: four, two for 2048-column rows (48 KiB of row registers at most)
+    const int rpb = pl4c <= 8 ? 4 : 2;
     const int vblocks = static_cast<int>((rows + rpb - 1) / rpb);
-    auto go = [&](auto kernel, int pl4c) {
-      const size_t smem = static_cast<size_t>(rpb) * a.n_vregs * pl4c * 32 * sizeof(float4);
-      return PdlLaunch(vblocks, kRowV4Threads, smem, stream)(kernel, a);
-    };
-    if (pl4 <= 1) return go(rows_program_v4<1>, 1);
-    if (pl4 <= 2) return go(rows_program_v4<2>, 2);
-    if (pl4 <= 4) return go(rows_program_v4<4>, 4);
-    if (pl4 <= 8) return go(rows_program_v4<8>, 8);
-  }
-  const int64_t pl = (a.cols + 31) / 32;
-  PdlLaunch launch(blocks, kThreads, 0, stream);
-  if (pl <= 1) return launch(rows_program<1>, a);
-  if (pl <= 2) return launch(rows_program<2>, a);
-  if (pl <= 4) return launch(rows_program<4>, a);
-  if (pl <= 8) return launch(rows_program<8>, a);
-  if (pl <= 16) return launch(rows_program<16>, a);
-  if (pl <= 32) return launch(rows_program<32>, a);
-  return cudaErrorInvalidValue;  // the planner admits rows up to 1024
+    const size_t smem = static_cast<size_t>(rpb) * nv * pl4c * 32 * sizeof(float4);
+    PdlLaunch launch(vblocks, rpb * 32, smem, stream);
+    return vec ? launch(vec_kernel, a) : launch(any_kernel, a);
+  };
+  if (pl4 <= 1) return go(rows_program<1, true>, rows_program<1, false>, 1);
+  if (pl4 <= 2) return go(rows_program<2, true>, rows_program<2, false>, 2);
+  if (pl4 <= 4) return go(rows_program<4, true>, rows_program<4, false>, 4);
+  if (pl4 <= 8) return go(rows_program<8, true>, rows_program<8, false>, 8);
+  if (pl4 <= 16) return go(rows_program<16, true>, rows_program<16, false>, 16);
+  return cudaErrorInvalidValue;  // the planner admits rows up to 2048
 }
 
 }  // namespace dev

@@ -665,7 +665,6 @@ class Classifier {
     }
     if (p.code.size() > static_cast<size_t>(kMaxInstr)) unsupported("the program is too long");
     p.softmax = is_softmax_chain(p);
-    if (!p.softmax && C > 1024) unsupported("row programs other than softmax support rows up to 1024 elements");
     return p;
   }
 
