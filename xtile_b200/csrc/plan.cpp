@@ -226,7 +226,18 @@ class Classifier {
       }
       return lead;
     };
-    auto new_val = [&](int vid, const Type& t) -> uint8_t {
+    // Shared-memory slots: a value's slot is freed after its last reader and
+    // may then hold a later value that fits; an elementwise op may write its
+    // result into the slot of a same-shaped operand it reads for the last
+    // time (each element is read and written by the same thread at the same
+    // index).  A permute folded into a store gets no slot: nothing writes it.
+    struct Slot {
+      int32_t offset;
+      int64_t floats;
+    };
+    std::vector<Slot> free_slots;
+    std::map<int, Slot> val_slot;  // tile value index -> its slot
+    auto new_val = [&](int vid, const Type& t, int inplace = -1, bool no_slot = false) -> uint8_t {
       if (p.vals.size() == static_cast<size_t>(kTileMaxVals)) unsupported("the program has more than 16 tiles");
       if (t.elem != Elem::F32 && t.elem != Elem::I8 && t.elem != Elem::BF16) unsupported("unsupported element type");
       TileVal v{};
@@ -236,8 +247,30 @@ class Classifier {
       const int64_t inner = v.shape[3] % 2 == 0 ? v.shape[3] + 1 : v.shape[3];
       const int64_t s2 = inner, s1 = s2 * v.shape[2], s0 = s1 * v.shape[1];
       const int64_t floats = s0 * v.shape[0];
-      const int64_t offset = (static_cast<int64_t>(p.smem_floats) + 3) & ~int64_t{3};
-      if (offset + floats > kTileSmemFloats) unsupported("the program's tiles exceed 192 KiB of shared memory");
+      int64_t offset = -1;
+      if (no_slot) {
+        offset = 0;
+      } else if (inplace >= 0) {
+        const Slot sl = val_slot.at(inplace);
+        val_slot.erase(inplace);  // the operand's slot passes to this value
+        offset = sl.offset;
+        val_slot[static_cast<int>(p.vals.size())] = sl;
+      } else {
+        int best = -1;
+        for (size_t k = 0; k < free_slots.size(); ++k)
+          if (free_slots[k].floats >= floats && (best < 0 || free_slots[k].floats < free_slots[best].floats))
+            best = static_cast<int>(k);
+        if (best >= 0) {
+          offset = free_slots[best].offset;
+          val_slot[static_cast<int>(p.vals.size())] = free_slots[best];
+          free_slots.erase(free_slots.begin() + best);
+        } else {
+          offset = (static_cast<int64_t>(p.smem_floats) + 3) & ~int64_t{3};
+          if (offset + floats > kTileSmemFloats) unsupported("the program's tiles exceed 192 KiB of shared memory");
+          p.smem_floats = static_cast<int32_t>(offset + floats);
+          val_slot[static_cast<int>(p.vals.size())] = Slot{static_cast<int32_t>(offset), floats};
+        }
+      }
       v.stride[3] = 1;
       v.stride[2] = static_cast<int32_t>(s2);
       v.stride[1] = static_cast<int32_t>(s1);
@@ -245,7 +278,6 @@ class Classifier {
       v.numel = v.shape[0] * v.shape[1] * v.shape[2] * v.shape[3];
       v.offset = static_cast<int32_t>(offset);
       v.i8 = t.elem == Elem::I8;
-      p.smem_floats = static_cast<int32_t>(offset + floats);
       val_of[vid] = static_cast<int>(p.vals.size());
       p.vals.push_back(v);
       return static_cast<uint8_t>(p.vals.size() - 1);
@@ -286,6 +318,53 @@ class Classifier {
     };
     std::map<int, const Access*> store_at;
     for (const Access& a : stores_) store_at[a.op] = &a;
+    // Last reader of every value (op index).  A permute whose result only
+    // feeds one store is folded into that store below, so its operand is
+    // read at the store.
+    std::map<int, int> last_use, n_uses, user;
+    for (size_t i = 0; i < f_.ops.size(); ++i)
+      for (int o : f_.ops[i].operands) {
+        last_use[o] = static_cast<int>(i);
+        ++n_uses[o];
+        user[o] = static_cast<int>(i);
+      }
+    std::set<size_t> folded;  // permutes that become part of their store
+    struct Fold {
+      uint8_t src;
+      uint8_t perm[kTileRank];
+    };
+    std::map<int, Fold> fold_of;  // folded permute's value index -> its operand and permutation
+    for (size_t i = 0; i < f_.ops.size(); ++i) {
+      const Op& op = f_.ops[i];
+      if ((op.name != "xt.transpose" && op.name != "xt.permute") || op.results.empty()) continue;
+      const int r = op.results[0];
+      if (n_uses[r] == 1 && f_.ops[user[r]].name == "xt.store" && f_.ops[user[r]].operands[0] == r) {
+        folded.insert(i);
+        last_use[op.operands[0]] = std::max(last_use[op.operands[0]], user[r]);
+      }
+    }
+    // frees the slots of the tile values whose last reader is op i
+    auto release = [&](int i) {
+      for (auto& kv : val_of) {
+        auto it = last_use.find(kv.first);
+        const int last = it == last_use.end() ? -1 : it->second;
+        if (last <= i && val_slot.count(kv.second)) {
+          free_slots.push_back(val_slot.at(kv.second));
+          val_slot.erase(kv.second);
+        }
+      }
+    };
+    // an operand of op i whose slot the elementwise result may take over
+    auto inplace_of = [&](const Op& op, int i, std::initializer_list<int> operand_idx) -> int {
+      for (int k : operand_idx) {
+        const int o = op.operands[k];
+        auto it = val_of.find(o);
+        if (it == val_of.end() || last_use[o] != i || !val_slot.count(it->second)) continue;
+        if (op.operand_types[k].shape != op.result_types[0].shape) continue;
+        return it->second;
+      }
+      return -1;
+    };
     static const std::map<std::string, uint8_t> kUn = {
         {"xt.exp", kExp}, {"xt.cos", kCos}, {"xt.sin", kSin}, {"xt.reciprocal", kRecip}, {"xt.rsqrt", kRsqrt},
         {"xt.sigmoid", kSigmoid}, {"xt.tanh", kTanh}, {"xt.silu", kSilu}};
@@ -311,6 +390,13 @@ class Classifier {
         const Access& a = *store_at.at(static_cast<int>(i));
         t.kind = kTStore;
         t.a = val(op.operands[0]);
+        auto fo = fold_of.find(t.a);
+        if (fo != fold_of.end()) {
+          // the stored tile is a folded permute: read its operand through the permuted strides
+          t.code = 1;
+          t.b = fo->second.src;
+          for (int d = 0; d < kTileRank; ++d) t.perm[d] = fo->second.perm[d];
+        }
         t.arg = slot_of(a);
         set_coords(t, a);
       } else if (kUn.count(n) || n == "xt.itof" || n == "xt.ftoi") {
@@ -321,13 +407,13 @@ class Classifier {
         t.kind = kTUnary;
         t.code = n == "xt.itof" ? kItof : n == "xt.ftoi" ? kFtoi : kUn.at(n);
         t.a = val(op.operands[0]);
-        t.dst = new_val(op.results[0], op.result_types[0]);
+        t.dst = new_val(op.results[0], op.result_types[0], inplace_of(op, static_cast<int>(i), {0}));
       } else if (kBin.count(n)) {
         t.kind = kTBinary;
         t.code = kBin.at(n);
         t.a = val(op.operands[0]);
         t.b = val(op.operands[1]);
-        t.dst = new_val(op.results[0], op.result_types[0]);
+        t.dst = new_val(op.results[0], op.result_types[0], inplace_of(op, static_cast<int>(i), {0, 1}));
         const TileVal &va = p.vals[t.a], &vb = p.vals[t.b], &vd = p.vals[t.dst];
         for (int d = 0; d < kTileRank; ++d)
           if ((va.shape[d] != vd.shape[d] && va.shape[d] != 1) || (vb.shape[d] != vd.shape[d] && vb.shape[d] != 1))
@@ -372,45 +458,30 @@ class Classifier {
         for (int d = 0; d < kTileRank; ++d)
           t.perm[d] = static_cast<uint8_t>(d < lead ? d : lead + perm[d - lead]);
         t.a = val(op.operands[0]);
-        t.dst = new_val(op.results[0], op.result_types[0]);
+        const bool fold = folded.count(i) > 0;
+        t.dst = new_val(op.results[0], op.result_types[0], -1, fold);
         for (int d = 0; d < kTileRank; ++d)
           if (p.vals[t.dst].shape[d] != p.vals[t.a].shape[t.perm[d]])
             unsupported("the result shape must be the operand shape permuted");
+        if (fold) {
+          // no op: the one store of this value reads t.a through the permutation
+          Fold f{t.a, {}};
+          for (int d = 0; d < kTileRank; ++d) f.perm[d] = t.perm[d];
+          fold_of[t.dst] = f;
+          release(static_cast<int>(i));
+          continue;
+        }
       } else {
         unsupported("'" + n + "' is not supported in tile programs");
       }
       if (p.ops.size() == static_cast<size_t>(kTileMaxOps)) unsupported("the program has more than 32 tile ops");
       p.ops.push_back(t);
+      release(static_cast<int>(i));
     }
-    // A permute whose result feeds nothing but one store is folded into that
-    // store: the store reads the permute's operand through the permuted
-    // strides (code 1, b = the operand, perm), which saves the kernel a pass
-    // over shared memory and a CTA barrier per Block.
-    {
-      std::vector<int> uses(p.vals.size(), 0);
-      for (const TileOp& t : p.ops) {
-        if (t.kind == kTStore || t.kind == kTUnary || t.kind == kTReduce || t.kind == kTReshape ||
-            t.kind == kTPermute || t.kind == kTBinary)
-          ++uses[t.a];
-        if (t.kind == kTBinary) ++uses[t.b];
-      }
-      std::vector<TileOp> ops;
-      for (size_t i = 0; i < p.ops.size(); ++i) {
-        const TileOp t = p.ops[i];
-        if (t.kind == kTPermute && uses[t.dst] == 1) {
-          auto st = std::find_if(p.ops.begin() + static_cast<std::ptrdiff_t>(i) + 1, p.ops.end(),
-                                 [&](const TileOp& o) { return o.kind == kTStore && o.a == t.dst; });
-          if (st != p.ops.end()) {
-            st->code = 1;
-            st->b = t.a;
-            for (int d = 0; d < kTileRank; ++d) st->perm[d] = t.perm[d];
-            continue;
-          }
-        }
-        ops.push_back(t);
-      }
-      p.ops = std::move(ops);
-    }
+    // (A permute whose result feeds nothing but one store was folded into
+    // that store above: the store reads the permute's operand through the
+    // permuted strides, code 1, which saves the kernel a pass over shared
+    // memory and a CTA barrier per Block.)
     // Every Block stores tiles of its own: Blocks differing along any grid
     // axis must store to different tiles, or the result would depend on the
     // order in which Blocks run.
