@@ -12,6 +12,9 @@ Workloads are the BASELINE configurations (synthetic, seeded inputs):
                   grid (128,64) split along bid0 across ranks, output rows
                   gathered to rank 0 over NVLink by peer stores from the GEMM
                   (--gather nccl: an NCCL gather; the default workload)
+  transpose, silu, row_center, row_bias
+                  not BASELINE configurations: the data-movement kernel and the
+                  ew, rows and tile interpreters on f32 programs over 128 MiB
 
 A step is one launch of the workload's Block program over its whole Grid
 (for sharded_matmul: every rank's share plus the gather).  ``value`` is the
@@ -173,6 +176,47 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
                     unit="GB/s", dtype="f32",
                     config={"workload": "transpose", "shape": [8, 2048, 2048], "block_tile": [1, 32, 64],
                             "grid": [8, 64, 32]})
+    if name in ("silu", "row_center", "row_bias"):
+        # not BASELINE configurations: the three program interpreters (ew,
+        # rows, tile) on HBM-bound f32 programs over 128 MiB arrays
+        R, C = (32768, 1024) if name == "row_center" else (16384, 2048)
+        x = torch.randn(R, C, generator=g(6))
+        F = xt.float32
+        if name == "silu":
+            @xt.kernel
+            def silu_rows(inp, out, trow, col):
+                i = xt.bid(0)
+                t = xt.load(inp, index=(i, 0), shape=(trow, col))
+                xt.store(out, index=(i, 0), tile=t * xt.sigmoid(t))
+
+            mod = xt.convert(silu_rows, args=(A((R, C), F), A((R, C), F), 16, C), grid=(R // 16, 1, 1),
+                             double_buffering=True)
+            inputs, tile, grid = [x], [16, C], [R // 16, 1, 1]
+        elif name == "row_center":
+            @xt.kernel
+            def row_center(inp, out, trow, col):
+                i = xt.bid(0)
+                t = xt.load(inp, index=(i, 0), shape=(trow, col))
+                m = xt.max(t, axis=1)
+                xt.store(out, index=(i, 0), tile=(t - m) * (t - m))
+
+            mod = xt.convert(row_center, args=(A((R, C), F), A((R, C), F), 1, C), grid=(R, 1, 1),
+                             double_buffering=True)
+            inputs, tile, grid = [x], [1, C], [R, 1, 1]
+        else:
+            @xt.kernel
+            def row_bias(inp, vec, out, tm, tn):
+                i, j = xt.bid(0), xt.bid(1)
+                t = xt.load(inp, index=(i, j), shape=(tm, tn))
+                r = xt.load(vec, index=(0, j), shape=(1, tn), shared=1)
+                xt.store(out, index=(i, j), tile=t * r + r)
+
+            v = torch.randn(1, C, generator=g(7))
+            mod = xt.convert(row_bias, args=(A((R, C), F), A((1, C), F), A((R, C), F), 32, 256),
+                             grid=(R // 32, C // 256, 1), double_buffering=True)
+            inputs, tile, grid = [x, v], [32, 256], [R // 32, C // 256, 1]
+        return dict(module=mod, inputs=inputs, out_shape=(R, C), out_dtype=torch.float32, unit="GB/s", dtype="f32",
+                    config={"workload": name, "shape": [R, C], "block_tile": tile, "grid": grid})
     raise SystemExit(f"unknown workload {name}")
 
 
@@ -413,7 +457,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="sharded_matmul",
-                    choices=["add", "softmax", "matmul", "conv2d", "sharded_matmul", "transpose"])
+                    choices=["add", "softmax", "matmul", "conv2d", "sharded_matmul", "transpose", "silu",
+                             "row_center", "row_bias"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference", "torch"],
                     help="b200: this backend; reference: the reference's CPU path; torch: the vendor library "
                          "(cuBLAS, cuDNN) through PyTorch on one GPU, for context")
@@ -816,6 +861,16 @@ def run_torch_library(args, torch) -> None:
     elif name == "transpose":
         lib = "torch copy_ of a transposed view"
         fn = lambda i: outs[i % n_sets].copy_(sets[i % n_sets][0].transpose(1, 2))  # noqa: E731
+    elif name == "silu":
+        lib = "torch.nn.functional.silu"
+        fn = lambda i: torch.nn.functional.silu(sets[i % n_sets][0], inplace=False)  # noqa: E731
+    elif name == "row_center":
+        lib = "torch: (x - x.amax(1, keepdim=True)) ** 2 (three kernels)"
+        fn = lambda i: (sets[i % n_sets][0] - sets[i % n_sets][0].amax(1, keepdim=True)).square_()  # noqa: E731
+    elif name == "row_bias":
+        lib = "torch.addcmul(r, x, r, out=)"
+        fn = lambda i: torch.addcmul(sets[i % n_sets][1], sets[i % n_sets][0], sets[i % n_sets][1],  # noqa: E731
+                                     out=outs[i % n_sets])
     else:
         lib = "cuDNN via torch.nn.functional.conv2d, channels-last bf16 in, bf16 out"
         fn = lambda i: torch.nn.functional.conv2d(sets[i % n_sets][0], sets[i % n_sets][1], padding=1)  # noqa: E731

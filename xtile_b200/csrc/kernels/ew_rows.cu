@@ -177,44 +177,61 @@ __device__ __forceinline__ float4 binary4(uint8_t op, float4 x, float4 y) {
   }
 }
 
-// Four elements per thread per pass, for arrays whose range starts at a
-// multiple of 4 elements on aligned pointers.  The program's registers live
-// in shared memory, one float4 slot per register and thread, so an operand is
-// one 16-byte shared load at a computed address instead of a predicated
-// selection over every register.  The program's leading loads (n_lead of
-// them) are all issued before any of them is written to its register, so a
-// thread has every input's 16 bytes in flight at once.  The last n % 4
-// elements run through ew_element.
-__global__ void __launch_bounds__(kThreads) ew_program_v4(const __grid_constant__ EwArgs p, int n_lead) {
-  __shared__ float4 rf[kEwRegs * kThreads];
-  float4* my = rf + threadIdx.x;  // register k of this thread: my[k * kThreads]
+// 4 * NV elements per thread per pass (NV consecutive float4 groups), for
+// arrays whose range starts at a multiple of 4 elements on aligned pointers.
+// The program's registers live in shared memory, NV float4 slots per
+// register and thread, so an operand is a 16-byte shared load at a computed
+// address instead of a predicated selection over every register; decoding
+// and dispatching an instruction is paid once per 4 * NV elements.  The
+// program's leading loads (n_lead of them) are all issued before any is
+// written to its register, so a thread has every input's bytes in flight at
+// once.  Elements past the last whole group of four run through ew_element.
+template <int NV, int TH = kThreads / NV>  // TH threads: 32 KiB of register slots
+__global__ void __launch_bounds__(TH) ew_program_v4(const __grid_constant__ EwArgs p, int n_lead) {
+  __shared__ float4 rf[kEwRegs * NV * TH];
+  float4* my = rf + threadIdx.x;  // register k, group j of this thread: my[(k * NV + j) * TH]
   griddep_launch_dependents();
   griddep_wait();
   const int64_t n4 = (p.end - p.begin) / 4;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
-  for (int64_t v = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; v < n4; v += stride) {
-    const int64_t i = p.begin + 4 * v;
-    float4 t[kMaxSlots];
+  const int64_t nv = n4 / NV;  // whole passes; the rest below
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * TH;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * TH + threadIdx.x; v < nv; v += stride) {
+    const int64_t i0 = p.begin + 4 * NV * v;
+    float4 t[kMaxSlots][NV];
 #pragma unroll
-    for (int j = 0; j < kMaxSlots; ++j)
-      if (j < n_lead) t[j] = load4(p.in[p.code[j].a], p.in_elem[p.code[j].a], i);
+    for (int q = 0; q < kMaxSlots; ++q)
 #pragma unroll
-    for (int j = 0; j < kMaxSlots; ++j)
-      if (j < n_lead) my[p.code[j].dst * kThreads] = t[j];
+      for (int j = 0; j < NV; ++j)
+        if (q < n_lead) t[q][j] = load4(p.in[p.code[q].a], p.in_elem[p.code[q].a], i0 + 4 * j);
+#pragma unroll
+    for (int q = 0; q < kMaxSlots; ++q)
+#pragma unroll
+      for (int j = 0; j < NV; ++j)
+        if (q < n_lead) my[(p.code[q].dst * NV + j) * TH] = t[q][j];
     for (int pc = n_lead; pc < p.n_code; ++pc) {
       const Instr ins = p.code[pc];
+      float4* d = my + ins.dst * NV * TH;
+      const float4* x = my + ins.a * NV * TH;
+      const float4* y = my + ins.b * NV * TH;
       if (ins.op == kLoad) {
-        my[ins.dst * kThreads] = load4(p.in[ins.a], p.in_elem[ins.a], i);
+#pragma unroll
+        for (int j = 0; j < NV; ++j) d[j * TH] = load4(p.in[ins.a], p.in_elem[ins.a], i0 + 4 * j);
       } else if (ins.op == kStore) {
-        store4(p.out[ins.dst], p.out_elem[ins.dst], i, my[ins.a * kThreads]);
+#pragma unroll
+        for (int j = 0; j < NV; ++j) store4(p.out[ins.dst], p.out_elem[ins.dst], i0 + 4 * j, x[j * TH]);
       } else if (ins.op == kAdd || ins.op == kSub || ins.op == kMul) {
-        my[ins.dst * kThreads] = binary4(ins.op, my[ins.a * kThreads], my[ins.b * kThreads]);
+#pragma unroll
+        for (int j = 0; j < NV; ++j) d[j * TH] = binary4(ins.op, x[j * TH], y[j * TH]);
       } else {
-        my[ins.dst * kThreads] = unary4(ins.op, my[ins.a * kThreads]);
+#pragma unroll
+        for (int j = 0; j < NV; ++j) d[j * TH] = unary4(ins.op, x[j * TH]);
       }
     }
   }
-  if (blockIdx.x == 0 && threadIdx.x < (p.end - p.begin) - 4 * n4) ew_element(p, p.begin + 4 * n4 + threadIdx.x);
+  // the last n % (4 NV) elements
+  const int64_t done = 4 * NV * nv;
+  for (int64_t e = done + static_cast<int64_t>(blockIdx.x) * TH + threadIdx.x; e < p.end - p.begin; e += stride)
+    ew_element(p, p.begin + e);
 }
 
 // ---------------------------------------------------------------------------
@@ -464,8 +481,9 @@ cudaError_t launch_ew(const EwArgs& a, cudaStream_t stream) {
   if (v4) {
     int n_lead = 0;
     while (n_lead < a.n_code && n_lead < kMaxSlots && a.code[n_lead].op == kLoad) ++n_lead;
-    const int64_t n4 = n / 4;
-    return PdlLaunch(grid_for(n4 > 0 ? n4 : 1, kThreads, max_blocks), kThreads, 0, stream)(ew_program_v4, a, n_lead);
+    const int64_t n8 = n / 8;
+    return PdlLaunch(grid_for(n8 > 0 ? n8 : 1, kThreads / 2, 2 * max_blocks), kThreads / 2, 0, stream)(
+        ew_program_v4<2>, a, n_lead);
   }
   return PdlLaunch(grid_for(n, kThreads, max_blocks), kThreads, 0, stream)(ew_program, a);
 }
