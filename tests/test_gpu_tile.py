@@ -111,13 +111,16 @@ def row_vector_ops(x, v, y, tm, tn):
     xt.store(y, index=(i, 0), tile=xt.sigmoid(t * r - r))
 
 
-def test_row_vector_broadcast_bit_exact():
-    x = torch.randn(128, 64, generator=gen(6))
-    v = torch.randn(1, 64, generator=gen(7))
-    y = torch.empty(128, 64, device=DEV)
-    m = xt.run(row_vector_ops, args=(x.to(DEV), v.to(DEV), y, 32, 64), grid=(4, 1, 1))
+@pytest.mark.parametrize("rows,cols,tm", [(128, 64, 32), (64, 256, 16), (96, 512, 8)])
+def test_row_vector_broadcast_bit_exact(rows, cols, tm):
+    # 64-column tiles run 128-thread CTAs, 256- and 512-column tiles 256
+    # threads (the row-only and the general variant)
+    x = torch.randn(rows, cols, generator=gen(6))
+    v = torch.randn(1, cols, generator=gen(7))
+    y = torch.empty(rows, cols, device=DEV)
+    m = xt.run(row_vector_ops, args=(x.to(DEV), v.to(DEV), y, tm, cols), grid=(rows // tm, 1, 1))
     assert m.plan()["family"] == "tile"
-    ref = oracle(m, [x, v, torch.zeros(128, 64)])[2]
+    ref = oracle(m, [x, v, torch.zeros(rows, cols)])[2]
     # sigmoid: CUDA expf against numpy's f64 exp, within a few ulp
     np.testing.assert_allclose(host(y), ref, rtol=1e-6, atol=1e-7)
 

@@ -43,9 +43,10 @@ __device__ __forceinline__ void unravel(int e, const int32_t (&s)[kTileRank], in
   i[0] = e / s[1];
 }
 
-// Walks the multi-indices of elements e = t, t + kTileThreads, ... of a
-// rank-4 shape: one unravel per thread, then a mixed-radix add of the stride's
-// digits with one carry per dim (no division per element).
+// Walks the multi-indices of elements e = t, t + TH, ... of a rank-4 shape
+// (TH threads per CTA): one unravel per thread, then a mixed-radix add of the
+// stride's digits with one carry per dim (no division per element).
+template <int TH>
 struct Walker {
   int i[kTileRank];
   int step[kTileRank];
@@ -55,7 +56,7 @@ struct Walker {
 #pragma unroll
     for (int k = 0; k < kTileRank; ++k) s[k] = sh[k] = shape[k];
     unravel(t, sh, i);
-    unravel(kTileThreads, sh, step);
+    unravel(TH, sh, step);
   }
   __device__ __forceinline__ void next() {
     int c = 0;
@@ -89,10 +90,12 @@ struct TV {
 };
 
 // A tile whose two leading dims are 1 is R x C (R = shape[2], C = shape[3]).
-// When C divides the CTA width, each thread keeps one column and steps whole
-// rows: every offset then advances by a constant, with no index arithmetic.
+// When C divides the CTA width TH, each thread keeps one column and steps
+// whole rows: every offset then advances by a constant, with no index
+// arithmetic.
+template <int TH>
 __device__ __forceinline__ bool rows_of(const TV& v) {
-  return v.shape[0] == 1 && v.shape[1] == 1 && kTileThreads % v.shape[3] == 0;
+  return v.shape[0] == 1 && v.shape[1] == 1 && TH % v.shape[3] == 0;
 }
 
 __device__ __forceinline__ float wrap_i8(float x) {
@@ -124,7 +127,7 @@ __device__ __forceinline__ SmemView store_view(const TileArgs& p, const TileOp& 
 // Load or store of one tile: elements past the array edge load 0 / are skipped.
 // A load writes the slot of ``v``; a store writes the tile ``v`` (its shape)
 // reading each element through ``rd``.
-template <bool LOAD, bool ROWS>
+template <bool LOAD, bool ROWS, int TH>
 __device__ __forceinline__ void move_tile(float* sm, const TileArgs& p, const TileOp& op, const TV& v,
                                           const int64_t (&bid)[3], const SmemView& rd) {
   int64_t astride[kTileRank];
@@ -146,14 +149,14 @@ __device__ __forceinline__ void move_tile(float* sm, const TileArgs& p, const Ti
   void* arr = p.arr[op.arg];
   const uint8_t elem = p.elem[op.arg];
   constexpr int kBatch = 8;
-  if ((ROWS || rows_of(v)) && elem == kF32 && v.shape[3] % 4 == 0 && lim[3] % 4 == 0 && base % 4 == 0 &&
+  if ((ROWS || rows_of<TH>(v)) && elem == kF32 && v.shape[3] % 4 == 0 && lim[3] % 4 == 0 && base % 4 == 0 &&
       astride[2] % 4 == 0 && (reinterpret_cast<uintptr_t>(arr) & 15) == 0) {
     constexpr int kVecBatch = 4;  // float4s in flight per thread
     // f32 rows of a multiple of 4 elements at 16-byte aligned global offsets:
     // one float4 per thread per access (shared memory stays scalar: its rows
     // are padded to an odd length)
     const int C4 = v.shape[3] / 4, R = v.shape[2];
-    const int c = (threadIdx.x % C4) * 4, rs = kTileThreads / C4;
+    const int c = (threadIdx.x % C4) * 4, rs = TH / C4;
     const bool col_in = c < lim[3] && lim[0] > 0 && lim[1] > 0;
     const int r_lim = lim[2];
     float4* g = reinterpret_cast<float4*>(arr);
@@ -190,9 +193,9 @@ __device__ __forceinline__ void move_tile(float* sm, const TileArgs& p, const Ti
     }
     return;
   }
-  if (ROWS || rows_of(v)) {
+  if (ROWS || rows_of<TH>(v)) {
     const int C = v.shape[3], R = v.shape[2];
-    const int c = threadIdx.x % C, rs = kTileThreads / C;
+    const int c = threadIdx.x % C, rs = TH / C;
     const bool col_in = c < lim[3] && lim[0] > 0 && lim[1] > 0;
     const int r_lim = lim[2];
     const int64_t gstep = rs * astride[2];
@@ -222,16 +225,16 @@ __device__ __forceinline__ void move_tile(float* sm, const TileArgs& p, const Ti
     return;
   }
   if constexpr (ROWS) return;
-  Walker w(threadIdx.x, v.shape);
+  Walker<TH> w(threadIdx.x, v.shape);
   if (LOAD) {
     // kBatch independent loads in flight per thread before their shared-memory
     // stores: one HBM round trip per kBatch elements, not per element
-    for (int e0 = threadIdx.x; e0 < v.numel; e0 += kBatch * kTileThreads) {
+    for (int e0 = threadIdx.x; e0 < v.numel; e0 += kBatch * TH) {
       float val[kBatch];
       int dst[kBatch];
 #pragma unroll
       for (int u = 0; u < kBatch; ++u) {
-        const bool live = e0 + u * kTileThreads < v.numel;
+        const bool live = e0 + u * TH < v.numel;
         const bool in = live && w.i[0] < lim[0] && w.i[1] < lim[1] && w.i[2] < lim[2] && w.i[3] < lim[3];
         const int64_t off = base + w.i[0] * astride[0] + w.i[1] * astride[1] + w.i[2] * astride[2] + w.i[3];
         val[u] = in ? load_elem(arr, elem, off) : 0.0f;
@@ -243,7 +246,7 @@ __device__ __forceinline__ void move_tile(float* sm, const TileArgs& p, const Ti
         if (dst[u] >= 0) sm[dst[u]] = val[u];
     }
   } else {
-    for (int e = threadIdx.x; e < v.numel; e += kTileThreads, w.next()) {
+    for (int e = threadIdx.x; e < v.numel; e += TH, w.next()) {
       const bool in = w.i[0] < lim[0] && w.i[1] < lim[1] && w.i[2] < lim[2] && w.i[3] < lim[3];
       const int64_t off = base + w.i[0] * astride[0] + w.i[1] * astride[1] + w.i[2] * astride[2] + w.i[3];
       if (in)
@@ -257,8 +260,13 @@ __device__ __forceinline__ void move_tile(float* sm, const TileArgs& p, const Ti
 // ROWS: every tile of the program is R x C with C dividing the CTA width (the
 // planner checks), so only the row paths are compiled: fewer registers, more
 // CTAs per SM.
-template <bool ROWS>
-__global__ void __launch_bounds__(kTileThreads, ROWS ? 5 : 1) tile_program(const __grid_constant__ TileArgs p) {
+//
+// TH threads per CTA: 256, or 128 for programs of small tiles (the launcher
+// decides), which halves what the per-op set-up costs a Block while twice as
+// many CTAs share an SM.
+template <bool ROWS, int TH>
+__global__ void __launch_bounds__(TH, ROWS ? (TH == 256 ? 5 : 10) : (TH == 256 ? 1 : 2))
+    tile_program(const __grid_constant__ TileArgs p) {
   extern __shared__ float sm[];
   griddep_launch_dependents();
   griddep_wait();
@@ -270,39 +278,39 @@ __global__ void __launch_bounds__(kTileThreads, ROWS ? 5 : 1) tile_program(const
     switch (kind) {
       case kTLoad: {
         const TV v(p.vals[op.dst]);
-        move_tile<true, ROWS>(sm, p, op, v, bid, SmemView{});
+        move_tile<true, ROWS, TH>(sm, p, op, v, bid, SmemView{});
         break;
       }
       case kTStore: {
         const TV v(p.vals[op.a]);
-        move_tile<false, ROWS>(sm, p, op, v, bid, store_view(p, op, v));
+        move_tile<false, ROWS, TH>(sm, p, op, v, bid, store_view(p, op, v));
         break;
       }
       case kTConst: {
         const TV d(p.vals[op.dst]);
         const float value = op.value;
-        if (ROWS || rows_of(d)) {
-          const int C = d.shape[3], c = threadIdx.x % C, rs = kTileThreads / C;
+        if (ROWS || rows_of<TH>(d)) {
+          const int C = d.shape[3], c = threadIdx.x % C, rs = TH / C;
           for (int r = threadIdx.x / C; r < d.shape[2]; r += rs) sm[d.offset + r * d.stride[2] + c] = value;
           break;
         }
         if constexpr (!ROWS) {
-          Walker w(threadIdx.x, d.shape);
-          for (int e = threadIdx.x; e < d.numel; e += kTileThreads, w.next()) sm[d.at(w.i)] = value;
+          Walker<TH> w(threadIdx.x, d.shape);
+          for (int e = threadIdx.x; e < d.numel; e += TH, w.next()) sm[d.at(w.i)] = value;
         }
         break;
       }
       case kTUnary: {
         const TV d(p.vals[op.dst]), a(p.vals[op.a]);
-        if (ROWS || rows_of(d)) {
-          const int C = d.shape[3], c = threadIdx.x % C, rs = kTileThreads / C;
+        if (ROWS || rows_of<TH>(d)) {
+          const int C = d.shape[3], c = threadIdx.x % C, rs = TH / C;
           for (int r = threadIdx.x / C; r < d.shape[2]; r += rs)
             sm[d.offset + r * d.stride[2] + c] = unary_op(code, sm[a.offset + r * a.stride[2] + c]);
           break;
         }
         if constexpr (!ROWS) {
-          Walker w(threadIdx.x, d.shape);
-          for (int e = threadIdx.x; e < d.numel; e += kTileThreads, w.next())
+          Walker<TH> w(threadIdx.x, d.shape);
+          for (int e = threadIdx.x; e < d.numel; e += TH, w.next())
             sm[d.at(w.i)] = unary_op(code, sm[a.at(w.i)]);
         }
         break;
@@ -316,8 +324,8 @@ __global__ void __launch_bounds__(kTileThreads, ROWS ? 5 : 1) tile_program(const
           sa[k] = a.shape[k] == 1 ? 0 : a.stride[k];
           sb[k] = b.shape[k] == 1 ? 0 : b.stride[k];
         }
-        if (ROWS || rows_of(d)) {
-          const int C = d.shape[3], c = threadIdx.x % C, rs = kTileThreads / C;
+        if (ROWS || rows_of<TH>(d)) {
+          const int C = d.shape[3], c = threadIdx.x % C, rs = TH / C;
           for (int r = threadIdx.x / C; r < d.shape[2]; r += rs) {
             const float x = sm[a.offset + r * sa[2] + c * sa[3]];
             const float y = sm[b.offset + r * sb[2] + c * sb[3]];
@@ -327,8 +335,8 @@ __global__ void __launch_bounds__(kTileThreads, ROWS ? 5 : 1) tile_program(const
           break;
         }
         if constexpr (!ROWS) {
-          Walker w(threadIdx.x, d.shape);
-          for (int e = threadIdx.x; e < d.numel; e += kTileThreads, w.next()) {
+          Walker<TH> w(threadIdx.x, d.shape);
+          for (int e = threadIdx.x; e < d.numel; e += TH, w.next()) {
             const int(&i)[kTileRank] = w.i;
             const float x = sm[a.offset + i[0] * sa[0] + i[1] * sa[1] + i[2] * sa[2] + i[3] * sa[3]];
             const float y = sm[b.offset + i[0] * sb[0] + i[1] * sb[1] + i[2] * sb[2] + i[3] * sb[3]];
@@ -345,7 +353,7 @@ __global__ void __launch_bounds__(kTileThreads, ROWS ? 5 : 1) tile_program(const
         if constexpr (ROWS) {
           // rows mode: d is R x C with the reduced dim (2 or 3) of size 1
           const int C = d.shape[3];
-          for (int e = threadIdx.x; e < d.numel; e += kTileThreads) {
+          for (int e = threadIdx.x; e < d.numel; e += TH) {
             const int r = e / C, c = e - (e / C) * C;
             const float* src = sm + a.offset + r * a.stride[2] + c;
             float v;
@@ -364,8 +372,8 @@ __global__ void __launch_bounds__(kTileThreads, ROWS ? 5 : 1) tile_program(const
           }
           break;
         }
-        Walker w(threadIdx.x, d.shape);
-        for (int e = threadIdx.x; e < d.numel; e += kTileThreads, w.next()) {
+        Walker<TH> w(threadIdx.x, d.shape);
+        for (int e = threadIdx.x; e < d.numel; e += TH, w.next()) {
           const float* src = sm + a.at(w.i);  // the reduced dim's index is 0 in w.i
           float r;
           if (code == 0) {
@@ -387,11 +395,11 @@ __global__ void __launch_bounds__(kTileThreads, ROWS ? 5 : 1) tile_program(const
         const TV d(p.vals[op.dst]), a(p.vals[op.a]);
         if constexpr (ROWS) {
           const int dc = d.shape[3], ac = a.shape[3];
-          for (int e = threadIdx.x; e < d.numel; e += kTileThreads)
+          for (int e = threadIdx.x; e < d.numel; e += TH)
             sm[d.offset + (e / dc) * d.stride[2] + e % dc] = sm[a.offset + (e / ac) * a.stride[2] + e % ac];
         } else {
-          Walker wd(threadIdx.x, d.shape), wa(threadIdx.x, a.shape);
-          for (int e = threadIdx.x; e < d.numel; e += kTileThreads, wd.next(), wa.next())
+          Walker<TH> wd(threadIdx.x, d.shape), wa(threadIdx.x, a.shape);
+          for (int e = threadIdx.x; e < d.numel; e += TH, wd.next(), wa.next())
             sm[d.at(wd.i)] = sm[a.at(wa.i)];
         }
         break;
@@ -402,15 +410,15 @@ __global__ void __launch_bounds__(kTileThreads, ROWS ? 5 : 1) tile_program(const
         int ss[kTileRank];
 #pragma unroll
         for (int k = 0; k < kTileRank; ++k) ss[k] = p.vals[op.a].stride[op.perm[k]];
-        if (ROWS || rows_of(d)) {
-          const int C = d.shape[3], c = threadIdx.x % C, rs = kTileThreads / C;
+        if (ROWS || rows_of<TH>(d)) {
+          const int C = d.shape[3], c = threadIdx.x % C, rs = TH / C;
           for (int r = threadIdx.x / C; r < d.shape[2]; r += rs)
             sm[d.offset + r * d.stride[2] + c] = sm[a.offset + r * ss[2] + c * ss[3]];
           break;
         }
         if constexpr (!ROWS) {
-          Walker w(threadIdx.x, d.shape);
-          for (int e = threadIdx.x; e < d.numel; e += kTileThreads, w.next()) {
+          Walker<TH> w(threadIdx.x, d.shape);
+          for (int e = threadIdx.x; e < d.numel; e += TH, w.next()) {
             const int(&i)[kTileRank] = w.i;
             sm[d.at(i)] = sm[a.offset + i[0] * ss[0] + i[1] * ss[1] + i[2] * ss[2] + i[3] * ss[3]];
           }
@@ -653,6 +661,13 @@ cudaError_t launch_tile(const TileArgs& a, cudaStream_t stream) {
       return transpose ? launch(tile_move<1, true>, m) : launch(tile_move<1, false>, m);
     }
   }
+  // 128 threads for programs of small tiles whose rows (in the row-only
+  // variant) divide 128 columns
+  bool small = true;
+  for (int v = 0; v < kTileMaxVals; ++v)
+    if (a.vals[v].numel > 0)
+      small = small && a.vals[v].numel <= 4096 && (!a.rows || 128 % a.vals[v].shape[3] == 0);
+  const int th = small ? 128 : kTileThreads;
   const size_t smem = static_cast<size_t>(a.smem_floats) * sizeof(float);
   if (smem > 48 * 1024) {
     // the opt-in to more than 48 KiB is per device; set it to the family's maximum once
@@ -661,7 +676,8 @@ cudaError_t launch_tile(const TileArgs& a, cudaStream_t stream) {
     static std::atomic<uint64_t> attr_devices{0};
     const uint64_t bit = dev < 64 ? (uint64_t{1} << dev) : 0;
     if (!(attr_devices.load(std::memory_order_relaxed) & bit)) {
-      for (auto k : {tile_program<true>, tile_program<false>}) {
+      for (auto k : {tile_program<true, 256>, tile_program<false, 256>, tile_program<true, 128>,
+                     tile_program<false, 128>}) {
         cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              kTileSmemFloats * static_cast<int>(sizeof(float)));
         if (e != cudaSuccess) return e;
@@ -669,8 +685,10 @@ cudaError_t launch_tile(const TileArgs& a, cudaStream_t stream) {
       attr_devices.fetch_or(bit, std::memory_order_relaxed);
     }
   }
-  return PdlLaunch(dim3(static_cast<unsigned>(gx), static_cast<unsigned>(a.grid[1]), static_cast<unsigned>(a.grid[2])),
-                   dim3(kTileThreads), smem, stream)(a.rows ? tile_program<true> : tile_program<false>, a);
+  PdlLaunch launch(dim3(static_cast<unsigned>(gx), static_cast<unsigned>(a.grid[1]), static_cast<unsigned>(a.grid[2])),
+                   dim3(th), smem, stream);
+  if (th == 128) return a.rows ? launch(tile_program<true, 128>, a) : launch(tile_program<false, 128>, a);
+  return a.rows ? launch(tile_program<true, 256>, a) : launch(tile_program<false, 256>, a);
 }
 
 }  // namespace dev
