@@ -111,10 +111,11 @@ def row_vector_ops(x, v, y, tm, tn):
     xt.store(y, index=(i, 0), tile=xt.sigmoid(t * r - r))
 
 
-@pytest.mark.parametrize("rows,cols,tm", [(128, 64, 32), (64, 256, 16), (96, 512, 8)])
+@pytest.mark.parametrize("rows,cols,tm", [(128, 64, 32), (128, 128, 32), (64, 256, 16), (96, 512, 8)])
 def test_row_vector_broadcast_bit_exact(rows, cols, tm):
-    # 64-column tiles run 128-thread CTAs, 256- and 512-column tiles 256
-    # threads (the row-only and the general variant)
+    # CTA widths by tile: 32x64 (2048 elements) 64 threads, 32x128 128
+    # threads, 16x256 256 threads (row-only variant); 8x512 runs the general
+    # variant with 128 threads
     x = torch.randn(rows, cols, generator=gen(6))
     v = torch.randn(1, cols, generator=gen(7))
     y = torch.empty(rows, cols, device=DEV)

@@ -265,7 +265,7 @@ __device__ __forceinline__ void move_tile(float* sm, const TileArgs& p, const Ti
 // decides), which halves what the per-op set-up costs a Block while twice as
 // many CTAs share an SM.
 template <bool ROWS, int TH>
-__global__ void __launch_bounds__(TH, ROWS ? (TH == 256 ? 5 : 10) : (TH == 256 ? 1 : 2))
+__global__ void __launch_bounds__(TH, ROWS ? (TH == 256 ? 5 : TH == 128 ? 10 : 20) : (256 / TH))
     tile_program(const __grid_constant__ TileArgs p) {
   extern __shared__ float sm[];
   griddep_launch_dependents();
@@ -663,11 +663,13 @@ cudaError_t launch_tile(const TileArgs& a, cudaStream_t stream) {
   }
   // 128 threads for programs of small tiles whose rows (in the row-only
   // variant) divide 128 columns
-  bool small = true;
+  bool small = true, tiny = true;
   for (int v = 0; v < kTileMaxVals; ++v)
-    if (a.vals[v].numel > 0)
+    if (a.vals[v].numel > 0) {
       small = small && a.vals[v].numel <= 4096 && (!a.rows || 128 % a.vals[v].shape[3] == 0);
-  const int th = small ? 128 : kTileThreads;
+      tiny = tiny && a.vals[v].numel <= 2048 && (!a.rows || 64 % a.vals[v].shape[3] == 0);
+    }
+  const int th = tiny ? 64 : small ? 128 : kTileThreads;
   const size_t smem = static_cast<size_t>(a.smem_floats) * sizeof(float);
   if (smem > 48 * 1024) {
     // the opt-in to more than 48 KiB is per device; set it to the family's maximum once
@@ -677,7 +679,7 @@ cudaError_t launch_tile(const TileArgs& a, cudaStream_t stream) {
     const uint64_t bit = dev < 64 ? (uint64_t{1} << dev) : 0;
     if (!(attr_devices.load(std::memory_order_relaxed) & bit)) {
       for (auto k : {tile_program<true, 256>, tile_program<false, 256>, tile_program<true, 128>,
-                     tile_program<false, 128>}) {
+                     tile_program<false, 128>, tile_program<true, 64>, tile_program<false, 64>}) {
         cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              kTileSmemFloats * static_cast<int>(sizeof(float)));
         if (e != cudaSuccess) return e;
@@ -687,6 +689,7 @@ cudaError_t launch_tile(const TileArgs& a, cudaStream_t stream) {
   }
   PdlLaunch launch(dim3(static_cast<unsigned>(gx), static_cast<unsigned>(a.grid[1]), static_cast<unsigned>(a.grid[2])),
                    dim3(th), smem, stream);
+  if (th == 64) return a.rows ? launch(tile_program<true, 64>, a) : launch(tile_program<false, 64>, a);
   if (th == 128) return a.rows ? launch(tile_program<true, 128>, a) : launch(tile_program<false, 128>, a);
   return a.rows ? launch(tile_program<true, 256>, a) : launch(tile_program<false, 256>, a);
 }
