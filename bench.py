@@ -15,6 +15,8 @@ Workloads are the BASELINE configurations (synthetic, seeded inputs):
   transpose, silu, row_center, row_bias
                   not BASELINE configurations: the data-movement kernel and the
                   ew, rows and tile interpreters on f32 programs over 128 MiB
+  matmul_i8       not a BASELINE configuration: the reference's int8
+                  kernels/matmul.py program (scale, bias, int8 out) at 8192^3
 
 A step is one launch of the workload's Block program over its whole Grid
 (for sharded_matmul: every rank's share plus the gather).  ``value`` is the
@@ -42,6 +44,13 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "TFLOP/s (matmul/conv) & HBM GB/s (add/softmax) vs B200 peak, 1–8 GPUs"
 L2_BYTES = 126 * 2 ** 20
+OPS_UNITS = ("TFLOP/s", "TOP/s")  # tensor-core work counted in multiply-add ops (bf16 / int8)
+
+
+def launch_arrays(w: dict, ins: list, out) -> list:
+    """The program's arrays in signature order: the output sits at w["out_pos"] (last by default)."""
+    pos = w.get("out_pos", len(ins))
+    return [*ins[:pos], out, *ins[pos:]]
 # SMs the sharded GEMM leaves to the NCCL gather it overlaps, and NCCL's
 # channel cap.  On 2 B200s, 16 free SMs did not let the gather's kernels run
 # beside the GEMM at all (it waited for the GEMM to finish); 32 did.
@@ -176,6 +185,34 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
                     unit="GB/s", dtype="f32",
                     config={"workload": "transpose", "shape": [8, 2048, 2048], "block_tile": [1, 32, 64],
                             "grid": [8, 64, 32]})
+    if name == "matmul_i8":
+        # not a BASELINE configuration: the reference's kernels/matmul.py
+        # Block program as written (int8 A, B; 64 x 64 Blocks over the whole K;
+        # t * scale + bias; int8 result) at 8192^3 on the int8 tensor cores
+        @xt.kernel
+        def matmul_kernel(lhs, rhs, res, scale, bias, tm, tn, tk):
+            bid_x, bid_y = xt.bid(0), xt.bid(1)
+            lhs_tile = xt.load(lhs, index=(bid_x, 0), shape=(tm, tk))
+            rhs_tile = xt.load(rhs, index=(0, bid_y), shape=(tk, tn), shared=1)
+            s_tile = xt.load(scale, index=(0, bid_y), shape=(1, tn), shared=1)
+            b_tile = xt.load(bias, index=(0, bid_y), shape=(1, tn), shared=1)
+            t = xt.matmul(lhs_tile, rhs_tile)
+            t = t * s_tile + b_tile
+            xt.store(res, index=(bid_x, bid_y), tile=xt.astype(t, dtype=xt.int8))
+
+        M = N = K = 8192
+        gen = g(8)
+        a = torch.randint(-128, 128, (M, K), generator=gen, dtype=torch.int8)
+        b = torch.randint(-128, 128, (K, N), generator=gen, dtype=torch.int8)
+        s = torch.rand(1, N, generator=gen) * 1e-5
+        bias = torch.rand(1, N, generator=gen) * 16 - 8
+        I8, F = xt.int8, xt.float32
+        mod = xt.convert(matmul_kernel, args=(A((M, K), I8), A((K, N), I8), A((M, N), I8), A((1, N), F), A((1, N), F),
+                                              64, 64, K), grid=(M // 64, N // 64, 1), double_buffering=True)
+        return dict(module=mod, inputs=[a, b, s, bias], out_pos=2, out_shape=(M, N), out_dtype=torch.int8,
+                    unit="TOP/s", dtype="int8",
+                    config={"workload": name, "M": M, "N": N, "K": K, "block_tile": [64, 64], "k_step": K,
+                            "grid": [M // 64, N // 64, 1], "epilogue": "t * scale + bias, int8 (round half even, saturate)"})
     if name in ("silu", "row_center", "row_bias"):
         # not BASELINE configurations: the three program interpreters (ew,
         # rows, tile) on HBM-bound f32 programs over 128 MiB arrays
@@ -347,10 +384,10 @@ def cpu_baseline(w: dict, xt, torch, budget_s: float = 12.0) -> dict:
     arrays = []
     for t in w["inputs"]:
         arrays.append(t.view(torch.uint16).numpy() if t.dtype == torch.bfloat16 else t.numpy())
-    out = np.zeros(w["out_shape"], dtype=np.float32)
-    arrays.append(out)
+    out = np.zeros(w["out_shape"], dtype=np.int8 if w["out_dtype"] == torch.int8 else np.float32)
+    arrays.insert(w.get("out_pos", len(arrays)), out)
     plan = module.plan()
-    work = plan["flops"] if w["unit"] == "TFLOP/s" else plan["bytes"]
+    work = plan["flops"] if w["unit"] in OPS_UNITS else plan["bytes"]
     interp = xt_oracle.Interpreter(func)
     done = 0
     t0 = time.perf_counter()
@@ -362,7 +399,7 @@ def cpu_baseline(w: dict, xt, torch, budget_s: float = 12.0) -> dict:
         done += 1
     dt = time.perf_counter() - t0
     per_block = work / len(order)
-    value = per_block * done / dt / (1e12 if w["unit"] == "TFLOP/s" else 1e9)
+    value = per_block * done / dt / (1e12 if w["unit"] in OPS_UNITS else 1e9)
     threads = torch.get_num_threads()
     return {"value": value, "unit": w["unit"], "cores": threads, "kind": "port",
             "sample": f"{done} of {len(order)} Blocks in {dt:.1f} s (numpy oracle, BLAS threads={threads})"}
@@ -414,8 +451,13 @@ def nccl_gather(out, rows_per_rank, world, rank, dist):
         dist.gather(mine, dst=0)
 
 
-def roofline_line(plan: dict, share: float, kernel_ms: float, peaks: dict, peak_kind: str) -> dict:
+def roofline_line(plan: dict, share: float, kernel_ms: float, peaks: dict, peak_kind: str,
+                  int8: bool = False) -> dict:
     """The ``roofline`` object for one launch of ``share`` of the Grid taking ``kernel_ms``.
+
+    ``int8``: the work is int8 tensor-core ops, whose dense rate is twice the
+    bf16 rate; the tensor peaks are the measured bf16 ones doubled, and the
+    unit is TOP/s.
 
     The binding roofline is the one whose floor (work / peak) is longer: a
     TFLOP/s workload below the ridge point (FLOP per byte < tensor peak / HBM
@@ -428,6 +470,10 @@ def roofline_line(plan: dict, share: float, kernel_ms: float, peaks: dict, peak_
     launch_bytes = plan["bytes"] * share
     launch_flops = plan["flops"] * share
     secs = kernel_ms * 1e-3
+    if int8:
+        peaks = {**peaks, "bf16_tflops": 2 * peaks["bf16_tflops"]}
+        if "bf16_tflops_sustained" in peaks:
+            peaks["bf16_tflops_sustained"] = 2 * peaks["bf16_tflops_sustained"]
     hbm_floor = launch_bytes / (peaks["hbm_gbs"] * 1e9)
     tensor_floor = launch_flops / (peaks["bf16_tflops"] * 1e12)
     bound = "hbm" if hbm_floor >= tensor_floor else "tensor"
@@ -435,8 +481,8 @@ def roofline_line(plan: dict, share: float, kernel_ms: float, peaks: dict, peak_
     if bound == "hbm":
         achieved, peak, unit = launch_bytes / secs / 1e9, peaks["hbm_gbs"], "GB/s"
     else:
-        achieved, peak, unit = launch_flops / secs / 1e12, peaks["bf16_tflops"], "TFLOP/s"
-    kind = f"{peak_kind} (burst)"
+        achieved, peak, unit = launch_flops / secs / 1e12, peaks["bf16_tflops"], "TOP/s" if int8 else "TFLOP/s"
+    kind = f"{peak_kind} (burst)" + (", int8 = 2 x bf16" if int8 and bound == "tensor" else "")
     extra = {}
     if launch_flops > 0:  # the non-binding roofline's fraction, for reference
         if bound == "hbm":
@@ -458,7 +504,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="sharded_matmul",
                     choices=["add", "softmax", "matmul", "conv2d", "sharded_matmul", "transpose", "silu",
-                             "row_center", "row_bias"])
+                             "row_center", "row_bias", "matmul_i8"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference", "torch"],
                     help="b200: this backend; reference: the reference's CPU path; torch: the vendor library "
                          "(cuBLAS, cuDNN) through PyTorch on one GPU, for context")
@@ -557,14 +603,14 @@ def main() -> None:
 
     def step(i, rng=(lo, hi)):
         ins, o = sets[i % n_sets]
-        xt.launch(mod, *ins, o, bid0_range=rng)
+        xt.launch(mod, *launch_arrays(w, ins, o), bid0_range=rng)
 
     def sharded_step(i, start=None, end=None):
         if peer:
             ins, o = sets[i % n_sets][0], targets[i % n_sets]
             if start is not None:
                 start.record(stream)
-            xt.launch(mod, *ins, o, bid0_range=(lo, hi))
+            xt.launch(mod, *launch_arrays(w, ins, o), bid0_range=(lo, hi))
             if end is not None:
                 end.record(stream)
             dist.all_reduce(flag)
@@ -577,7 +623,7 @@ def main() -> None:
         if start is not None:
             start.record(stream)
         with xt.sm_budget(sms - GATHER_SMS if world > 1 else 0):
-            xt.launch(mod, *ins, o, bid0_range=(lo, hi))
+            xt.launch(mod, *launch_arrays(w, ins, o), bid0_range=(lo, hi))
         if end is not None:
             end.record(stream)
         computed[i % n_sets].record(stream)
@@ -712,7 +758,7 @@ def main() -> None:
                 s_k.wait_event(ev_in[b])
                 if j >= 2:
                     s_k.wait_event(ev_out[b])  # step j - 2's result has been copied out
-                xt.launch(mod, *e_ins, e_o, bid0_range=(lo, hi))
+                xt.launch(mod, *launch_arrays(w, e_ins, e_o), bid0_range=(lo, hi))
                 ev_k[b].record(s_k)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(ev_k[b])
@@ -727,10 +773,10 @@ def main() -> None:
                 for d, h in zip(ins, host_in):
                     d.copy_(h, non_blocking=True)
             if peer:
-                xt.launch(mod, *ins, targets[0], bid0_range=(lo, hi))
+                xt.launch(mod, *launch_arrays(w, ins, targets[0]), bid0_range=(lo, hi))
                 dist.all_reduce(flag)
             else:
-                xt.launch(mod, *ins, o, bid0_range=(lo, hi))
+                xt.launch(mod, *launch_arrays(w, ins, o), bid0_range=(lo, hi))
                 if sharded:
                     nccl_gather(o, rows_per_rank, world, rank, dist)
             if host_out.numel():
@@ -777,12 +823,12 @@ def main() -> None:
 
     # ---- report
     peaks, peak_kind = load_peaks()
-    work = plan["flops"] if w["unit"] == "TFLOP/s" else plan["bytes"]
-    scale = 1e12 if w["unit"] == "TFLOP/s" else 1e9
+    work = plan["flops"] if w["unit"] in OPS_UNITS else plan["bytes"]
+    scale = 1e12 if w["unit"] in OPS_UNITS else 1e9
     job_units = work if (sharded or world == 1) else work * world
     ms_per_step = total_ms / args.steps
     value = job_units / (ms_per_step * 1e-3) / scale
-    roofline = roofline_line(plan, (hi - lo) / grid0, kernel_ms, peaks, peak_kind)
+    roofline = roofline_line(plan, (hi - lo) / grid0, kernel_ms, peaks, peak_kind, int8=w["unit"] == "TOP/s")
     roofline["traffic"] = NCU_TRAFFIC_BYTES.get(args.workload)
     line = {
         "metric": METRIC,
@@ -861,6 +907,13 @@ def run_torch_library(args, torch) -> None:
     elif name == "transpose":
         lib = "torch copy_ of a transposed view"
         fn = lambda i: outs[i % n_sets].copy_(sets[i % n_sets][0].transpose(1, 2))  # noqa: E731
+    elif name == "matmul_i8":
+        lib = "torch._int_mm (cuBLASLt int8) + f32 scale/bias + int8 cast"
+
+        def fn(i):
+            a, b, sc, bi = sets[i % n_sets]
+            t = torch._int_mm(a, b).float().mul_(sc).add_(bi)
+            return t.round_().clamp_(-128, 127).to(torch.int8)
     elif name == "silu":
         lib = "torch.nn.functional.silu"
         fn = lambda i: torch.nn.functional.silu(sets[i % n_sets][0], inplace=False)  # noqa: E731
@@ -891,8 +944,8 @@ def run_torch_library(args, torch) -> None:
     graph.replay()
     torch.cuda.synchronize()
     ms = g_begin.elapsed_time(g_end) / args.steps
-    work = plan["flops"] if w["unit"] == "TFLOP/s" else plan["bytes"]
-    scale = 1e12 if w["unit"] == "TFLOP/s" else 1e9
+    work = plan["flops"] if w["unit"] in OPS_UNITS else plan["bytes"]
+    scale = 1e12 if w["unit"] in OPS_UNITS else 1e9
     print(json.dumps({"metric": METRIC, "impl": "torch", "library": lib, "value": round(work / (ms * 1e-3) / scale, 3),
                       "unit": w["unit"], "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
                       "ms_per_step": round(ms, 4), "higher_is_better": True,

@@ -94,16 +94,6 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   nt = r / gm;
 }
 
-__device__ __forceinline__ float epilogue_value(const Params& p, float v, int64_t row, int64_t col) {
-  if (p.acc) v = __fadd_rn(__ldg(p.acc + row * p.ldc + col), v);
-  for (int s = 0; s < p.n_epi; ++s) {
-    const uint8_t k = p.epi_kind[s];
-    const float e = __ldg(p.epi_ptr[s] + ((k == kEpiMulRow || k == kEpiAddRow) ? col : 0));
-    v = (k == kEpiMulRow || k == kEpiMulScalar) ? __fmul_rn(v, e) : __fadd_rn(v, e);
-  }
-  return v;
-}
-
 __device__ __forceinline__ int8_t to_i8(float v) {
   return v != v ? 0 : static_cast<int8_t>(static_cast<int>(fminf(fmaxf(rintf(v), -128.0f), 127.0f)));
 }
@@ -381,9 +371,51 @@ __global__ void __launch_bounds__(kThreads, 1)
           v[j] = AB == kI8 ? __int2float_rn(static_cast<int>(r[j])) : __uint_as_float(r[j]);
         const bool full_chunk = col0 + 32 <= p.N;
         if (!plain) {
+          // the epilogue in program order (accumulator tile + t, then each
+          // scale / bias step), each step applied to the chunk's 32 columns
+          // at once: the accumulator tile's and each row vector's 32 values
+          // are read once per chunk (8 x 16-byte loads when aligned).  Read
+          // per element inside the step loop they made the int8 GEMM with
+          // kernels/matmul.py's epilogue epilogue-bound (tensor pipe 15% busy)
+          auto load32 = [&](const float* src, float (&e)[32]) {
+            if (full_chunk && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (col0 + j < p.N) v[j] = epilogue_value(p, v[j], row, col0 + j);
+              for (int j = 0; j < 32; j += 4) {
+                const float4 q4 = __ldg(reinterpret_cast<const float4*>(src + j));
+                e[j] = q4.x;
+                e[j + 1] = q4.y;
+                e[j + 2] = q4.z;
+                e[j + 3] = q4.w;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) e[j] = col0 + j < p.N ? __ldg(src + j) : 0.0f;
+            }
+          };
+          float e[32];
+          if (p.acc) {
+            load32(p.acc + row * p.ldc + col0, e);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(e[j], v[j]);
+          }
+          for (int s = 0; s < p.n_epi; ++s) {
+            const uint8_t k = p.epi_kind[s];
+            const bool mul = k == kEpiMulRow || k == kEpiMulScalar;
+            if (k == kEpiMulRow || k == kEpiAddRow) {
+              load32(p.epi_ptr[s] + col0, e);
+            } else {
+              const float x = __ldg(p.epi_ptr[s]);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) e[j] = x;
+            }
+            if (mul) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(v[j], e[j]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], e[j]);
+            }
+          }
         }
         if (p.c_elem == kF32) {
           float* dst = static_cast<float*>(p.C) + row * p.ldc + col0;
