@@ -77,6 +77,7 @@ NCU_TRAFFIC_BYTES: dict[str, float] = {
     "softmax": 33_566_464 + 343_552,
     "sharded_matmul": 6_210_000_000 + 1_060_000_000,
     "transpose": 134_227_712 + 88_921_088,
+    "matmul_i8": 215_210_496 + 55_281_408,
 }
 
 
