@@ -14,7 +14,7 @@ Workloads are the BASELINE configurations (synthetic, seeded inputs):
                   (--gather nccl: an NCCL gather; the default workload)
   transpose, silu, row_center, row_bias
                   not BASELINE configurations: the data-movement kernel and the
-                  ew, rows and tile interpreters on f32 programs over 128 MiB
+                  ew and rows interpreters on f32 programs over 128 MiB
   matmul_i8       not a BASELINE configuration: the reference's int8
                   kernels/matmul.py program (scale, bias, int8 out) at 8192^3
 
@@ -215,8 +215,9 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
                     config={"workload": name, "M": M, "N": N, "K": K, "block_tile": [64, 64], "k_step": K,
                             "grid": [M // 64, N // 64, 1], "epilogue": "t * scale + bias, int8 (round half even, saturate)"})
     if name in ("silu", "row_center", "row_bias"):
-        # not BASELINE configurations: the three program interpreters (ew,
-        # rows, tile) on HBM-bound f32 programs over 128 MiB arrays
+        # not BASELINE configurations: the ew and rows program interpreters
+        # on HBM-bound f32 programs over 128 MiB arrays (row_bias: a
+        # broadcast row, which the ew interpreter reads as element i mod C)
         R, C = (32768, 1024) if name == "row_center" else (16384, 2048)
         x = torch.randn(R, C, generator=g(6))
         F = xt.float32

@@ -111,18 +111,47 @@ def row_vector_ops(x, v, y, tm, tn):
     xt.store(y, index=(i, 0), tile=xt.sigmoid(t * r - r))
 
 
-@pytest.mark.parametrize("rows,cols,tm", [(128, 64, 32), (128, 128, 32), (64, 256, 16), (96, 512, 8)])
-def test_row_vector_broadcast_bit_exact(rows, cols, tm):
-    # CTA widths by tile: 32x64 (2048 elements) 64 threads, 32x128 128
-    # threads, 16x256 256 threads (row-only variant); 8x512 runs the general
-    # variant with 128 threads
+@pytest.mark.parametrize("rows,cols,tm", [(128, 64, 32), (96, 37, 32), (64, 512, 8)])
+def test_row_vector_broadcast_runs_elementwise(rows, cols, tm):
+    # a [1, C] row broadcast over the rows is an elementwise program (the row
+    # is element i mod C of the flat map); 37 columns take the one-element
+    # interpreter, 64 and 512 the vectorised one; a bid0 split matches
     x = torch.randn(rows, cols, generator=gen(6))
     v = torch.randn(1, cols, generator=gen(7))
     y = torch.empty(rows, cols, device=DEV)
     m = xt.run(row_vector_ops, args=(x.to(DEV), v.to(DEV), y, tm, cols), grid=(rows // tm, 1, 1))
-    assert m.plan()["family"] == "tile"
+    assert m.plan()["family"] == "ew"
     ref = oracle(m, [x, v, torch.zeros(rows, cols)])[2]
     # sigmoid: CUDA expf against numpy's f64 exp, within a few ulp
+    np.testing.assert_allclose(host(y), ref, rtol=1e-6, atol=1e-7)
+    y2 = torch.full((rows, cols), float("nan"), device=DEV)
+    g0 = rows // tm
+    for lo, hi in [(0, 1), (1, g0)]:
+        xt.launch(m, x.to(DEV), v.to(DEV), y2, bid0_range=(lo, hi))
+    assert torch.equal(y, y2)
+
+
+@xt.kernel
+def col_vector_ops(x, c, y, tm, tn):
+    i, j = xt.bid(0), xt.bid(1)
+    t = xt.load(x, index=(i, j), shape=(tm, tn))
+    s = xt.load(c, index=(i, 0), shape=(tm, 1))
+    xt.store(y, index=(i, j), tile=xt.sigmoid(t * s - s))
+
+
+@pytest.mark.parametrize("rows,cols,tm,tn", [(128, 128, 32, 64), (128, 256, 32, 128), (64, 512, 16, 256),
+                                             (96, 1024, 8, 512)])
+def test_column_vector_broadcast_tile_cta_widths(rows, cols, tm, tn):
+    # a (tm, 1) column broadcast over tiles narrower than a row runs in the
+    # tile interpreter; CTA widths by tile: 32x64 (2048 elements) 64 threads,
+    # 32x128 128 threads, 16x256 256 threads (row-only variant); 8x512 runs
+    # the general variant with 128 threads
+    x = torch.randn(rows, cols, generator=gen(6))
+    c = torch.randn(rows, 1, generator=gen(7))
+    y = torch.empty(rows, cols, device=DEV)
+    m = xt.run(col_vector_ops, args=(x.to(DEV), c.to(DEV), y, tm, tn), grid=(rows // tm, cols // tn, 1))
+    assert m.plan()["family"] == "tile"
+    ref = oracle(m, [x, c, torch.zeros(rows, cols)])[2]
     np.testing.assert_allclose(host(y), ref, rtol=1e-6, atol=1e-7)
 
 

@@ -120,7 +120,9 @@ int launch_plan(const xt::Plan& p, void* const* args, int64_t b0, int64_t b1, cu
       for (int i = 0; i < e.n_in; ++i) {
         a.in[i] = args[e.in_arg[i]];
         a.in_elem[i] = elem_code(e.in_elem[i]);
+        a.in_bcast[i] = e.in_bcast[i] ? 1 : 0;
       }
+      a.bcast_period = e.bcast_period;
       for (int i = 0; i < e.n_out; ++i) {
         a.out[i] = args[e.out_arg[i]];
         a.out_elem[i] = elem_code(e.out_elem[i]);
@@ -417,10 +419,12 @@ int xt_plan(const xt_module* module, const char* func, xt_plan_info* out) {
     switch (p->family) {
       case xt::Family::Ew: {
         out->m = p->ew.numel;
-        double bytes = 0;
-        for (int i = 0; i < p->ew.n_in; ++i) bytes += xt::elem_bytes(p->ew.in_elem[i]);
+        double bytes = 0, row_bytes = 0;
+        for (int i = 0; i < p->ew.n_in; ++i)
+          (p->ew.in_bcast[i] ? row_bytes : bytes) += xt::elem_bytes(p->ew.in_elem[i]);
         for (int i = 0; i < p->ew.n_out; ++i) bytes += xt::elem_bytes(p->ew.out_elem[i]);
-        out->bytes = bytes * static_cast<double>(p->ew.numel);
+        // a broadcast row is read once
+        out->bytes = bytes * static_cast<double>(p->ew.numel) + row_bytes * static_cast<double>(p->ew.bcast_period);
         break;
       }
       case xt::Family::Rows: {

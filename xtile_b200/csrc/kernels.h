@@ -22,6 +22,8 @@ struct EwArgs {
   int n_code;
   int n_in, n_out;
   int64_t begin, end;        // element range [begin, end)
+  uint8_t in_bcast[kMaxSlots];  // input read at element i mod bcast_period (a broadcast row)
+  int64_t bcast_period;
 };
 cudaError_t launch_ew(const EwArgs& a, cudaStream_t stream);
 

@@ -92,7 +92,7 @@ __device__ __forceinline__ void ew_element(const EwArgs& p, int64_t i) {
   for (int pc = 0; pc < p.n_code; ++pc) {
     const Instr ins = p.code[pc];
     if (ins.op == kLoad) {
-      put(r, ins.dst, load_elem(p.in[ins.a], p.in_elem[ins.a], i));
+      put(r, ins.dst, load_elem(p.in[ins.a], p.in_elem[ins.a], p.in_bcast[ins.a] ? i % p.bcast_period : i));
     } else if (ins.op == kStore) {
       store_elem(p.out[ins.dst], p.out_elem[ins.dst], i, pick(r, ins.a));
     } else if (ins.op == kAdd || ins.op == kSub || ins.op == kMul) {
@@ -195,14 +195,26 @@ __global__ void __launch_bounds__(TH) ew_program_v4(const __grid_constant__ EwAr
   const int64_t n4 = (p.end - p.begin) / 4;
   const int64_t nv = n4 / NV;  // whole passes; the rest below
   const int64_t stride = static_cast<int64_t>(gridDim.x) * TH;
-  for (int64_t v = static_cast<int64_t>(blockIdx.x) * TH + threadIdx.x; v < nv; v += stride) {
+  // broadcast rows: column of this thread's first element, advanced per pass
+  // without a division (the period is a multiple of 4)
+  const int64_t period = p.bcast_period > 0 ? p.bcast_period : 1;
+  const int64_t v_first = static_cast<int64_t>(blockIdx.x) * TH + threadIdx.x;
+  int64_t col = (p.begin + 4 * NV * v_first) % period;
+  const int64_t col_step = (4 * NV * stride) % period;
+  // element index of group j of the pass at element i0, for input slot s
+  auto at = [&](int s, int64_t i0, int j) -> int64_t {
+    if (!p.in_bcast[s]) return i0 + 4 * j;
+    const int64_t c = col + 4 * j;
+    return c >= period ? c - period : c;
+  };
+  for (int64_t v = v_first; v < nv; v += stride) {
     const int64_t i0 = p.begin + 4 * NV * v;
     float4 t[kMaxSlots][NV];
 #pragma unroll
     for (int q = 0; q < kMaxSlots; ++q)
 #pragma unroll
       for (int j = 0; j < NV; ++j)
-        if (q < n_lead) t[q][j] = load4(p.in[p.code[q].a], p.in_elem[p.code[q].a], i0 + 4 * j);
+        if (q < n_lead) t[q][j] = load4(p.in[p.code[q].a], p.in_elem[p.code[q].a], at(p.code[q].a, i0, j));
 #pragma unroll
     for (int q = 0; q < kMaxSlots; ++q)
 #pragma unroll
@@ -215,7 +227,7 @@ __global__ void __launch_bounds__(TH) ew_program_v4(const __grid_constant__ EwAr
       const float4* y = my + ins.b * NV * TH;
       if (ins.op == kLoad) {
 #pragma unroll
-        for (int j = 0; j < NV; ++j) d[j * TH] = load4(p.in[ins.a], p.in_elem[ins.a], i0 + 4 * j);
+        for (int j = 0; j < NV; ++j) d[j * TH] = load4(p.in[ins.a], p.in_elem[ins.a], at(ins.a, i0, j));
       } else if (ins.op == kStore) {
 #pragma unroll
         for (int j = 0; j < NV; ++j) store4(p.out[ins.dst], p.out_elem[ins.dst], i0 + 4 * j, x[j * TH]);
@@ -227,6 +239,8 @@ __global__ void __launch_bounds__(TH) ew_program_v4(const __grid_constant__ EwAr
         for (int j = 0; j < NV; ++j) d[j * TH] = unary4(ins.op, x[j * TH]);
       }
     }
+    col += col_step;
+    if (col >= period) col -= period;
   }
   // the last n % (4 NV) elements
   const int64_t done = 4 * NV * nv;
@@ -451,7 +465,8 @@ cudaError_t launch_ew(const EwArgs& a, cudaStream_t stream) {
   if (n <= 0) return cudaSuccess;
   const int max_blocks = sm_count() * 8;
   // dedicated path: out = in0 (op) in1, all f32, 16-byte aligned
-  if (a.n_code == 4 && a.n_in == 2 && a.n_out == 1 && a.code[0].op == kLoad && a.code[1].op == kLoad &&
+  if (a.n_code == 4 && a.n_in == 2 && a.n_out == 1 && !a.in_bcast[0] && !a.in_bcast[1] &&
+      a.code[0].op == kLoad && a.code[1].op == kLoad &&
       a.code[3].op == kStore && a.code[3].a == a.code[2].dst && a.in_elem[0] == kF32 &&
       a.in_elem[1] == kF32 && a.out_elem[0] == kF32 &&
       (a.code[2].op == kAdd || a.code[2].op == kSub || a.code[2].op == kMul) && a.begin % 4 == 0) {
@@ -473,7 +488,7 @@ cudaError_t launch_ew(const EwArgs& a, cudaStream_t stream) {
   }
   // vectorised interpreter: a range starting at a multiple of 4 elements on
   // pointers aligned to 4 elements of their type
-  bool v4 = a.begin % 4 == 0 && a.n_code <= kMaxInstr;
+  bool v4 = a.begin % 4 == 0 && a.n_code <= kMaxInstr && a.bcast_period % 4 == 0;
   for (int k = 0; k < a.n_in && v4; ++k)
     v4 = reinterpret_cast<uintptr_t>(a.in[k]) % (a.in_elem[k] == kF32 ? 16 : a.in_elem[k] == kBF16 ? 8 : 4) == 0;
   for (int k = 0; k < a.n_out && v4; ++k)

@@ -510,7 +510,24 @@ class Classifier {
       if (a.tile != ref->tile || a.idx != ref->idx || a.array.shape != ref->array.shape)
         unsupported("loads and stores must use the same tile shape, index and array shape");
     };
-    for (auto& kv : loads_) same_map(kv.second);
+    // A load of a [1, C] row at (0, j) with tiles (1, tn), beside [R, C]
+    // arrays in (tm, tn) tiles at (i, j), broadcasts the row over the rows:
+    // element (r, c) of the flat map reads element c of the row.
+    auto row_bcast = [&](const Access& a) {
+      return ref && ref->array.shape.size() == 2 && a.array.shape.size() == 2 && a.array.shape[0] == 1 &&
+             a.array.shape[1] == ref->array.shape[1] && ref->array.shape[0] > 1 && a.tile.size() == 2 &&
+             a.tile[0] == 1 && a.tile[1] == ref->tile[1] && !a.idx[0].bid && a.idx[0].value == 0 &&
+             a.idx[1] == ref->idx[1];
+    };
+    if (!ref) unsupported("the program stores nothing");
+    std::set<int> bcast_vals;  // SSA values loaded as row broadcasts, and values computed only from them
+    for (auto& kv : loads_) {
+      if (row_bcast(kv.second)) {
+        bcast_vals.insert(kv.first);
+        continue;
+      }
+      same_map(kv.second);
+    }
     for (auto& s : stores_) same_map(s);
     // the grid must cover every element exactly once
     std::set<int> axes;
@@ -550,6 +567,7 @@ class Classifier {
         const Access& a = loads_.at(op.results[0]);
         Elem e = a.array.elem;
         if (e != Elem::F32 && e != Elem::I8 && e != Elem::BF16) unsupported("unsupported element type");
+        const bool bc = bcast_vals.count(op.results[0]) > 0;
         auto it = in_slot.find(a.arg);
         int slot;
         if (it == in_slot.end()) {
@@ -557,13 +575,17 @@ class Classifier {
           slot = p.n_in++;
           p.in_arg[slot] = a.arg;
           p.in_elem[slot] = e;
+          p.in_bcast[slot] = bc;
           in_slot[a.arg] = slot;
         } else {
           slot = it->second;
+          if (p.in_bcast[slot] != bc) unsupported("an array is loaded both as a row broadcast and as tiles");
         }
+        if (bc) p.bcast_period = ref->array.shape[1];
         int r = alloc(op.results[0]);
         p.code.push_back({kLoad, static_cast<uint8_t>(r), static_cast<uint8_t>(slot), 0});
       } else if (n == "xt.store") {
+        if (bcast_vals.count(op.operands[0])) unsupported("a row-broadcast value is stored");
         const Access* a = nullptr;
         for (auto& s : stores_) if (s.op == static_cast<int>(i)) a = &s;
         Elem e = a->array.elem;
@@ -581,8 +603,26 @@ class Classifier {
             {"xt.itof", kItof}, {"xt.ftoi", kFtoi}};
         auto it = kOps.find(n);
         if (it == kOps.end()) unsupported("'" + n + "' is not an elementwise op");
-        for (const Type& t : op.operand_types)
-          if (t.shape != op.result_types[0].shape) unsupported("broadcasting ops are not elementwise");
+        // an operand of the row-broadcast shape (1, tn) must hold broadcast
+        // values; a result of that shape is one too
+        const std::vector<int64_t> row_shape = {1, ref->tile.size() == 2 ? ref->tile[1] : -1};
+        bool all_bcast = true;
+        for (size_t k = 0; k < op.operands.size(); ++k) {
+          const Type& t = op.operand_types[k];
+          const bool bc = bcast_vals.count(op.operands[k]) > 0;
+          all_bcast = all_bcast && bc;
+          if (t.shape == op.result_types[0].shape && (!bc || t.shape == row_shape)) continue;
+          if (bc && t.shape == row_shape && op.result_types[0].shape.size() == 2 &&
+              op.result_types[0].shape[1] == row_shape[1])
+            continue;
+          unsupported("broadcasting ops are not elementwise");
+        }
+        if (all_bcast) {
+          if (op.result_types[0].shape != row_shape) unsupported("broadcasting ops are not elementwise");
+          bcast_vals.insert(op.results[0]);
+        } else if (op.result_types[0].shape == row_shape && ref->tile[0] != 1) {
+          unsupported("broadcasting ops are not elementwise");
+        }
         bool binary = op.operands.size() == 2;
         if (binary && op.result_types[0].elem != Elem::F32)
           unsupported("elementwise arithmetic is supported on f32 tiles");

@@ -56,6 +56,10 @@ struct EwPlan {
   int64_t numel = 0;            // elements of each (identically shaped) array
   int64_t bid0_span = 0;        // elements covered by one bid0 step (0: bid0 unused)
   std::vector<int64_t> shape;
+  // inputs that are a [1, C] row broadcast over the [R, C] arrays: element i
+  // of the flat map reads element i mod C of the row (bcast_period = C)
+  bool in_bcast[kMaxSlots] = {};
+  int64_t bcast_period = 0;
 };
 
 struct RowPlan {
