@@ -49,3 +49,27 @@ def test_clock_summary_from_nvml_samples():
 
 def test_clock_summary_without_samples_is_marked_unavailable():
     assert bench.ClockSampler("GPU-test").summary()["reasons"] == ["unavailable"]
+
+
+def test_int8_roofline_doubles_the_tensor_peak():
+    # int8 ops are measured against twice the bf16 peaks, in TOP/s
+    plan = {"flops": 2.0 * 8192 ** 3, "bytes": 3 * 8192 ** 2}
+    r = bench.roofline_line(plan, 1.0, 0.332, PEAKS, "measured", int8=True)
+    assert r["bound"] == "tensor" and r["unit"] == "TOP/s"
+    assert r["peak"] == 2 * PEAKS["bf16_tflops"]
+    assert abs(r["frac"] - plan["flops"] / 0.332e-3 / 1e12 / (2 * PEAKS["bf16_tflops"])) < 1e-3
+    assert "int8 = 2 x bf16" in r["peak_kind"]
+
+
+def test_launch_arrays_places_the_output():
+    # kernels/matmul.py takes (lhs, rhs, res, scale, bias): the output third
+    assert bench.launch_arrays({"out_pos": 2}, ["a", "b", "s", "t"], "o") == ["a", "b", "o", "s", "t"]
+    assert bench.launch_arrays({}, ["a", "b"], "o") == ["a", "b", "o"]
+
+
+def test_interpreter_workloads_plan_onto_their_families():
+    import torch
+    import xtile as xt
+    fams = {name: bench.build_workload(name, xt, torch, 1, 0)["module"].plan()["family"]
+            for name in ("silu", "row_center", "row_bias", "transpose", "matmul_i8")}
+    assert fams == {"silu": "ew", "row_center": "rows", "row_bias": "ew", "transpose": "tile", "matmul_i8": "gemm"}

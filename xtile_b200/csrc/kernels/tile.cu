@@ -446,8 +446,8 @@ struct MoveGeom {
   int64_t cst;          // first element of the tile for bid = (0, 0, 0)
   int64_t mult[3];      // elements per unit of bid(k)
   int64_t row;          // array row stride (elements)
-  int32_t r_cst, r_mult[3];  // first tile row, as an array row index
-  int32_t c_cst, c_mult[3];  // first tile column
+  int64_t r_cst, c_cst;      // first tile row / column (array indices) for bid = (0, 0, 0)
+  int32_t r_mult[3], c_mult[3];  // rows / columns per unit of bid(k)
   int32_t ext_r, ext_c;      // array rows / columns
 };
 
@@ -623,8 +623,8 @@ bool plan_move(const TileArgs& a, MoveArgs& m, bool& transpose, int& eb) {
         if (d == 3) g.c_mult[cb] = static_cast<int32_t>(step);
       } else {
         g.cst += op.coord[d] * step * astride[d];
-        if (d == 2) g.r_cst = static_cast<int32_t>(op.coord[d] * step);
-        if (d == 3) g.c_cst = static_cast<int32_t>(op.coord[d] * step);
+        if (d == 2) g.r_cst = op.coord[d] * step;
+        if (d == 3) g.c_cst = op.coord[d] * step;
       }
     }
     return true;
