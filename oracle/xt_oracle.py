@@ -23,7 +23,7 @@ file interprets the xt program the way the reference's passes define it:
   as ``t * s + b`` stays two f32 roundings (``lib/nova/NovaOptimize.cpp:126-296``
   folds them into the matmul epilogue without changing their order).
 
-Deviations that are deliberate (recorded in DESIGN.md):
+Deviations from the reference, all deliberate:
 
 * every load reads the tile its index names.  The reference's serialize pass
   reuses a ``shared=k`` load across blocks keyed by ``(op, k==2 ? 0 : y, z)``
