@@ -405,7 +405,7 @@ class Classifier {
         if (n == "xt.ftoi" && op.result_types[0].elem != Elem::I8) unsupported("ftoi produces i8");
         if (kUn.count(n) && op.operand_types[0].elem != Elem::F32) unsupported("'" + n + "' expects an f32 tile");
         t.kind = kTUnary;
-        t.code = n == "xt.itof" ? kItof : n == "xt.ftoi" ? kFtoi : kUn.at(n);
+        t.code = n == "xt.itof" ? static_cast<uint8_t>(kItof) : n == "xt.ftoi" ? static_cast<uint8_t>(kFtoi) : kUn.at(n);
         t.a = val(op.operands[0]);
         t.dst = new_val(op.results[0], op.result_types[0], inplace_of(op, static_cast<int>(i), {0}));
       } else if (kBin.count(n)) {
