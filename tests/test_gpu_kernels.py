@@ -155,6 +155,30 @@ def test_ew_interpreter_int8_casts_tail_and_shards_bit_exact():
     assert torch.equal(y, y2) and torch.equal(yq, yq2)
 
 
+@xt.kernel
+def ew_copy(x, y, trow, col):
+    i = xt.bid(0)
+    xt.store(y, index=(i, 0), tile=xt.load(x, index=(i, 0), shape=(trow, col)))
+
+
+@pytest.mark.parametrize("shape,trow", [((64, 200), 16), ((9, 35), 3)])
+def test_ew_bf16_copy_bit_exact(shape, trow):
+    # bf16 through the ew interpreter: 8-byte groups of four; 9 x 35 = 315
+    # elements leave a 3-element tail, and its bid0 shard starting at element
+    # 105 takes the one-element form; values pass through f32 and come back
+    # bit for bit
+    x = torch.randn(*shape, generator=gen(31)).to(torch.bfloat16)
+    y = torch.zeros(*shape, dtype=torch.bfloat16, device=DEV)
+    m = xt.run(ew_copy, args=(x.to(DEV), y, trow, shape[1]), grid=(shape[0] // trow, 1, 1))
+    assert m.plan()["family"] == "ew"
+    assert torch.equal(y.cpu(), x)
+    y2 = torch.zeros(*shape, dtype=torch.bfloat16, device=DEV)
+    g0 = shape[0] // trow
+    for lo, hi in [(0, 1), (1, g0)]:
+        xt.launch(m, x.to(DEV), y2, bid0_range=(lo, hi))
+    assert torch.equal(y2.cpu(), x)
+
+
 # --------------------------------------------------------------- softmax
 @xt.kernel
 def softmax_rows(inp, out, trow, col):
