@@ -85,7 +85,14 @@ NCU_TRAFFIC_BYTES: dict[str, float] = {
 
 # ---------------------------------------------------------------- workloads
 def build_workload(name: str, xt, torch, world: int, rank: int):
-    """Returns (module, host input tensors, output index, ...) for ``name``."""
+    """The workload ``name``: its Block program's xt text and seeded host inputs.
+
+    ``xt`` is the DSL namespace (``xtile_b200/dsl.py``, which is pure Python):
+    the text is traced here without the native library, so the reference arm
+    can use it too.  ``work`` is the algorithmic work of one full launch
+    (bytes for HBM-bound programs, FLOP or int8 ops for the tensor-core ones),
+    from the configuration's own formula.
+    """
     g = torch.Generator().manual_seed
     A = xt.Array
     if name == "add":
@@ -100,9 +107,9 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
         a = torch.rand(2048, 2048, generator=gen) * 2 - 1
         b = torch.rand(2048, 2048, generator=gen) * 2 - 1
         args = (A((2048, 2048), xt.float32),) * 3
-        mod = xt.convert(add_tiles, args=(*args, 32, 64), grid=(64, 32, 1), double_buffering=True)
-        return dict(module=mod, inputs=[a, b], out_shape=(2048, 2048), out_dtype=torch.float32,
-                    unit="GB/s", dtype="f32",
+        text = xt.trace_text(add_tiles, args=(*args, 32, 64), grid=(64, 32, 1), double_buffering=True)
+        return dict(text=text, inputs=[a, b], out_shape=(2048, 2048), out_dtype=torch.float32,
+                    unit="GB/s", dtype="f32", work=3 * 2048 * 2048 * 4,
                     config={"workload": "add", "shape": [2048, 2048], "block_tile": [32, 64],
                             "grid": [64, 32, 1]})
     if name == "softmax":
@@ -115,10 +122,10 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
             xt.store(out, index=(i, 0), tile=x / xt.sum(x, axis=-1))
 
         x = torch.randn(8192, 1024, generator=g(1)) * 4
-        mod = xt.convert(softmax_rows, args=(A((8192, 1024), xt.float32), A((8192, 1024), xt.float32),
-                                             1, 1024), grid=(8192, 1, 1), double_buffering=True)
-        return dict(module=mod, inputs=[x], out_shape=(8192, 1024), out_dtype=torch.float32,
-                    unit="GB/s", dtype="f32",
+        text = xt.trace_text(softmax_rows, args=(A((8192, 1024), xt.float32), A((8192, 1024), xt.float32),
+                                                 1, 1024), grid=(8192, 1, 1), double_buffering=True)
+        return dict(text=text, inputs=[x], out_shape=(8192, 1024), out_dtype=torch.float32,
+                    unit="GB/s", dtype="f32", work=2 * 8192 * 1024 * 4,
                     config={"workload": "softmax", "shape": [8192, 1024], "block_tile": [1, 1024],
                             "grid": [8192, 1, 1]})
     if name in ("matmul", "sharded_matmul"):
@@ -144,16 +151,16 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
         a = (torch.randn(M, K, generator=gen) * s).to(torch.bfloat16)
         b = (torch.randn(K, N, generator=gen) * s).to(torch.bfloat16)
         grid = (M // tm, N // tn, 1)
-        mod = xt.convert(matmul_kloop, args=(A((M, K), xt.bfloat16), A((K, N), xt.bfloat16),
-                                             A((M, N), xt.float32), tm, tn, tk, K // tk),
-                         grid=grid, double_buffering=True)
+        text = xt.trace_text(matmul_kloop, args=(A((M, K), xt.bfloat16), A((K, N), xt.bfloat16),
+                                                 A((M, N), xt.float32), tm, tn, tk, K // tk),
+                             grid=grid, double_buffering=True)
         cfg = {"workload": name, "M": M, "N": N, "K": K, "block_tile": [tm, tn], "k_step": tk,
                "grid": list(grid)}
         if name == "sharded_matmul":
             cfg["parallelism"] = ("one GPU, the whole Grid" if world == 1 else
                                   f"bid0 split over {world} GPUs, NCCL gather of C rows to rank 0")
-        return dict(module=mod, inputs=[a, b], out_shape=(M, N), out_dtype=torch.float32,
-                    unit="TFLOP/s", dtype="bf16", config=cfg, sharded=name == "sharded_matmul")
+        return dict(text=text, inputs=[a, b], out_shape=(M, N), out_dtype=torch.float32,
+                    unit="TFLOP/s", dtype="bf16", config=cfg, sharded=name == "sharded_matmul", work=2 * M * N * K)
     if name == "conv2d":
         @xt.kernel
         def conv2d_bf16(inp, filt, out, tile_h, tile_w, cin, cout, kh, kw):
@@ -166,11 +173,12 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
         gen = g(3)
         x = (torch.randn(32, 56, 56, 64, generator=gen) * 0.1).to(torch.bfloat16)
         f = (torch.randn(3, 3, 64, 64, generator=gen) * 0.1).to(torch.bfloat16)
-        mod = xt.convert(conv2d_bf16, args=(A((32, 56, 56, 64), xt.bfloat16), A((3, 3, 64, 64), xt.bfloat16),
-                                            A((32, 56, 56, 64), xt.float32), 8, 56, 64, 64, 3, 3),
-                         grid=(32, 7, 1), double_buffering=True)
-        return dict(module=mod, inputs=[x, f], out_shape=(32, 56, 56, 64), out_dtype=torch.float32,
-                    unit="TFLOP/s", dtype="bf16",
+        text = xt.trace_text(conv2d_bf16, args=(A((32, 56, 56, 64), xt.bfloat16), A((3, 3, 64, 64), xt.bfloat16),
+                                                A((32, 56, 56, 64), xt.float32), 8, 56, 64, 64, 3, 3),
+                             grid=(32, 7, 1), double_buffering=True)
+        # implicit GEMM: M = 32*56*56 output pixels, N = 64 channels, K = 3*3*64
+        return dict(text=text, inputs=[x, f], out_shape=(32, 56, 56, 64), out_dtype=torch.float32,
+                    unit="TFLOP/s", dtype="bf16", work=2 * (32 * 56 * 56) * 64 * (3 * 3 * 64),
                     config={"workload": "conv2d", "input": [32, 56, 56, 64], "filter": [3, 3, 64, 64],
                             "pad": 1, "block_tile": [1, 8, 56, 64], "grid": [32, 7, 1]})
     if name == "transpose":
@@ -182,10 +190,10 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
             xt.store(out, index=(b, j, i), tile=xt.transpose(t))
 
         x = torch.randn(8, 2048, 2048, generator=g(5))
-        mod = xt.convert(transpose3, args=(A((8, 2048, 2048), xt.float32), A((8, 2048, 2048), xt.float32), 32, 64),
-                         grid=(8, 64, 32), double_buffering=True)
-        return dict(module=mod, inputs=[x], out_shape=(8, 2048, 2048), out_dtype=torch.float32,
-                    unit="GB/s", dtype="f32",
+        text = xt.trace_text(transpose3, args=(A((8, 2048, 2048), xt.float32), A((8, 2048, 2048), xt.float32),
+                                               32, 64), grid=(8, 64, 32), double_buffering=True)
+        return dict(text=text, inputs=[x], out_shape=(8, 2048, 2048), out_dtype=torch.float32,
+                    unit="GB/s", dtype="f32", work=2 * 8 * 2048 * 2048 * 4,
                     config={"workload": "transpose", "shape": [8, 2048, 2048], "block_tile": [1, 32, 64],
                             "grid": [8, 64, 32]})
     if name == "matmul_i8":
@@ -210,10 +218,11 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
         s = torch.rand(1, N, generator=gen) * 1e-5
         bias = torch.rand(1, N, generator=gen) * 16 - 8
         I8, F = xt.int8, xt.float32
-        mod = xt.convert(matmul_kernel, args=(A((M, K), I8), A((K, N), I8), A((M, N), I8), A((1, N), F), A((1, N), F),
-                                              64, 64, K), grid=(M // 64, N // 64, 1), double_buffering=True)
-        return dict(module=mod, inputs=[a, b, s, bias], out_pos=2, out_shape=(M, N), out_dtype=torch.int8,
-                    unit="TOP/s", dtype="int8",
+        text = xt.trace_text(matmul_kernel, args=(A((M, K), I8), A((K, N), I8), A((M, N), I8), A((1, N), F),
+                                                  A((1, N), F), 64, 64, K), grid=(M // 64, N // 64, 1),
+                             double_buffering=True)
+        return dict(text=text, inputs=[a, b, s, bias], out_pos=2, out_shape=(M, N), out_dtype=torch.int8,
+                    unit="TOP/s", dtype="int8", work=2 * M * N * K,
                     config={"workload": name, "M": M, "N": N, "K": K, "block_tile": [64, 64], "k_step": K,
                             "grid": [M // 64, N // 64, 1], "epilogue": "t * scale + bias, int8 (round half even, saturate)"})
     if name in ("silu", "row_center", "row_bias"):
@@ -230,9 +239,9 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
                 t = xt.load(inp, index=(i, 0), shape=(trow, col))
                 xt.store(out, index=(i, 0), tile=t * xt.sigmoid(t))
 
-            mod = xt.convert(silu_rows, args=(A((R, C), F), A((R, C), F), 16, C), grid=(R // 16, 1, 1),
-                             double_buffering=True)
-            inputs, tile, grid = [x], [16, C], [R // 16, 1, 1]
+            text = xt.trace_text(silu_rows, args=(A((R, C), F), A((R, C), F), 16, C), grid=(R // 16, 1, 1),
+                                 double_buffering=True)
+            inputs, tile, grid, work = [x], [16, C], [R // 16, 1, 1], 2 * R * C * 4
         elif name == "row_center":
             @xt.kernel
             def row_center(inp, out, trow, col):
@@ -241,9 +250,9 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
                 m = xt.max(t, axis=1)
                 xt.store(out, index=(i, 0), tile=(t - m) * (t - m))
 
-            mod = xt.convert(row_center, args=(A((R, C), F), A((R, C), F), 1, C), grid=(R, 1, 1),
-                             double_buffering=True)
-            inputs, tile, grid = [x], [1, C], [R, 1, 1]
+            text = xt.trace_text(row_center, args=(A((R, C), F), A((R, C), F), 1, C), grid=(R, 1, 1),
+                                 double_buffering=True)
+            inputs, tile, grid, work = [x], [1, C], [R, 1, 1], 2 * R * C * 4
         else:
             @xt.kernel
             def row_bias(inp, vec, out, tm, tn):
@@ -253,10 +262,11 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
                 xt.store(out, index=(i, j), tile=t * r + r)
 
             v = torch.randn(1, C, generator=g(7))
-            mod = xt.convert(row_bias, args=(A((R, C), F), A((1, C), F), A((R, C), F), 32, 256),
-                             grid=(R // 32, C // 256, 1), double_buffering=True)
-            inputs, tile, grid = [x, v], [32, 256], [R // 32, C // 256, 1]
-        return dict(module=mod, inputs=inputs, out_shape=(R, C), out_dtype=torch.float32, unit="GB/s", dtype="f32",
+            text = xt.trace_text(row_bias, args=(A((R, C), F), A((1, C), F), A((R, C), F), 32, 256),
+                                 grid=(R // 32, C // 256, 1), double_buffering=True)
+            # the broadcast row is read once
+            inputs, tile, grid, work = [x, v], [32, 256], [R // 32, C // 256, 1], (2 * R * C + C) * 4
+        return dict(text=text, inputs=inputs, work=work, out_shape=(R, C), out_dtype=torch.float32, unit="GB/s", dtype="f32",
                     config={"workload": name, "shape": [R, C], "block_tile": tile, "grid": grid})
     raise SystemExit(f"unknown workload {name}")
 
@@ -376,37 +386,49 @@ def load_peaks() -> tuple[dict, str]:
     return dict(FALLBACK_PEAKS), "fallback"
 
 
-def cpu_baseline(w: dict, xt, torch, budget_s: float = 12.0) -> dict:
-    """Times the CPU oracle on a bounded sample of the workload's Blocks."""
+def oracle_arrays(w: dict, torch) -> list:
+    """The workload's arrays as the oracle takes them (numpy, bf16 as uint16 bits), output zeroed."""
     import numpy as np
-    from oracle import xt_oracle
 
-    module = w["module"]
-    text = xt._module_asm(module)
-    func = xt_oracle.parse_module(text)[0]
-    order = xt_oracle.serialize_order(func.grid)
-    arrays = []
-    for t in w["inputs"]:
-        arrays.append(t.view(torch.uint16).numpy() if t.dtype == torch.bfloat16 else t.numpy())
+    arrays = [t.view(torch.uint16).numpy() if t.dtype == torch.bfloat16 else t.numpy() for t in w["inputs"]]
     out = np.zeros(w["out_shape"], dtype=np.int8 if w["out_dtype"] == torch.int8 else np.float32)
     arrays.insert(w.get("out_pos", len(arrays)), out)
-    plan = module.plan()
-    work = plan["flops"] if w["unit"] in OPS_UNITS else plan["bytes"]
-    interp = xt_oracle.Interpreter(func)
-    done = 0
-    t0 = time.perf_counter()
-    rng = np.random.default_rng(0)
-    picks = rng.permutation(len(order))
-    interp.run(arrays, blocks=[])  # binds arrays
-    while done < len(order) and time.perf_counter() - t0 < budget_s:
-        interp.run_block(order[picks[done]])
-        done += 1
-    dt = time.perf_counter() - t0
-    per_block = work / len(order)
-    value = per_block * done / dt / (1e12 if w["unit"] in OPS_UNITS else 1e9)
-    threads = torch.get_num_threads()
-    return {"value": value, "unit": w["unit"], "cores": threads, "kind": "port",
-            "sample": f"{done} of {len(order)} Blocks in {dt:.1f} s (numpy oracle, BLAS threads={threads})"}
+    return arrays
+
+
+def load_dsl():
+    """``xtile_b200/dsl.py`` loaded by path: the tracer is pure Python, and
+    importing the package would load the native library."""
+    import importlib.util
+
+    name = "xt_bench_dsl"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, ROOT / "xtile_b200" / "dsl.py")
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def oracle_rate(w: dict, done: int, secs: float, n_blocks: int) -> float:
+    """Throughput in the workload's unit of ``done`` Blocks in ``secs``."""
+    scale = 1e12 if w["unit"] in OPS_UNITS else 1e9
+    return w["work"] / n_blocks * done / secs / scale
+
+
+def cpu_baseline(w: dict, torch, budget_s: float = 12.0) -> dict:
+    """Times the CPU oracle on a bounded sample of the workload's Blocks, on
+    every host core (one process per core, Blocks split between them)."""
+    from oracle.parallel import BlockTimer
+
+    with BlockTimer(w["text"], oracle_arrays(w, torch)) as timer:
+        timer.sample(min(2.0, budget_s / 6))  # first touch of the mapped inputs
+        done, secs = timer.sample(budget_s)
+        n, procs = timer.n_blocks, timer.procs
+    return {"value": oracle_rate(w, done, secs, n), "unit": w["unit"], "cores": procs, "kind": "port",
+            "sample": f"{done} Blocks ({done / n:.3g} of the Grid's {n}) in {secs:.1f} s; numpy oracle, "
+                      f"{procs} processes with one BLAS thread each"}
 
 
 def bid0_share(grid0: int, world: int, rank: int, root_share: float | None = None) -> tuple[int, int]:
@@ -549,9 +571,12 @@ def main() -> None:
         os.environ.setdefault("NCCL_MAX_NCHANNELS", str(GATHER_CHANNELS))
         os.environ.setdefault("NCCL_MAX_P2P_NCHANNELS", str(GATHER_CHANNELS))
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
-    w = build_workload(args.workload, xt, torch, world, rank)
-    mod = w["module"]
+    w = build_workload(args.workload, load_dsl(), torch, world, rank)
+    mod = xt.parse(w["text"])
     plan = mod.plan()
+    plan_work = plan["flops"] if w["unit"] in OPS_UNITS else plan["bytes"]
+    if abs(plan_work - w["work"]) > 1e-9 * w["work"]:
+        raise SystemExit(f"bench: the planner's work {plan_work} differs from the configuration's {w['work']}")
     grid0 = plan["grid"][0]
     sharded = w.get("sharded", False)
     if world > 1 and not sharded:
@@ -827,7 +852,7 @@ def main() -> None:
 
     # ---- report
     peaks, peak_kind = load_peaks()
-    work = plan["flops"] if w["unit"] in OPS_UNITS else plan["bytes"]
+    work = w["work"]
     scale = 1e12 if w["unit"] in OPS_UNITS else 1e9
     job_units = work if (sharded or world == 1) else work * world
     ms_per_step = total_ms / args.steps
@@ -870,7 +895,7 @@ def main() -> None:
                        "ms_per_step": round(e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                        "pipelining": e_note}
     if not args.no_cpu and world == 1:  # the host-core baseline is a 1-GPU figure
-        line["cpu_baseline"] = cpu_baseline(w, xt, torch)
+        line["cpu_baseline"] = cpu_baseline(w, torch)
     print(json.dumps(line), flush=True)
     if dist:
         dist.destroy_process_group()
@@ -884,12 +909,9 @@ def run_torch_library(args, torch) -> None:
     bf16, half the bytes of this backend's f32 output).  The same inputs,
     rotating buffer sets and graph-replay timing as the b200 arm.
     """
-    import xtile as xt
-
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    w = build_workload(args.workload, xt, torch, 1, 0)
-    plan = w["module"].plan()
+    w = build_workload(args.workload, load_dsl(), torch, 1, 0)
     name = args.workload
     ins = [t.to(dev) for t in w["inputs"]]
     if name == "conv2d":
@@ -948,7 +970,7 @@ def run_torch_library(args, torch) -> None:
     graph.replay()
     torch.cuda.synchronize()
     ms = g_begin.elapsed_time(g_end) / args.steps
-    work = plan["flops"] if w["unit"] in OPS_UNITS else plan["bytes"]
+    work = w["work"]
     scale = 1e12 if w["unit"] in OPS_UNITS else 1e9
     print(json.dumps({"metric": METRIC, "impl": "torch", "library": lib, "value": round(work / (ms * 1e-3) / scale, 3),
                       "unit": w["unit"], "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
@@ -957,26 +979,37 @@ def run_torch_library(args, torch) -> None:
 
 
 def run_reference(args, world: int, rank: int, torch) -> None:
-    """Reference arm: the CPU oracle (the reference executes nothing itself)."""
+    """Reference arm: the CPU oracle (the reference executes nothing itself).
+
+    Self-contained: the Block program is traced by the pure-Python DSL and the
+    work comes from the configuration's formula, so no library of this
+    repository is loaded.  Every host core in the affinity mask is used,
+    whatever ``OMP_NUM_THREADS`` torchrun sets.
+    """
     if rank != 0:
         return
-    import xtile as xt
+    from oracle.parallel import BlockTimer
 
-    w = build_workload(args.workload, xt, torch, 1, 0)
+    w = build_workload(args.workload, load_dsl(), torch, 1, 0)
+    budget = max(1.0, 60.0 / (args.warmup + args.steps))
     samples = []
-    for i in range(args.warmup + args.steps):
-        b = cpu_baseline(w, xt, torch, budget_s=max(1.0, 60.0 / (args.warmup + args.steps)))
-        if i >= args.warmup:
-            samples.append(b)
-    value = statistics.fmean(s["value"] for s in samples)
-    base = samples[-1]
+    with BlockTimer(w["text"], oracle_arrays(w, torch)) as timer:
+        for i in range(args.warmup + args.steps):
+            done, secs = timer.sample(budget)
+            if i >= args.warmup:
+                samples.append((done, secs))
+        n, procs = timer.n_blocks, timer.procs
+    value = statistics.fmean(oracle_rate(w, d, s, n) for d, s in samples)
+    done = sum(d for d, _ in samples)
+    secs = sum(s for _, s in samples)
     line = {
         "metric": METRIC, "impl": "reference", "value": round(value, 6), "unit": w["unit"], "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
         "scaling": "strong" if w.get("sharded") else "weak", "vs_baseline": None, "dtype": w["dtype"],
         "data": "synthetic (seeded torch.Generator inputs of the BASELINE shapes)", "config": w["config"],
-        "cpu_baseline": {"value": round(value, 6), "unit": w["unit"], "cores": base["cores"],
-                         "kind": "port", "sample": base["sample"]},
+        "cpu_baseline": {"value": round(value, 6), "unit": w["unit"], "cores": procs, "kind": "port",
+                         "sample": f"{args.steps} steps of about {budget:.1f} s: {done} Blocks of the Grid's {n} "
+                                   f"in {secs:.1f} s; numpy oracle, {procs} processes with one BLAS thread each"},
         "e2e": {"value": round(value, 6), "unit": w["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference (sjjeong94/xtile) compiles to NPU command IR and executes nothing; this arm "
                 "times the CPU oracle that restates its semantics on a bounded sample of Blocks",

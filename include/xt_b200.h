@@ -83,6 +83,13 @@ void xt_string_free(char* text);
  * the B200 kernel plan.  Launching never depends on the stage. */
 int xt_run_pass(xt_module* module, const char* pass);
 
+/* Canonicalizes the module in place: xt.add(x, 0), xt.add(0, x) and
+ * xt.sub(x, 0) with 0 a splat zero constant fold to x, and side-effect-free
+ * ops left unused are erased.  Replaces MLIR's --canonicalize with the xt
+ * dialect's patterns (lib/xt/XTOps.cpp:395-449), which the reference's
+ * xt-opt runs (xt-opt/xt-opt.cpp:18-33; test/xt/canonicalize.mlir). */
+int xt_canonicalize(xt_module* module);
+
 /* Number of functions and the name of function ``index``. */
 int xt_num_funcs(const xt_module* module, int* out_count);
 int xt_func_name(const xt_module* module, int index, const char** out_name);
@@ -147,10 +154,13 @@ int xt_ipc_close(void* base);
  * cudaMalloc's implicit synchronisation.  The GEMM's scratch (its 4-byte error
  * word) lives in a 256-byte static __device__ array that every GPU loading
  * this library holds until exit; a launch needing more scratch is rejected.
- * The first call on a device resolves that array's address (make it before
- * any stream capture).  All calls share the array: each call clears the error
- * word on its stream first, calls whose kernels overlap on the GPU race on
- * it, and the word is not reported back. */
+ * The launch arguments (bid0 range, SM budget of xt_set_sm_budget) are built
+ * by the same code as xt_launch's.  The first call on a device resolves that
+ * array's address (make it before any stream capture); the address is kept,
+ * so the entry point must not be used on a device after cudaDeviceReset.  All
+ * calls share the array: each call clears the error word on its stream first,
+ * calls whose kernels overlap on the GPU race on it, and the word is not
+ * reported back. */
 int xt_matmul_launch_noalloc(const xt_module* module, const char* func, void* const* args, int n_args,
                              int64_t bid0_begin, int64_t bid0_end, void* stream);
 

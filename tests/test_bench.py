@@ -2,7 +2,16 @@
 
 These run on the CPU; the timings themselves need a B200 (``bench.py``).
 """
+import json
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
 import bench
+
+ROOT = Path(__file__).resolve().parents[1]
 
 PEAKS = {"hbm_gbs": 6544.7, "bf16_tflops": 1634.5, "bf16_tflops_sustained": 1385.9}
 
@@ -70,6 +79,41 @@ def test_launch_arrays_places_the_output():
 def test_interpreter_workloads_plan_onto_their_families():
     import torch
     import xtile as xt
-    fams = {name: bench.build_workload(name, xt, torch, 1, 0)["module"].plan()["family"]
+    fams = {name: xt.parse(bench.build_workload(name, bench.load_dsl(), torch, 1, 0)["text"]).plan()["family"]
             for name in ("silu", "row_center", "row_bias", "transpose", "matmul_i8")}
     assert fams == {"silu": "ew", "row_center": "rows", "row_bias": "ew", "transpose": "tile", "matmul_i8": "gemm"}
+
+
+@pytest.mark.parametrize("name", ["add", "softmax", "matmul", "conv2d", "sharded_matmul", "transpose", "silu",
+                                  "row_center", "row_bias", "matmul_i8"])
+def test_configuration_work_matches_the_plan(name):
+    # the reference arm takes the work from the configuration's formula; the
+    # planner must count the same bytes / FLOP for the GPU arm
+    import torch
+    import xtile as xt
+    w = bench.build_workload(name, bench.load_dsl(), torch, 1, 0)
+    plan = xt.parse(w["text"]).plan()
+    assert (plan["flops"] if w["unit"] in bench.OPS_UNITS else plan["bytes"]) == w["work"]
+
+
+def test_reference_arm_loads_no_library_of_this_repository(tmp_path):
+    # the reference arm traces with the pure-Python DSL and times the oracle:
+    # neither the _xtile extension nor libxt_b200.so may be mapped
+    code = (
+        "import sys, io, contextlib, json\n"
+        "sys.argv = ['bench.py', '--impl', 'reference', '--workload', 'add', '--steps', '1', '--warmup', '1']\n"
+        "import bench\n"
+        "buf = io.StringIO()\n"
+        "with contextlib.redirect_stdout(buf):\n"
+        "    bench.main()\n"
+        "line = json.loads(buf.getvalue().strip().splitlines()[-1])\n"
+        "maps = open('/proc/self/maps').read()\n"
+        "print(json.dumps({'line': line, 'so': [m for m in ('libxt_b200', '_xtile') if m in maps],\n"
+        "                  'mods': [m for m in sys.modules if m.startswith(('xtile', 'xtile_b200'))]}))\n")
+    res = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stderr[-2000:]
+    out = json.loads(res.stdout.strip().splitlines()[-1])
+    assert out["so"] == [] and out["mods"] == []
+    line = out["line"]
+    assert line["impl"] == "reference" and line["value"] > 0 and line["unit"] == "GB/s"
+    assert line["cpu_baseline"]["cores"] >= 1 and line["e2e"]["h2d_bytes_per_step"] == 0

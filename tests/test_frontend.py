@@ -298,7 +298,7 @@ def test_ew_register_program_matches_oracle():
     got = [a, b, np.zeros_like(a), np.zeros_like(a)]
     run_register_program(m, got)
     ref = [a, b, np.zeros_like(a), np.zeros_like(a)]
-    xt_oracle.run(xt._module_asm(m).split("// b200")[0] + "}", ref)
+    xt_oracle.run(m.source_text, ref)
     np.testing.assert_allclose(got[2], ref[2], rtol=1e-6, atol=1e-6)
     np.testing.assert_allclose(got[3], ref[3], rtol=1e-6, atol=1e-6)
 
@@ -319,6 +319,6 @@ def test_rows_register_program_matches_oracle():
     got = [x, np.zeros_like(x), np.zeros((12, 1), np.float32)]
     run_register_program(m, got)
     ref = [x, np.zeros_like(x), np.zeros((12, 1), np.float32)]
-    xt_oracle.run(xt._module_asm(m).split("// b200")[0] + "}", ref)
+    xt_oracle.run(m.source_text, ref)
     np.testing.assert_array_equal(got[1], ref[1])
     np.testing.assert_allclose(got[2], ref[2], rtol=1e-6)

@@ -30,7 +30,7 @@ def host(t):
 
 def oracle(module, arrays, blocks=None):
     outs = [host(a).copy() for a in arrays]
-    xt_oracle.run(xt._module_asm(module), outs, blocks=blocks)
+    xt_oracle.run(module.source_text, outs, blocks=blocks)
     return outs
 
 

@@ -96,7 +96,7 @@ def test_random_program_matches_oracle(seed):
     xt.launch(m, x.to(DEV), y.to(DEV), v.to(DEV), out, out2)
     refs = [np.zeros((R, C), np.float32), np.zeros((R, C), np.float32)]
     arrays = [x.numpy(), y.numpy(), v.numpy(), refs[0], refs[1]]
-    xt_oracle.run(xt._module_asm(m), arrays)
+    xt_oracle.run(m.source_text, arrays)
     for got, ref in ((out, arrays[3]), (out2, arrays[4])):
         got = got.cpu().numpy()
         assert np.all(np.isfinite(got) == np.isfinite(ref)), m.plan()["family"]

@@ -27,7 +27,7 @@ def host(t):
 
 def oracle(module, arrays):
     outs = [np.array(host(a)) for a in arrays]
-    xt_oracle.run(xt._module_asm(module), outs)
+    xt_oracle.run(module.source_text, outs)
     return outs
 
 

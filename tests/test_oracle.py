@@ -11,6 +11,8 @@ structure the oracle restates:
 The numeric cases then check the interpreter against formulas written
 independently here (numpy / torch), on small seeded inputs.
 """
+from pathlib import Path
+
 import numpy as np
 import pytest
 import torch
@@ -172,3 +174,84 @@ def test_lit_syntax_parses():
     xo.run(text, [src, dst])
     assert np.allclose(dst[:32], np.exp(src[:32]))
     assert np.all(dst[32:] == 0)
+
+
+# --------------------------------------------------------------------------
+# The product's C++ parse + print must not change a program.  The GPU parity
+# tests feed the oracle the DSL's own text (``Module.source_text``) while the
+# kernels run from the C++ parse of that text; these cases show that the two
+# readings are the same program, op by op with every attribute, so a misread
+# attribute in the C++ parser (a conv pad, a shared level, an epilogue
+# constant) cannot hide behind a re-printed text.
+# --------------------------------------------------------------------------
+def _bf16_programs():
+    A, bf, f32 = xt.Array, xt.bfloat16, xt.float32
+
+    @xt.kernel
+    def matmul_kloop(lhs, rhs, out, tm, tn, tk, ksteps):
+        i, j = xt.bid(0), xt.bid(1)
+        acc = None
+        for k in range(ksteps):
+            p = xt.matmul(xt.load(lhs, index=(i, k), shape=(tm, tk)),
+                          xt.load(rhs, index=(k, j), shape=(tk, tn), shared=1))
+            acc = p if acc is None else acc + p
+        xt.store(out, index=(i, j), tile=acc)
+
+    @xt.kernel
+    def conv2d_bf16(inp, filt, out, th, tw, cin, cout):
+        n, h, w = xt.bid(0), xt.bid(1), xt.bid(2)
+        f = xt.load(filt, index=(0, 0, 0, 0), shape=(3, 3, cin, cout), shared=2)
+        y = xt.load_conv2d(inp, f, index=(n, h, w, 0), shape=(1, th, tw, cout), group=1,
+                           pad=(1, 1, 1, 1), stride=(1, 1), dilation=(1, 1))
+        xt.store(out, index=(n, h, w, 0), tile=y)
+
+    return {
+        "matmul_4096_bf16": xt.trace_text(
+            matmul_kloop, args=(A((4096, 4096), bf), A((4096, 4096), bf), A((4096, 4096), f32), 128, 128, 64, 64),
+            grid=(32, 32, 1), double_buffering=True),
+        "sharded_matmul_bf16": xt.trace_text(
+            matmul_kloop, args=(A((32768, 8192), bf), A((8192, 8192), bf), A((32768, 8192), f32), 256, 128,
+                                8192, 1), grid=(128, 64, 1), double_buffering=True),
+        "conv2d_bf16_32x56x56x64": xt.trace_text(
+            conv2d_bf16, args=(A((32, 56, 56, 64), bf), A((3, 3, 64, 64), bf), A((32, 56, 56, 64), f32),
+                               8, 56, 64, 64), grid=(32, 7, 1), double_buffering=True),
+    }
+
+
+def _roundtrip_cases():
+    golden = Path(__file__).resolve().parent / "golden" / "dsl_text"
+    cases = [(p.stem, p.read_text()) for p in sorted(golden.glob("*.mlir"))]
+    return cases + sorted(_bf16_programs().items())
+
+
+@pytest.mark.parametrize("name,text", _roundtrip_cases(), ids=[c[0] for c in _roundtrip_cases()])
+def test_cpp_parse_print_preserves_program(name, text):
+    import xtile_b200 as b200
+
+    printed = b200._module_asm(b200.parse(text))
+    want = xo.parse_module(text)
+    got = xo.parse_module(printed)
+    assert len(got) == len(want)
+    for fg, fw in zip(got, want):
+        assert (fg.name, fg.args, fg.grid) == (fw.name, fw.args, fw.grid)
+        assert len(fg.ops) == len(fw.ops)
+        for og, ow in zip(fg.ops, fw.ops):
+            assert og == ow, f"{name}: {og} != {ow}"
+
+
+def test_roundtrip_comparison_sees_a_changed_attribute():
+    # a planted change in the oracle's input (a conv pad) must show up in the comparison
+    text = _bf16_programs()["conv2d_bf16_32x56x56x64"]
+    planted = text.replace("pad = array<i64: 1, 1, 1, 1>", "pad = array<i64: 1, 0, 1, 1>")
+    assert planted != text
+    assert xo.parse_module(planted) != xo.parse_module(text)
+
+
+def test_module_source_text_is_the_dsl_text():
+    import xtile_b200 as b200
+
+    text = _bf16_programs()["matmul_4096_bf16"]
+    m = b200.parse(text)
+    b200.compile(m)  # stages change the printed module, never the source text
+    assert m.source_text == text
+    assert str(m) != text

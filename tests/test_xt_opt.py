@@ -66,6 +66,27 @@ def test_plan_is_appended(tmp_path):
     assert rc == 0 and '// plan @g: {"family": "ew"' in out
 
 
-def test_canonicalize_is_refused(tmp_path):
-    rc, _, err, _ = run(tmp_path, GOOD, "--canonicalize")
-    assert rc == 2 and "no rewrite patterns" in err
+ZEROS = """func.func @z(%a: tensor<16x16xf32>, %b: tensor<16x1xf32>) -> tensor<16x16xf32> {
+  %zero = arith.constant dense<0.0> : tensor<16x16xf32>
+  %izero = arith.constant dense<0> : tensor<16x16xf32>
+  %0 = xt.add(%zero, %a) : tensor<16x16xf32>, tensor<16x16xf32> -> tensor<16x16xf32>
+  %1 = xt.sub(%0, %izero) : tensor<16x16xf32>, tensor<16x16xf32> -> tensor<16x16xf32>
+  %2 = xt.sub(%zero, %1) : tensor<16x16xf32>, tensor<16x16xf32> -> tensor<16x16xf32>
+  %3 = xt.add(%b, %zero) : tensor<16x1xf32>, tensor<16x16xf32> -> tensor<16x16xf32>
+  %4 = xt.mul(%2, %3) : tensor<16x16xf32>, tensor<16x16xf32> -> tensor<16x16xf32>
+  %5 = xt.exp(%a) : tensor<16x16xf32> -> tensor<16x16xf32>
+  return %4 : tensor<16x16xf32>
+}
+"""
+
+
+def test_canonicalize_folds_zero_operands(tmp_path):
+    # lib/xt/XTOps.cpp:395-449: 0 + x and x - 0 fold; 0 - x does not; a fold
+    # whose operand has another type than the result (a broadcast) is kept;
+    # the unused exp and the constants left unused are erased
+    rc, out, err, _ = run(tmp_path, ZEROS, "--canonicalize", "--keep-names")
+    assert rc == 0, err
+    assert "xt.sub(%zero, %a)" in out
+    assert "xt.add(%b, %zero)" in out
+    assert "xt.exp" not in out and "%izero" not in out
+    assert out.count("xt.add") == 1 and out.count("xt.sub") == 1

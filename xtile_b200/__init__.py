@@ -41,6 +41,7 @@ from .api import (
     Module,
     _module_asm,
     _parse_module,
+    canonicalize,
     cdiv,
     compile,
     convert,
@@ -58,7 +59,8 @@ from .api import (
 from .runtime import PeerArray, device_error, export_array, launch, run, sm_budget
 
 __all__ = [
-    "Array", "DType", "Module", "PeerArray", "add", "astype", "bfloat16", "bid", "cdiv", "compile", "convert",
+    "Array", "DType", "Module", "PeerArray", "add", "astype", "bfloat16", "bid", "canonicalize", "cdiv", "compile",
+    "convert",
     "cos", "device_error", "exp", "export_array", "float32", "int8", "kernel", "launch", "load", "load_conv2d",
     "matmul", "max", "mma", "mul", "nova_allocate", "nova_barrier", "nova_optimize",
     "nova_threading", "nova_to_x1", "parse", "reciprocal", "reshape", "rsqrt", "run",

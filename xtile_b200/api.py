@@ -40,9 +40,10 @@ def _wrap_module_asm(asm: str) -> tuple[str, str | None]:
 class Module:
     """A parsed xt module; owns the native handle (a capsule)."""
 
-    def __init__(self, raw_module: Any, display_asm: str | None = None) -> None:
+    def __init__(self, raw_module: Any, display_asm: str | None = None, source_asm: str | None = None) -> None:
         self._raw_module = raw_module
         self._display_asm = display_asm
+        self._source_asm = source_asm
 
     @property
     def _CAPIPtr(self):
@@ -57,6 +58,14 @@ class Module:
         self._display_asm = None
 
     # -- B200 additions -----------------------------------------------------
+    @property
+    def source_text(self) -> str:
+        """The text this module was parsed from, unchanged (for a converted
+        kernel: the DSL's own xt text).  Stages never alter it."""
+        if self._source_asm is None:
+            raise ValueError("module has no source text (it was not created by xtile.parse)")
+        return self._source_asm
+
     def func_names(self) -> list[str]:
         return list(_native.func_names(self._raw_module))
 
@@ -71,7 +80,7 @@ class Module:
 
 def parse(asm: str) -> Module:
     wrapped, display = _wrap_module_asm(asm)
-    return Module(_native.parse(wrapped), display_asm=display)
+    return Module(_native.parse(wrapped), display_asm=display, source_asm=asm)
 
 
 def _run_stage(name: str, module: Any):
@@ -109,6 +118,14 @@ def nova_allocate(module: Any):
 
 def nova_to_x1(module: Any):
     return _run_stage("nova_to_x1", module)
+
+
+def canonicalize(module: Any):
+    """The xt dialect's canonicalization (``xt-opt --canonicalize`` of the
+    reference): ``x + 0``, ``0 + x`` and ``x - 0`` fold to ``x``
+    (``lib/xt/XTOps.cpp:395-449``) and unused side-effect-free ops are erased.
+    In place; returns the same module."""
+    return _run_stage("canonicalize", module)
 
 
 def compile(module: Any):  # noqa: A001 - the reference's name

@@ -107,6 +107,55 @@ int64_t clamp64(int64_t v, int64_t lo, int64_t hi) { return v < lo ? lo : (v > h
 // SM budget of the persistent (gemm, conv) kernels launched by this thread.
 thread_local int t_sm_budget = 0;
 
+}  // namespace
+
+namespace xt {
+
+// Launch arguments of the GEMM of plan ``p`` for the Blocks with bid0 in
+// [b0, b1) (a sub-range selects a contiguous slab of output rows), with the
+// calling thread's SM budget and ``error_word`` as the kernel's error word.
+// ``who`` prefixes error messages.  A range holding no rows gives out->M == 0.
+int gemm_launch_args(const Plan& p, void* const* args, int64_t b0, int64_t b1, uint32_t* error_word,
+                     const char* who, dev::GemmArgs* out) {
+  const GemmPlan& g = p.gemm;
+  dev::GemmArgs a{};
+  a.A = args[g.a_arg];
+  a.B = args[g.b_arg];
+  a.C = args[g.c_arg];
+  a.acc = g.acc_arg >= 0 ? static_cast<const float*>(args[g.acc_arg]) : nullptr;
+  a.N = g.N;
+  a.K = g.K;
+  a.lda = g.lda;
+  a.ldb = g.ldb;
+  a.ldc = g.ldc;
+  a.ab_elem = elem_code(g.ab_elem);
+  a.c_elem = elem_code(g.c_elem);
+  a.n_epi = static_cast<int>(g.epi.size());
+  if (a.n_epi > 4) return fail(XT_EUNSUPPORTED, std::string(who) + ": at most 4 epilogue steps are supported");
+  for (int i = 0; i < a.n_epi; ++i) {
+    a.epi_kind[i] = g.epi[i].kind;
+    a.epi_ptr[i] = static_cast<const float*>(args[g.epi[i].arg]);
+  }
+  a.error_word = error_word;
+  a.max_sms = t_sm_budget;
+  if (b0 == 0 && b1 == p.grid[0]) {
+    a.m_begin = 0;
+    a.M = g.M;
+  } else {
+    if (g.m_axis != 0)
+      return fail(XT_EARGUMENT, std::string(who) + ": output rows of @" + p.func + " are not indexed by xt.bid(0)");
+    const int64_t r0 = clamp64(b0 * g.tm, 0, g.M), r1 = clamp64(b1 * g.tm, 0, g.M);
+    a.m_begin = r0;
+    a.M = r1 - r0;
+  }
+  *out = a;
+  return XT_OK;
+}
+
+}  // namespace xt
+
+namespace {
+
 int launch_plan(const xt::Plan& p, void* const* args, int64_t b0, int64_t b1, cudaStream_t stream) {
   using namespace xt;
   const int64_t g0 = p.grid[0];
@@ -174,40 +223,12 @@ int launch_plan(const xt::Plan& p, void* const* args, int64_t b0, int64_t b1, cu
       return err == cudaSuccess ? XT_OK : cuda_fail(err, "rows kernel launch");
     }
     case Family::Gemm: {
-      const GemmPlan& g = p.gemm;
       Workspace* ws = nullptr;
       cudaError_t err = workspace(device, &ws);
       if (err != cudaSuccess) return cuda_fail(err, "workspace allocation");
       dev::GemmArgs a{};
-      a.A = args[g.a_arg];
-      a.B = args[g.b_arg];
-      a.C = args[g.c_arg];
-      a.acc = g.acc_arg >= 0 ? static_cast<const float*>(args[g.acc_arg]) : nullptr;
-      a.N = g.N;
-      a.K = g.K;
-      a.lda = g.lda;
-      a.ldb = g.ldb;
-      a.ldc = g.ldc;
-      a.ab_elem = elem_code(g.ab_elem);
-      a.c_elem = elem_code(g.c_elem);
-      a.n_epi = static_cast<int>(g.epi.size());
-      if (a.n_epi > 4) return fail(XT_EUNSUPPORTED, "at most 4 epilogue steps are supported");
-      for (int i = 0; i < a.n_epi; ++i) {
-        a.epi_kind[i] = g.epi[i].kind;
-        a.epi_ptr[i] = static_cast<const float*>(args[g.epi[i].arg]);
-      }
-      a.error_word = ws->error_word;
-      a.max_sms = t_sm_budget;
-      if (full) {
-        a.m_begin = 0;
-        a.M = g.M;
-      } else {
-        if (g.m_axis != 0)
-          return fail(XT_EARGUMENT, "xt_launch: output rows of @" + p.func + " are not indexed by xt.bid(0)");
-        int64_t r0 = clamp64(b0 * g.tm, 0, g.M), r1 = clamp64(b1 * g.tm, 0, g.M);
-        a.m_begin = r0;
-        a.M = r1 - r0;
-      }
+      int st = xt::gemm_launch_args(p, args, b0, b1, ws->error_word, "xt_launch", &a);
+      if (st != XT_OK) return st;
       if (a.M <= 0) return XT_OK;
       err = dev::launch_gemm(a, stream);
       return err == cudaSuccess ? XT_OK : cuda_fail(err, "gemm kernel launch");
@@ -358,6 +379,21 @@ int xt_run_pass(xt_module* module, const char* pass) {
   try {
     if (index == 0) module->unrolled = xt::serialize_module(*module->source);
     module->stage = index + 1 > module->stage ? index + 1 : module->stage;
+    return XT_OK;
+  } catch (const xt::Error& e) {
+    return fail(e);
+  }
+}
+
+int xt_canonicalize(xt_module* module) {
+  if (!module) return fail(XT_EARGUMENT, "xt_canonicalize: null argument");
+  try {
+    std::lock_guard<std::mutex> lock(module->mu);
+    xt::canonicalize_module(*module->source);
+    xt::verify_module(*module->source);
+    module->plans.clear();  // plans describe the program as it was
+    module->plan_errors.clear();
+    if (module->unrolled) module->unrolled = xt::serialize_module(*module->source);
     return XT_OK;
   } catch (const xt::Error& e) {
     return fail(e);

@@ -111,6 +111,10 @@ std::string print_module(const Module& m);
 // Unrolls every function's grid the way the reference's xt-serialize pass
 // does (lib/xt/XTSerialize.cpp:29-105); used for the stage dump only.
 std::unique_ptr<Module> serialize_module(const Module& m);
+// The xt dialect's canonicalization in place: x + 0, 0 + x and x - 0 fold to
+// x (lib/xt/XTOps.cpp:395-449), then side-effect-free ops left unused are
+// erased.
+void canonicalize_module(Module& m);
 
 // Grid of a function (attribute xt.grid), or {1,1,1} when absent.
 std::vector<int64_t> func_grid(const Func& f, bool* present = nullptr);

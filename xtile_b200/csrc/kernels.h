@@ -95,4 +95,12 @@ cudaError_t launch_conv(const ConvArgs& a, cudaStream_t stream);
 void* tensor_map_encoder();
 
 }  // namespace dev
+
+// Launch arguments of the GEMM of plan ``p`` for the Blocks with bid0 in
+// [b0, b1), the one place they are built for every GEMM entry point
+// (capi.cpp).  Returns XT_OK or an XT_E* code with the calling thread's last
+// error set.
+int gemm_launch_args(const Plan& p, void* const* args, int64_t b0, int64_t b1, uint32_t* error_word,
+                     const char* who, dev::GemmArgs* out);
+
 }  // namespace xt

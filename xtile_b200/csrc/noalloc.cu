@@ -17,7 +17,9 @@
 //    exits;
 //  * the first call on a device resolves the array's device address with
 //    cudaGetSymbolAddress (with that device current); make that first call
-//    before any stream capture;
+//    before any stream capture.  The address is kept for the process's
+//    lifetime: after cudaDeviceReset on a device it is stale, so do not call
+//    this entry point on a device that has been reset;
 //  * all calls share the array and it keeps the last call's contents: each
 //    call clears the error word on its stream before the kernel runs, and
 //    calls whose kernels overlap on the GPU race on that word;
@@ -42,6 +44,7 @@ namespace {
 
 constexpr size_t kScratchBytes = 256;
 constexpr size_t kGemmScratchBytes = sizeof(uint32_t);  // the error word
+static_assert(kGemmScratchBytes <= kScratchBytes, "the GEMM's scratch must fit the static array");
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) uint32_t g_scratch[kScratchBytes / sizeof(uint32_t)];
@@ -68,10 +71,6 @@ int scratch_address(int device, uint32_t** out) {
   return XT_OK;
 }
 
-uint8_t elem_code(xt::Elem e) {
-  return e == xt::Elem::BF16 ? xt::dev::kBF16 : e == xt::Elem::I8 ? xt::dev::kI8 : xt::dev::kF32;
-}
-
 }  // namespace
 
 extern "C" int xt_matmul_launch_noalloc(const xt_module* module, const char* func, void* const* args,
@@ -88,10 +87,6 @@ extern "C" int xt_matmul_launch_noalloc(const xt_module* module, const char* fun
   if (p->family != Family::Gemm)
     return record_error(XT_EUNSUPPORTED, "xt_matmul_launch_noalloc: @" + p->func + " maps onto the '" +
                                              family_name(p->family) + "' family; only matmul programs");
-  if (kGemmScratchBytes > kScratchBytes)
-    return record_error(XT_EARGUMENT, "xt_matmul_launch_noalloc: the launch needs " +
-                                          std::to_string(kGemmScratchBytes) + " scratch bytes, more than the " +
-                                          std::to_string(kScratchBytes) + " reserved");
   if (n_args != static_cast<int>(p->arg_types.size()))
     return record_error(XT_EARGUMENT, "xt_matmul_launch_noalloc: @" + p->func + " takes " +
                                           std::to_string(p->arg_types.size()) + " arrays, got " +
@@ -103,45 +98,14 @@ extern "C" int xt_matmul_launch_noalloc(const xt_module* module, const char* fun
       return record_error(XT_EARGUMENT,
                           "xt_matmul_launch_noalloc: array %" + p->arg_names[i] + " is not 16-byte aligned");
   }
-  const GemmPlan& g = p->gemm;
   const int64_t g0 = p->grid[0];
   const int64_t b0 = bid0_end <= 0 ? 0 : bid0_begin;
   const int64_t b1 = bid0_end <= 0 ? g0 : bid0_end;
   if (b0 < 0 || b1 > g0 || b0 > b1)
-    return record_error(XT_EARGUMENT, "xt_matmul_launch_noalloc: bid0 range outside the grid");
+    return record_error(XT_EARGUMENT, "xt_matmul_launch_noalloc: bid0 range [" + std::to_string(b0) + ", " +
+                                          std::to_string(b1) + ") is outside the grid's [0, " +
+                                          std::to_string(g0) + ")");
   if (b0 == b1) return XT_OK;
-
-  dev::GemmArgs a{};
-  a.A = args[g.a_arg];
-  a.B = args[g.b_arg];
-  a.C = args[g.c_arg];
-  a.acc = g.acc_arg >= 0 ? static_cast<const float*>(args[g.acc_arg]) : nullptr;
-  a.N = g.N;
-  a.K = g.K;
-  a.lda = g.lda;
-  a.ldb = g.ldb;
-  a.ldc = g.ldc;
-  a.ab_elem = elem_code(g.ab_elem);
-  a.c_elem = elem_code(g.c_elem);
-  a.n_epi = static_cast<int>(g.epi.size());
-  if (a.n_epi > 4) return record_error(XT_EUNSUPPORTED, "xt_matmul_launch_noalloc: more than 4 epilogue steps");
-  for (int i = 0; i < a.n_epi; ++i) {
-    a.epi_kind[i] = g.epi[i].kind;
-    a.epi_ptr[i] = static_cast<const float*>(args[g.epi[i].arg]);
-  }
-  if (b0 == 0 && b1 == g0) {
-    a.m_begin = 0;
-    a.M = g.M;
-  } else {
-    if (g.m_axis != 0)
-      return record_error(XT_EARGUMENT,
-                          "xt_matmul_launch_noalloc: output rows of @" + p->func + " are not indexed by xt.bid(0)");
-    const int64_t r0 = std::min(std::max<int64_t>(b0 * g.tm, 0), g.M);
-    const int64_t r1 = std::min(std::max<int64_t>(b1 * g.tm, 0), g.M);
-    a.m_begin = r0;
-    a.M = r1 - r0;
-  }
-  if (a.M <= 0) return XT_OK;
 
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
@@ -150,11 +114,16 @@ extern "C" int xt_matmul_launch_noalloc(const xt_module* module, const char* fun
   uint32_t* scratch = nullptr;
   int st = scratch_address(device, &scratch);
   if (st != XT_OK) return st;
+  // the same arguments xt_launch builds (SM budget included); only the error
+  // word's home differs
+  dev::GemmArgs a{};
+  st = gemm_launch_args(*p, args, b0, b1, scratch, "xt_matmul_launch_noalloc", &a);
+  if (st != XT_OK) return st;
+  if (a.M <= 0) return XT_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   e = cudaMemsetAsync(scratch, 0, kGemmScratchBytes, s);
   if (e != cudaSuccess)
     return record_error(XT_ECUDA, std::string("xt_matmul_launch_noalloc: clearing scratch: ") + cudaGetErrorString(e));
-  a.error_word = scratch;
   e = dev::launch_gemm(a, s);
   if (e != cudaSuccess)
     return record_error(XT_ECUDA, std::string("xt_matmul_launch_noalloc: gemm kernel launch: ") + cudaGetErrorString(e));

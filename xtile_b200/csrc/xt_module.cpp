@@ -178,6 +178,14 @@ PYBIND11_MODULE(_xtile, m) {
         name, [n](py::object module) { return run_pass(module, n.c_str()); }, py::arg("module"),
         ("Run the " + n + " stage in place and return the module.").c_str());
   }
+  m.def(
+      "canonicalize",
+      [](py::object module) {
+        int st = xt_canonicalize(unwrap(module));
+        if (st != XT_OK) raise_status(st, "xtile.canonicalize");
+        return module;
+      },
+      py::arg("module"), "Fold x + 0 / x - 0 and erase unused side-effect-free ops, in place.");
   m.def("plan", &plan, py::arg("module"), py::arg("func") = py::none());
   m.def(
       "ipc_export",
