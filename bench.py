@@ -522,6 +522,240 @@ def roofline_line(plan: dict, share: float, kernel_ms: float, peaks: dict, peak_
     return out
 
 
+# ---------------------------------------------------------------- checks
+def close_enough(got, ref, unit: str, dtype: str) -> dict:
+    """Compares ``got`` with the oracle's ``ref`` at the tolerance of the
+    workload's path: f32 elementwise programs bit-exact, the row softmax
+    1e-5 relative per element, bf16 tensor-core work (f32 accumulation)
+    max|d| / max|ref| <= 1e-2 and |d| <= 1e-2 |ref| + 1e-2 rms(ref)."""
+    import numpy as np
+
+    got = np.asarray(got)
+    ref = np.asarray(ref)
+    if dtype == "bf16":
+        g, r = got.astype(np.float64), ref.astype(np.float64)
+        d = np.abs(g - r)
+        scale = float(np.max(np.abs(r))) or 1.0
+        rms = float(np.sqrt(np.mean(r * r)))
+        ok = bool(d.max() / scale <= 1e-2 and np.all(d <= 1e-2 * np.abs(r) + 1e-2 * rms))
+        return {"ok": ok, "max_rel": float(d.max() / scale),
+                "tolerance": "max|d|/max|ref| <= 1e-2 and |d| <= 1e-2|ref| + 1e-2 rms(ref)"}
+    if unit == "GB/s" and np.all(np.isfinite(ref)) and np.all(ref > 0) and np.all(ref <= 1):
+        rel = float(np.max(np.abs(got.astype(np.float64) - ref) / ref))
+        return {"ok": rel <= 1e-5, "max_rel": rel, "tolerance": "|d|/ref <= 1e-5 (softmax)"}
+    same = bool(np.array_equal(got.view(np.uint32), ref.view(np.uint32)))
+    return {"ok": same, "max_rel": 0.0 if same else float(np.max(np.abs(got - ref))), "tolerance": "bit-exact"}
+
+
+def sample_check(w: dict, out, torch, n_blocks: int = 8, seed: int = 0, blocks=None) -> dict:
+    """Checks a seeded sample of the Grid's Blocks of the device output ``out``
+    against the CPU oracle run on those Blocks only (the oracle reads the DSL's
+    own text).  Entries the sampled Blocks do not store are not compared."""
+    import numpy as np
+    from oracle import xt_oracle
+
+    func = xt_oracle.parse_module(w["text"])[0]
+    order = xt_oracle.serialize_order(func.grid)
+    if blocks is None:
+        rng = np.random.default_rng(seed)
+        picks = sorted(rng.choice(len(order), size=min(n_blocks, len(order)), replace=False))
+        blocks = [order[i] for i in picks]
+    arrays = oracle_arrays(w, torch)
+    pos = w.get("out_pos", len(w["inputs"]))
+    if arrays[pos].dtype != np.float32:
+        raise ValueError("sample_check compares f32 outputs")
+    arrays[pos][...] = np.nan  # marks what the sampled Blocks do not store
+    xt_oracle.run(w["text"], arrays, blocks=blocks)
+    ref = arrays[pos]
+    mask = ~np.isnan(ref)
+    got = out.cpu().numpy()[mask]
+    res = close_enough(got, ref[mask], w["unit"], w["dtype"])
+    return {"ok": res["ok"], "blocks": len(blocks), "values": int(mask.sum()), "max_rel": res["max_rel"],
+            "tolerance": res["tolerance"], "seed": seed}
+
+
+def gather_check(w: dict, out, shares: list, rows_per_block: int, torch, per_shard: int = 3, seed: int = 0) -> dict:
+    """The rows rank 0 gathered: ``per_shard`` seeded Blocks of every rank's
+    bid0 range against the oracle, and the full rows on both sides of every
+    boundary between two ranks' ranges against fp64 dot products."""
+    import numpy as np
+    from oracle import xt_oracle
+
+    rng = np.random.default_rng(seed)
+    gx, gy, gz = xt_oracle.parse_module(w["text"])[0].grid
+    blocks = [(int(rng.integers(lo, hi)), int(rng.integers(0, gy)), int(rng.integers(0, gz)))
+              for lo, hi in shares for _ in range(per_shard)]
+    blk = sample_check(w, out, torch, blocks=blocks)
+    rows = sorted({r for lo, _ in shares[1:] for r in (lo * rows_per_block - 1, lo * rows_per_block)})
+    a, b = w["inputs"][0], w["inputs"][1]
+    ref = (a[rows].double() @ b.double()).numpy()
+    row = close_enough(out[rows].cpu().numpy(), ref, w["unit"], w["dtype"])
+    return {"ok": bool(blk["ok"] and row["ok"]), "blocks": blk["blocks"], "block_max_rel": blk["max_rel"],
+            "rows": len(rows), "row_max_rel": row["max_rel"], "max_rel": max(blk["max_rel"], row["max_rel"]),
+            "tolerance": row["tolerance"], "seed": seed}
+
+
+# ---------------------------------------------------------------- timing helpers
+def capture_graph(step, steps: int, dev, torch):
+    """``steps`` calls of ``step(i)`` captured in one CUDA graph, with the two
+    timing events recorded inside it (so the interval is the launches on the
+    device, not the host's graph-launch latency)."""
+    g_begin = torch.cuda.Event(enable_timing=True, external=True)
+    g_end = torch.cuda.Event(enable_timing=True, external=True)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        cap = torch.cuda.current_stream(dev)
+        g_begin.record(cap)
+        for i in range(steps):
+            step(i)
+        g_end.record(cap)
+    graph.replay()
+    torch.cuda.synchronize()
+    return graph, g_begin, g_end
+
+
+def rotating_sets(w: dict, dev, torch):
+    """Device copies of the inputs and an output, repeated until the sets
+    together exceed three times the 126 MB L2 (each launch then reads its
+    inputs from HBM)."""
+    inputs_dev = [t.to(dev) for t in w["inputs"]]
+    out = torch.empty(w["out_shape"], dtype=w["out_dtype"], device=dev)
+    ws_bytes = sum(t.numel() * t.element_size() for t in inputs_dev) + out.numel() * out.element_size()
+    n_sets = 1 if ws_bytes > 3 * L2_BYTES else int(-(-3 * L2_BYTES // ws_bytes)) + 1
+    sets = [(inputs_dev, out)] + [([t.clone() for t in inputs_dev], torch.empty_like(out))
+                                  for _ in range(n_sets - 1)]
+    return sets
+
+
+def gpu_id_of(dev, torch) -> str:
+    uuid = str(getattr(torch.cuda.get_device_properties(dev), "uuid", dev.index))
+    return uuid if uuid.startswith("GPU-") or uuid.isdigit() else f"GPU-{uuid}"
+
+
+PER_CONFIG = ("add", "softmax", "matmul", "conv2d")
+
+
+def run_per_config(xt, torch, dev, peaks: dict, peak_kind: str, steps: int = 50, warmup: int = 5,
+                   region_ms: float = 300.0) -> dict:
+    """BASELINE configurations 1-4 on one GPU, each timed like the headline's
+    graph mode (K launches in a CUDA graph over rotating buffer sets, events
+    inside the graph), replayed for about ``region_ms`` with the clocks
+    sampled, then checked on a seeded sample of Blocks against the oracle."""
+    out = {}
+    for name in PER_CONFIG:
+        w = build_workload(name, load_dsl(), torch, 1, 0)
+        mod = xt.parse(w["text"])
+        plan = mod.plan()
+        sets = rotating_sets(w, dev, torch)
+        n_sets = len(sets)
+
+        def step(i, sets=sets, mod=mod, w=w):
+            ins, o = sets[i % len(sets)]
+            xt.launch(mod, *launch_arrays(w, ins, o))
+
+        for i in range(warmup):
+            step(i)
+        torch.cuda.synchronize()
+        graph, g_begin, g_end = capture_graph(step, steps, dev, torch)
+        one = g_begin.elapsed_time(g_end)
+        replays = max(3, int(region_ms / max(one, 1e-3)))
+        times = []
+        with ClockSampler(gpu_id_of(dev, torch)) as clocks:
+            for _ in range(replays):
+                graph.replay()
+                torch.cuda.synchronize()
+                times.append(g_begin.elapsed_time(g_end))
+        del graph
+        ms = statistics.fmean(times) / steps
+        scale = 1e12 if w["unit"] in OPS_UNITS else 1e9
+        roof = roofline_line(plan, 1.0, ms, peaks, peak_kind)
+        roof["traffic"] = NCU_TRAFFIC_BYTES.get(name)
+        out[name] = {"value": round(w["work"] / (ms * 1e-3) / scale, 3), "unit": w["unit"],
+                     "ms_per_launch": round(ms, 5), "launches": steps * replays, "roofline": roof,
+                     "clocks": clocks.summary(), "l2": f"{n_sets} rotating input/output sets",
+                     "timing": "CUDA-graph replay of K launches, events recorded inside the graph",
+                     "parity": sample_check(w, sets[0][1], torch), "config": w["config"]}
+        del sets
+        torch.cuda.empty_cache()
+    return out
+
+
+def _cudart(torch):
+    """torch's CUDA runtime (the same primary contexts), for plain copies."""
+    import ctypes
+    import glob
+
+    base = Path(torch.__file__).resolve().parent
+    for pat in ("../nvidia/cuda_runtime/lib/libcudart.so*", "lib/libcudart*.so*"):
+        hits = sorted(glob.glob(str(base / pat)))
+        if hits:
+            lib = ctypes.CDLL(hits[0])
+            lib.cudaMemcpyAsync.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int,
+                                            ctypes.c_void_p]
+            return lib
+    return None
+
+
+def measure_ingest(xt, torch, dev, dist, rank: int, world: int, src, target, rows: tuple, flag,
+                   reps: int = 3) -> dict:
+    """Rate at which rank 0 takes in rows over NVLink while every other rank
+    sends its rows [rows[0], rows[1]) at once, measured on rank 0 between two
+    all-reduces that bracket the transfer (max over none needed: rank 0's
+    interval covers every sender).  Two senders: this repository's ew kernel
+    (a load/store Block program whose output is rank 0's array, the same
+    SM-issued stores the GEMM's epilogue makes) and the copy engines (one
+    cudaMemcpyAsync per rank, device to peer device)."""
+    dsl = load_dsl()
+    A = dsl.Array
+    n_rows, n_cols = src.shape
+
+    @dsl.kernel
+    def copy_rows(inp, out, trow, col):
+        i = dsl.bid(0)
+        dsl.store(out, index=(i, 0), tile=dsl.load(inp, index=(i, 0), shape=(trow, col)))
+
+    trow = 32
+    mod = xt.parse(dsl.trace_text(copy_rows, args=(A((n_rows, n_cols), dsl.float32), A((n_rows, n_cols), dsl.float32),
+                                                   trow, n_cols), grid=(n_rows // trow, 1, 1), double_buffering=True))
+    lo, hi = rows
+    nbytes = (hi - lo) * n_cols * 4
+    total = torch.tensor([float(nbytes if rank else 0)], device=dev)
+    dist.all_reduce(total)
+    cudart = _cudart(torch)
+    stream = torch.cuda.current_stream(dev)
+    res = {}
+    for how in ("sm_stores", "copy_engines"):
+        if how == "copy_engines" and cudart is None:
+            continue
+        best = None
+        for _ in range(reps):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            dist.all_reduce(flag)
+            e0.record(stream)
+            if rank != 0 and hi > lo:
+                if how == "sm_stores":
+                    xt.launch(mod, src, target, bid0_range=(lo // trow, hi // trow))
+                else:
+                    off = lo * n_cols * 4
+                    rc = cudart.cudaMemcpyAsync(target.data_ptr() + off, src.data_ptr() + off, nbytes, 4,
+                                                stream.cuda_stream)
+                    if rc != 0:
+                        raise RuntimeError(f"cudaMemcpyAsync to rank 0 failed: {rc}")
+            dist.all_reduce(flag)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1)
+            best = ms if best is None else min(best, ms)
+        t = torch.tensor([best], device=dev)
+        dist.broadcast(t, src=0)  # rank 0's interval is the one that covers every sender
+        res[how] = round(total.item() / (t.item() * 1e-3) / 1e9, 1)
+    res["bytes"] = int(total.item())
+    res["how"] = ("rank 0 times, between two all-reduces, every other rank sending its equal share of the "
+                  "output rows at once; best of %d" % reps)
+    return res
+
+
 # ---------------------------------------------------------------- main
 def main() -> None:
     ap = argparse.ArgumentParser()
@@ -541,6 +775,8 @@ def main() -> None:
                     help="peer gather: rank 0's fraction of the Grid (default: balanced against its NVLink ingress)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-per-config", action="store_true",
+                    help="skip configurations 1-4 beside the default (sharded_matmul) line on one GPU")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -587,28 +823,19 @@ def main() -> None:
     peer = sharded and world > 1 and args.gather == "peer"
     # equal ranges: compute-only scaling (output left in place) and the NCCL gather
     even_lo, even_hi = bid0_share(grid0, world, rank) if sharded else (0, grid0)
-    root_share = None
-    if peer:
-        out_bytes = w["out_shape"][0] * w["out_shape"][1] * 4
-        root_share = args.root_share if args.root_share is not None else gather_root_share(
-            world, plan["flops"], out_bytes)
-    lo, hi = bid0_share(grid0, world, rank, root_share) if sharded else (0, grid0)
     rows_per_block = w["out_shape"][0] // grid0
     rows_per_rank = w["out_shape"][0] // world if sharded else 0
 
     # device-resident inputs; rotate enough sets to defeat the 126 MB L2
-    inputs_dev = [t.to(dev) for t in w["inputs"]]
-    out = torch.empty(w["out_shape"], dtype=w["out_dtype"], device=dev)
-    ws_bytes = sum(t.numel() * t.element_size() for t in inputs_dev) + out.numel() * out.element_size()
-    n_sets = 1 if ws_bytes > 3 * L2_BYTES else int(-(-3 * L2_BYTES // ws_bytes)) + 1
     if sharded:
         # two output buffers: step i + 1 computes into one while step i's rows
         # are still being gathered out of the other
-        n_sets = 2
+        inputs_dev = [t.to(dev) for t in w["inputs"]]
+        out = torch.empty(w["out_shape"], dtype=w["out_dtype"], device=dev)
         sets = [(inputs_dev, out), (inputs_dev, torch.empty_like(out))]
     else:
-        sets = [(inputs_dev, out)] + [([t.clone() for t in inputs_dev], torch.empty_like(out))
-                                      for _ in range(n_sets - 1)]
+        sets = rotating_sets(w, dev, torch)
+    n_sets = len(sets)
     stream = torch.cuda.current_stream(dev)
     comm = torch.cuda.Stream(dev) if sharded else None
     # peer gather: every rank's kernel stores its rows into rank 0's output
@@ -617,15 +844,50 @@ def main() -> None:
     targets = [o for _, o in sets]
     flag = torch.zeros(1, device=dev)
     if peer:
-        b0 = bid0_share(grid0, world, 0, root_share)[1]
-        w["config"]["parallelism"] = (f"bid0 split over {world} GPUs, rank 0 {b0} of {grid0} Blocks, the others "
-                                      f"{(grid0 - b0) // (world - 1)}-{-(-(grid0 - b0) // (world - 1))}; each "
-                                      f"rank's kernel stores its C rows into rank 0's output over NVLink (CUDA IPC)")
         handles = [xt.export_array(o) for o in targets] if rank == 0 else None
         box = [handles]
         dist.broadcast_object_list(box, src=0)
         if rank != 0:
             targets = [xt.PeerArray.open(h, tuple(w["out_shape"]), w["out_dtype"]) for h in box[0]]
+
+    # ---- peer gather: rank 0's share of the Grid from rates measured here.
+    # T: the whole GEMM on one GPU (every rank times its equal share; the
+    # slowest share times N).  R: rank 0 taking in the whole output at the
+    # ingest rate of SM-issued stores from all other ranks at once.
+    rates = None
+    root_share = None
+    if peer:
+        for i in range(2):  # warm the GEMM's tensor maps and clocks
+            xt.launch(mod, *launch_arrays(w, sets[0][0], sets[0][1]), bid0_range=(even_lo, even_hi))
+        torch.cuda.synchronize()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        for i in range(3):
+            xt.launch(mod, *launch_arrays(w, sets[0][0], sets[0][1]), bid0_range=(even_lo, even_hi))
+        c1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([c0.elapsed_time(c1) / 3], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        gemm_ms = t.item() * world
+        src = sets[1][1]  # a local buffer of the output's shape (rank 0's is never sent)
+        rows = (even_lo * rows_per_block, even_hi * rows_per_block)
+        ingest = measure_ingest(xt, torch, dev, dist, rank, world, src, targets[0], rows, flag)
+        out_bytes = w["out_shape"][0] * w["out_shape"][1] * 4
+        tflops = plan["flops"] / (gemm_ms * 1e-3) / 1e12
+        rates = {"gemm_tflops_1gpu": round(tflops, 1), "gemm_ms_1gpu": round(gemm_ms, 4), "ingest_gbs": ingest}
+        root_share = args.root_share if args.root_share is not None else gather_root_share(
+            world, plan["flops"], out_bytes, tflops=tflops, ingest_gbs=ingest["sm_stores"])
+        r_ms = out_bytes / (ingest["sm_stores"] * 1e9) * 1e3
+        rates["bound_ms"] = round(gemm_ms * r_ms / (gemm_ms + r_ms), 4)  # T*R/(T+R): no split does better
+        rates["bound_note"] = ("T*R/(T+R): T the one-GPU GEMM, R rank 0 taking in the whole output at the "
+                               "measured SM-store ingest rate")
+    lo, hi = bid0_share(grid0, world, rank, root_share) if sharded else (0, grid0)
+    shares = [bid0_share(grid0, world, r, root_share) for r in range(world)] if sharded else [(0, grid0)]
+    if peer:
+        b0 = shares[0][1]
+        w["config"]["parallelism"] = (f"bid0 split over {world} GPUs, rank 0 {b0} of {grid0} Blocks, the others "
+                                      f"{(grid0 - b0) // (world - 1)}-{-(-(grid0 - b0) // (world - 1))}; each "
+                                      f"rank's kernel stores its C rows into rank 0's output over NVLink (CUDA IPC)")
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     computed = [torch.cuda.Event() for _ in range(n_sets)]
     gathered = [torch.cuda.Event() for _ in range(n_sets)]
@@ -682,23 +944,11 @@ def main() -> None:
     # the launches would add gaps of their own, so there are none.)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    g_begin = torch.cuda.Event(enable_timing=True, external=True)
-    g_end = torch.cuda.Event(enable_timing=True, external=True)
     if use_graph:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            cap = torch.cuda.current_stream(dev)
-            g_begin.record(cap)
-            for i in range(args.steps):
-                step(i)
-            g_end.record(cap)
-        graph.replay()
-        torch.cuda.synchronize()
+        graph, g_begin, g_end = capture_graph(step, args.steps, dev, torch)
     t_begin = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
-    uuid = str(getattr(torch.cuda.get_device_properties(dev), "uuid", local))
-    gpu_id = uuid if uuid.startswith("GPU-") or uuid.isdigit() else f"GPU-{uuid}"
-    with ClockSampler(gpu_id) as clocks:
+    with ClockSampler(gpu_id_of(dev, torch)) as clocks:
         torch.cuda.synchronize()
         if dist:
             dist.barrier()
@@ -726,6 +976,20 @@ def main() -> None:
         total_ms, kernel_ms = t.tolist()
     clock = clocks.summary()
     err = xt.device_error()
+
+    # ---- correctness of what the timed steps produced (after the timed
+    # region): a seeded sample of Blocks against the oracle; on N GPUs, rank 0
+    # checks the rows it gathered from every rank (the others wait at the
+    # next barrier)
+    parity = None
+    last_out = sets[(args.steps - 1) % n_sets][1]
+    if w["out_dtype"] == torch.float32:
+        if world == 1:
+            parity = sample_check(w, last_out, torch)
+        elif sharded and rank == 0:
+            parity = gather_check(w, last_out, shares, rows_per_block, torch)
+    if dist:
+        dist.barrier()
 
     # ---- compute-only timing (sharded: no gather), for the scaling report
     compute = None
@@ -889,11 +1153,28 @@ def main() -> None:
                                 "value": round(work / (compute * 1e-3) / scale, 3)}
         line["gather"] = {"ms_per_step": round(ms_per_step - compute, 4),
                           "bytes": (w["out_shape"][0] - (hi - lo) * rows_per_block) * w["out_shape"][1] * 4}
+    if parity is not None:
+        line["parity" if world == 1 else "gather_check"] = parity
+    if rates is not None:
+        # which term of the step model binds at this split: rank 0's own share,
+        # rank 0's ingress of the others' rows, or another rank's share
+        f = shares[0][1] / grid0
+        t_ms, r_ms = rates["gemm_ms_1gpu"], w["out_shape"][0] * w["out_shape"][1] * 4 / (
+            rates["ingest_gbs"]["sm_stores"] * 1e9) * 1e3
+        terms = {"rank 0's own share of the GEMM": f * t_ms, "rank 0's NVLink ingress of the other ranks' rows":
+                 (1 - f) * r_ms, "the other ranks' shares of the GEMM": (1 - f) * t_ms / (world - 1)}
+        rates["model_ms"] = {k: round(v, 4) for k, v in terms.items()}
+        rates["limiter"] = max(terms, key=terms.get)
+        rates["efficiency_vs_bound"] = round(rates["bound_ms"] / ms_per_step, 4)
+        line["gather_rates"] = rates
     if e2e is not None:
         e_ms, h2d, d2h, e_note = e2e
         line["e2e"] = {"value": round(job_units / (e_ms * 1e-3) / scale, 3), "unit": w["unit"],
                        "ms_per_step": round(e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                        "pipelining": e_note}
+    if world == 1 and args.workload == "sharded_matmul" and not args.no_per_config:
+        # BASELINE configurations 1-4, one GPU each, beside the headline
+        line["per_config"] = run_per_config(xt, torch, dev, peaks, peak_kind)
     if not args.no_cpu and world == 1:  # the host-core baseline is a 1-GPU figure
         line["cpu_baseline"] = cpu_baseline(w, torch)
     print(json.dumps(line), flush=True)

@@ -117,3 +117,58 @@ def test_reference_arm_loads_no_library_of_this_repository(tmp_path):
     line = out["line"]
     assert line["impl"] == "reference" and line["value"] > 0 and line["unit"] == "GB/s"
     assert line["cpu_baseline"]["cores"] >= 1 and line["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def _small_matmul_workload(torch):
+    dsl = bench.load_dsl()
+    A = dsl.Array
+
+    @dsl.kernel
+    def matmul_rows(lhs, rhs, out, tm, tn, tk):
+        i, j = dsl.bid(0), dsl.bid(1)
+        a = dsl.load(lhs, index=(i, 0), shape=(tm, tk))
+        b = dsl.load(rhs, index=(0, j), shape=(tk, tn), shared=1)
+        dsl.store(out, index=(i, j), tile=dsl.matmul(a, b))
+
+    M, N, K = 64, 48, 32
+    g = torch.Generator().manual_seed(3)
+    a = (torch.randn(M, K, generator=g) / 4).to(torch.bfloat16)
+    b = (torch.randn(K, N, generator=g) / 4).to(torch.bfloat16)
+    text = dsl.trace_text(matmul_rows, args=(A((M, K), dsl.bfloat16), A((K, N), dsl.bfloat16), A((M, N), dsl.float32),
+                                             8, 16, K), grid=(8, 3, 1), double_buffering=True)
+    w = dict(text=text, inputs=[a, b], out_shape=(M, N), out_dtype=torch.float32, unit="TFLOP/s", dtype="bf16",
+             work=2 * M * N * K)
+    full = (a.double() @ b.double()).float()
+    return w, full
+
+
+def test_sample_check_passes_the_right_output_and_catches_a_planted_error():
+    import torch
+    w, full = _small_matmul_workload(torch)
+    c = bench.sample_check(w, full, torch, n_blocks=24)
+    assert c["ok"] and c["blocks"] == 24 and c["values"] == 64 * 48
+    bad = full.clone()
+    bad[13, 7] += 1.0  # a wrong value in a sampled Block
+    assert not bench.sample_check(w, bad, torch, n_blocks=24)["ok"]
+
+
+def test_gather_check_covers_every_shard_and_the_boundary_rows():
+    import torch
+    w, full = _small_matmul_workload(torch)
+    shares = [bench.bid0_share(8, 3, r, 0.5) for r in range(3)]
+    c = bench.gather_check(w, full, shares, 8, torch)
+    assert c["ok"] and c["blocks"] == 9 and c["rows"] == 4
+    bad = full.clone()
+    bad[shares[1][0] * 8, 40] -= 0.5  # first row of rank 1's range
+    assert not bench.gather_check(w, bad, shares, 8, torch)["ok"]
+
+
+def test_close_enough_modes():
+    import numpy as np
+    x = np.array([0.25, 0.5], np.float32)
+    assert bench.close_enough(x, x.copy(), "GB/s", "f32")["ok"]
+    assert bench.close_enough(x, x * (1 + 1e-4), "GB/s", "f32")["tolerance"].startswith("|d|/ref")
+    assert not bench.close_enough(x, x * (1 + 1e-4), "GB/s", "f32")["ok"]
+    y = np.array([-1.5, 2.0], np.float32)
+    assert not bench.close_enough(y, np.nextafter(y, np.inf), "GB/s", "f32")["ok"]  # bit-exact for add
+    assert bench.close_enough(y * 1.001, y, "TFLOP/s", "bf16")["ok"]
