@@ -329,8 +329,8 @@ def test_matmul_config5_shards_full_size():
     """
     import bench
 
-    w = bench.build_workload("sharded_matmul", xt, torch, 1, 0)
-    m = w["module"]
+    w = bench.build_workload("sharded_matmul", bench.load_dsl(), torch, 1, 0)
+    m = xt.parse(w["text"])
     a_h, b_h = w["inputs"]
     a, b = a_h.to(DEV), b_h.to(DEV)
     M, N = w["out_shape"]
