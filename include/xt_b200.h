@@ -135,6 +135,18 @@ int xt_device_error(uint32_t* out_code);
  * GEMM rounds the budget down to an even number (its CTAs come in pairs). */
 int xt_set_sm_budget(int sms);
 
+/* No counterpart in the reference.  Sets how long a pipeline wait (TMA data,
+ * MMA completion, accumulator hand-off) of the gemm and conv kernels that the
+ * calling thread launches later may take before the kernel gives up: it then
+ * records a code in the error word (read with xt_device_error: 0x101-0x103
+ * gemm, 0x201-0x203 conv), stops every role, lets issued copies and MMAs
+ * land, frees its tensor memory and returns, leaving the context usable.
+ * ``ns`` 0 restores the default (about 2 s); at most 60 s.  Every wait takes
+ * at least a few tens of microseconds before it can give up, whatever the
+ * limit.  Teardown drains keep their own limits.  Used to test the failure
+ * path; production keeps the default. */
+int xt_set_wait_limit_ns(uint64_t ns);
+
 /* No counterpart in the reference.  CUDA IPC for row gathers without a
  * collective: xt_ipc_export gives the 64-byte handle of the device allocation
  * holding ``ptr`` and ptr's byte offset in it; xt_ipc_open maps such an

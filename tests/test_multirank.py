@@ -118,3 +118,73 @@ def test_gather_root_share_balances_compute_and_ingress():
         assert (1 - f) / (world - 1) * t <= f * t
     # slower links give rank 0 more of the Grid
     assert bench.gather_root_share(8, flops, out_bytes, ingest_gbs=300.0) > bench.gather_root_share(8, flops, out_bytes)
+
+
+# ---------------------------------------------------------------------------
+# Failure detection on the host (gloo ranks, no GPU): a rank that never joins,
+# and a rank that leaves between steps.  The surviving rank must end with an
+# error within a bounded time, never hang.
+# ---------------------------------------------------------------------------
+def never_joins_worker(rank, world, port, result_q):
+    import datetime
+    import time
+
+    if rank == 1:
+        return  # this rank never joins the process group
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    t0 = time.monotonic()
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+        result_q.put(("joined", time.monotonic() - t0))
+        dist.destroy_process_group()
+    except Exception as e:  # noqa: BLE001 - the error itself is what is checked
+        result_q.put((type(e).__name__, time.monotonic() - t0))
+
+
+def test_rank_that_never_joins_ends_with_an_error():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=never_joins_worker, args=(r, 2, free_port(), q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    kind, secs = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+    assert kind != "joined"
+    assert secs < 60
+
+
+def leaves_between_steps_worker(rank, world, port, result_q):
+    import datetime
+    import time
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    t = torch.ones(4)
+    dist.all_reduce(t)  # step 0: both ranks
+    if rank == 1:
+        os._exit(0)  # leaves between steps, nothing in flight
+    t0 = time.monotonic()
+    try:
+        dist.all_reduce(t)  # step 1: the peer is gone
+        result_q.put(("completed", time.monotonic() - t0))
+    except Exception as e:  # noqa: BLE001
+        result_q.put((type(e).__name__, time.monotonic() - t0))
+
+
+def test_rank_that_leaves_between_steps_fails_the_next_collective():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=leaves_between_steps_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    kind, secs = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.terminate()
+    assert kind != "completed"
+    assert secs < 60

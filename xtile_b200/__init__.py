@@ -56,7 +56,7 @@ from .api import (
     xt_serialize,
     xt_to_nova,
 )
-from .runtime import PeerArray, device_error, export_array, launch, run, sm_budget
+from .runtime import PeerArray, device_error, export_array, launch, run, sm_budget, wait_limit
 
 __all__ = [
     "Array", "DType", "Module", "PeerArray", "add", "astype", "bfloat16", "bid", "canonicalize", "cdiv", "compile",
@@ -65,5 +65,5 @@ __all__ = [
     "matmul", "max", "mma", "mul", "nova_allocate", "nova_barrier", "nova_optimize",
     "nova_threading", "nova_to_x1", "parse", "reciprocal", "reshape", "rsqrt", "run",
     "save_compile_results", "save_ir", "sigmoid", "silu", "sin", "sm_budget", "store", "sub", "sum", "tanh",
-    "transpose", "truediv", "xt_serialize", "xt_to_nova",
+    "transpose", "truediv", "wait_limit", "xt_serialize", "xt_to_nova",
 ]

@@ -107,6 +107,13 @@ int64_t clamp64(int64_t v, int64_t lo, int64_t hi) { return v < lo ? lo : (v > h
 // SM budget of the persistent (gemm, conv) kernels launched by this thread.
 thread_local int t_sm_budget = 0;
 
+// Pipeline wait limit of the gemm and conv kernels launched by this thread,
+// in nanoseconds (0: the kernels' default of about 2 s).  Kernels count SM
+// cycles; at the B200's 1.9-2.0 GHz SM clock a nanosecond is 2 cycles.
+thread_local uint64_t t_wait_limit_ns = 0;
+
+uint64_t wait_limit_cycles() { return t_wait_limit_ns * 2; }
+
 }  // namespace
 
 namespace xt {
@@ -138,6 +145,7 @@ int gemm_launch_args(const Plan& p, void* const* args, int64_t b0, int64_t b1, u
   }
   a.error_word = error_word;
   a.max_sms = t_sm_budget;
+  a.wait_limit_cycles = wait_limit_cycles();
   if (b0 == 0 && b1 == p.grid[0]) {
     a.m_begin = 0;
     a.M = g.M;
@@ -261,6 +269,7 @@ int launch_plan(const xt::Plan& p, void* const* args, int64_t b0, int64_t b1, cu
       a.elem = elem_code(c.elem);
       a.error_word = ws->error_word;
       a.max_sms = t_sm_budget;
+      a.wait_limit_cycles = wait_limit_cycles();
       if (full) {
         a.n_begin = 0;
         a.ON = c.ON;
@@ -600,6 +609,12 @@ int xt_ipc_close(void* base) {
 int xt_set_sm_budget(int sms) {
   if (sms < 0) return fail(XT_EARGUMENT, "xt_set_sm_budget: negative SM count");
   t_sm_budget = sms;
+  return XT_OK;
+}
+
+int xt_set_wait_limit_ns(uint64_t ns) {
+  if (ns > 60ull * 1000000000ull) return fail(XT_EARGUMENT, "xt_set_wait_limit_ns: more than 60 s");
+  t_wait_limit_ns = ns;
   return XT_OK;
 }
 

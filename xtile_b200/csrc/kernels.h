@@ -72,6 +72,7 @@ struct GemmArgs {
   const float* epi_ptr[4];
   uint32_t* error_word;
   int max_sms;             // SMs the persistent grid may occupy (0: all)
+  uint64_t wait_limit_cycles;  // SM cycles a pipeline wait may take before the kernel gives up (0: 2 s)
 };
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream);
 
@@ -88,6 +89,7 @@ struct ConvArgs {
   uint8_t elem;
   uint32_t* error_word;
   int max_sms;             // SMs the persistent grid may occupy (0: all)
+  uint64_t wait_limit_cycles;  // SM cycles a pipeline wait may take before the kernel gives up (0: 2 s)
 };
 cudaError_t launch_conv(const ConvArgs& a, cudaStream_t stream);
 

@@ -73,6 +73,7 @@ struct Params {
   int tmem_cols;
   uint32_t idesc;
   uint32_t* error_word;
+  uint64_t wait_limit;  // SM cycles per pipeline wait
 };
 
 template <int AB>
@@ -154,7 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   griddep_launch_dependents();
   griddep_wait();
   const uint32_t tmem_base = *tmem_slot;
-  const Abort ab{abort_flag, p.error_word};
+  const Abort ab{abort_flag, p.error_word, p.wait_limit};
   const int num_kb = p.KH * p.KW * p.kc;
   const int chunk_elems = p.b_span / T::kEb;
 
@@ -398,6 +399,7 @@ struct WinParams {
   int64_t out_h, out_w, out_c;
   int v8;  // output rows 32-byte aligned: 32-byte stores
   uint32_t* error_word;
+  uint64_t wait_limit;  // SM cycles per pipeline wait
 };
 
 __device__ __forceinline__ void win_tile(const WinParams& p, int t, int& n, int& w0, int& f0) {
@@ -493,7 +495,7 @@ __global__ void __launch_bounds__(kWinThreads, 1)
   griddep_launch_dependents();
   griddep_wait();
   const uint32_t tmem_base = *tmem_slot;
-  const Abort ab{abort_flag, p.error_word};
+  const Abort ab{abort_flag, p.error_word, p.wait_limit};
   const int n_fbars = p.KH < kMaxFBars ? p.KH : kMaxFBars;
 
   if (warp == 0) {
@@ -807,6 +809,7 @@ bool launch_window(const ConvArgs& a, const CUtensorMap& m_f, int span, EncodeIn
   p.out_c = a.out_c;
   p.v8 = a.out_c % 8 == 0 && reinterpret_cast<uintptr_t>(a.out) % 32 == 0;
   p.error_word = a.error_word;
+  p.wait_limit = wait_limit_or_default(a.wait_limit_cycles);
   *err = cudaSuccess;
   if (p.num_tiles == 0) return true;
   const int smem = p.barrier_offset + 256 + 1024;
@@ -933,6 +936,7 @@ cudaError_t launch_typed(const ConvArgs& a, cudaStream_t stream) {
   p.tmem_cols = cols;
   p.idesc = instr_desc(AB == kBF16 ? 1 : 2, 1, 1, 0, 1, kBM, static_cast<uint32_t>(p.N));
   p.error_word = a.error_word;
+  p.wait_limit = wait_limit_or_default(a.wait_limit_cycles);
   if (p.num_tiles == 0) return cudaSuccess;
   const int smem = p.barrier_offset + 256 + 1024;
   cudaError_t e = cudaFuncSetAttribute(conv_tc<AB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

@@ -56,7 +56,16 @@ struct Params {
   const float* epi_ptr[4];
   int tma_store;  // plain f32 output: epilogue stores through shared memory with TMA
   uint32_t* error_word;
+  uint64_t wait_limit;  // SM cycles per pipeline wait
 };
+
+// After an abort, the time a CTA waits before it passes the final cluster
+// barrier: every TMA load a producer issued lands within it.  A pair's
+// producers issue into their own shared memory but complete on the leader's
+// barriers, and the follower cannot observe those; the leader drains the
+// stages it armed, and this wait covers loads the follower issued for a
+// stage the leader gave up on before arming it.  Only the abort path pays it.
+constexpr uint64_t kAbortSettleNs = 1000000ull;
 
 // Work item -> tile and its column range.  Items below tail_begin are whole
 // 256 x 256 tiles; the tiles of the last, partial wave are split into two
@@ -206,7 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   griddep_launch_dependents();
   griddep_wait();
   const uint32_t tmem_base = *tmem_slot;
-  const Abort ab{abort_flag, p.error_word};
+  const Abort ab{abort_flag, p.error_word, p.wait_limit};
   const int num_items = p.num_items;
 
   if (warp == 0) {
@@ -453,6 +462,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.tma_store && lane == 0) bulk_wait_group<0>();  // this warp's stores are complete
   }
   __syncthreads();
+  // every role of this CTA has stopped; if any gave up, let issued loads land
+  if (*abort_flag && threadIdx.x == 0) spin_ns(kAbortSettleNs);
   cluster_sync();  // the peer is done with this CTA's shared memory and TMEM, and vice versa
   if (warp == 2) {
     tc_fence_after();
@@ -510,6 +521,7 @@ cudaError_t launch_pair(const GemmArgs& a, cudaStream_t stream) {
     p.epi_ptr[i] = a.epi_ptr[i];
   }
   p.error_word = a.error_word;
+  p.wait_limit = wait_limit_or_default(a.wait_limit_cycles);
   p.tma_store = tma_store ? 1 : 0;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);

@@ -80,16 +80,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 struct Abort {
   volatile int* flag;      // shared memory
   uint32_t* error_word;    // global memory, first error code wins
+  uint64_t limit;          // SM cycles a pipeline wait may take (kWaitLimitCycles by default)
 };
 
 constexpr uint64_t kWaitLimitCycles = 4000000000ull;  // ~2 s at the B200's 1.9-2.0 GHz SM clock
 
+// Limit of a launch: ``cycles`` when set, else the default.
+__host__ __device__ __forceinline__ uint64_t wait_limit_or_default(uint64_t cycles) {
+  return cycles ? cycles : kWaitLimitCycles;
+}
+
 // Waits for the phase of ``bar`` with parity ``parity`` to complete.  Gives up
-// after kWaitLimitCycles SM cycles or when another role aborted; a timeout
-// records ``code`` in the error word and raises the CTA's abort flag.
-// Returns false when giving up.  The limit is checked only every 1024 polls
-// (with the cheap per-SM cycle counter) so the common, short wait costs
-// nothing but the polls themselves.
+// after ab.limit SM cycles or when another role aborted; a timeout records
+// ``code`` in the error word and raises the CTA's abort flag.  Returns false
+// when giving up.  The limit is checked only every 1024 polls (with the cheap
+// per-SM cycle counter) so the common, short wait costs nothing but the polls
+// themselves; a wait therefore gives up after at least 2048 polls plus the
+// limit, whatever the limit.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const Abort& ab, uint32_t code) {
   uint64_t t0 = 0;
   uint32_t polls = 0;
@@ -99,7 +106,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
     const uint64_t now = clock64();
     if (t0 == 0) {
       t0 = now;
-    } else if (now - t0 > kWaitLimitCycles) {
+    } else if (now - t0 > ab.limit) {
       *ab.flag = 1;
       atomicCAS(ab.error_word, 0u, code);
       return false;
@@ -129,7 +136,7 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, c
       const uint64_t now = clock64();
       if (t0 == 0) {
         t0 = now;
-      } else if (now - t0 > kWaitLimitCycles) {
+      } else if (now - t0 > ab.limit) {
         *ab.flag = 1;
         atomicCAS(ab.error_word, 0u, code);
         ok = false;
@@ -148,6 +155,12 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
   while (!mbar_try_wait(bar, parity))
     if (global_timer_ns() - t0 > limit_ns) return false;
   return true;
+}
+
+// Waits ``ns`` nanoseconds of the global timer (a bounded spin).
+__device__ __forceinline__ void spin_ns(uint64_t ns) {
+  const uint64_t t0 = global_timer_ns();
+  while (global_timer_ns() - t0 < ns) __nanosleep(1000);
 }
 
 // ---------------------------------------------------------------- TMA

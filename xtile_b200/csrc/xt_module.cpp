@@ -220,6 +220,12 @@ PYBIND11_MODULE(_xtile, m) {
         if (xt_set_sm_budget(sms) != XT_OK) throw std::invalid_argument(xt_last_error());
       },
       py::arg("sms"));
+  m.def(
+      "set_wait_limit_ns",
+      [](uint64_t ns) {
+        if (xt_set_wait_limit_ns(ns) != XT_OK) throw std::invalid_argument(xt_last_error());
+      },
+      py::arg("ns"));
   m.def("launch", &launch, py::arg("module"), py::arg("ptrs"), py::arg("bid0_begin"), py::arg("bid0_end"),
         py::arg("stream"), py::arg("func") = py::none());
   m.def("func_names", &func_names, py::arg("module"));

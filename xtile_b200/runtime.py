@@ -165,6 +165,23 @@ def device_error() -> int:
     return int(_native.device_error())
 
 
+class wait_limit:
+    """Limits how long a pipeline wait of the gemm and conv kernels launched
+    by this thread inside a ``with`` block may take, in nanoseconds, before
+    the kernel gives up, records an error code (``device_error()``), drains
+    and returns.  For testing the failure path; the default is about 2 s."""
+
+    def __init__(self, ns: int) -> None:
+        self.ns = int(ns)
+
+    def __enter__(self) -> "wait_limit":
+        _native.set_wait_limit_ns(self.ns)
+        return self
+
+    def __exit__(self, *exc) -> None:
+        _native.set_wait_limit_ns(0)
+
+
 class sm_budget:
     """Caps the SMs the persistent kernels (gemm, conv) launched by this
     thread occupy, for the duration of a ``with`` block (0: all SMs).
