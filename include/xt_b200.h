@@ -135,6 +135,17 @@ int xt_device_error(uint32_t* out_code);
  * GEMM rounds the budget down to an even number (its CTAs come in pairs). */
 int xt_set_sm_budget(int sms);
 
+/* No counterpart in the reference.  Elementwise and row programs (other than
+ * the dedicated add and softmax kernels) run in kernels generated for the
+ * program and compiled at their first launch with NVRTC for sm_100a.
+ * xt_generated_source gives that CUDA source for ``func`` (NULL: the first)
+ * in a malloc'ed string (free with xt_string_free); XT_EUNSUPPORTED for
+ * programs that run a compiled kernel.  xt_compile_generated compiles such a
+ * source as a launch would and reports the cubin's size; it needs NVRTC but
+ * no GPU. */
+int xt_generated_source(const xt_module* module, const char* func, char** out_text);
+int xt_compile_generated(const char* source, size_t* out_cubin_bytes);
+
 /* No counterpart in the reference.  Sets how long a pipeline wait (TMA data,
  * MMA completion, accumulator hand-off) of the gemm and conv kernels that the
  * calling thread launches later may take before the kernel gives up: it then

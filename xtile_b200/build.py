@@ -56,7 +56,7 @@ def _run(cmd: list[str]) -> None:
 def _compile(src: Path, force: bool, deps: list[Path]) -> Path:
     obj = BUILD / (src.relative_to(CSRC).as_posix().replace("/", "_") + ".o")
     if force or _stale(obj, src, deps):
-        inc = [f"-I{CSRC}", f"-I{ROOT / 'include'}", f"-I{CUDA / 'include'}"]
+        inc = [f"-I{CSRC}", f"-I{ROOT / 'include'}", f"-I{CUDA / 'include'}", f"-I{BUILD}"]
         if src.suffix == ".cu":
             cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
                    "--expt-relaxed-constexpr", *inc, "-c", str(src), "-o", str(obj)]
@@ -67,8 +67,23 @@ def _compile(src: Path, force: bool, deps: list[Path]) -> Path:
     return obj
 
 
+def _embed_op_math() -> None:
+    """Writes op_math.cuh's text as a C++ string literal into the build
+    directory: codegen.cpp puts it at the top of every generated kernel, so
+    the generated kernels and the compiled ones share one definition of each
+    element op.  Rewritten only when the text changes (keeps objects fresh)."""
+    text = (CSRC / "kernels" / "op_math.cuh").read_text()
+    if ")XTOPS\"" in text:
+        raise RuntimeError("op_math.cuh may not contain the string literal's delimiter")
+    inc = BUILD / "op_math_src.inc"
+    body = 'R"XTOPS(' + text + ')XTOPS"\n'
+    if not inc.exists() or inc.read_text() != body:
+        inc.write_text(body)
+
+
 def build(force: bool = False, verbose: bool = False) -> None:
     BUILD.mkdir(exist_ok=True)
+    _embed_op_math()
     deps = _headers()
     lib_srcs = [p for p in sorted(CSRC.rglob("*.cpp")) if p.name != "xt_module.cpp"]
     lib_srcs += sorted(CSRC.rglob("*.cu"))

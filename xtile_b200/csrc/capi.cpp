@@ -11,6 +11,7 @@
 #include <string>
 
 #include "../../include/xt_b200.h"
+#include "codegen.h"
 #include "ir.h"
 #include "kernels.h"
 #include "plan.h"
@@ -164,6 +165,50 @@ int gemm_launch_args(const Plan& p, void* const* args, int64_t b0, int64_t b1, u
 
 namespace {
 
+// Launch arguments of an ew / rows plan; ``args`` null leaves the pointers
+// null (the generated source depends only on the rest).
+xt::dev::EwArgs ew_args_of(const xt::EwPlan& e, void* const* args) {
+  xt::dev::EwArgs a{};
+  for (int i = 0; i < e.n_in; ++i) {
+    a.in[i] = args ? args[e.in_arg[i]] : nullptr;
+    a.in_elem[i] = elem_code(e.in_elem[i]);
+    a.in_bcast[i] = e.in_bcast[i] ? 1 : 0;
+  }
+  a.bcast_period = e.bcast_period;
+  for (int i = 0; i < e.n_out; ++i) {
+    a.out[i] = args ? args[e.out_arg[i]] : nullptr;
+    a.out_elem[i] = elem_code(e.out_elem[i]);
+  }
+  a.n_in = e.n_in;
+  a.n_out = e.n_out;
+  a.n_code = static_cast<int>(e.code.size());
+  for (size_t i = 0; i < e.code.size(); ++i) a.code[i] = e.code[i];
+  a.begin = 0;
+  a.end = e.numel;
+  return a;
+}
+
+xt::dev::RowArgs row_args_of(const xt::RowPlan& r, void* const* args) {
+  xt::dev::RowArgs a{};
+  for (int i = 0; i < r.n_in; ++i) {
+    a.in[i] = args ? static_cast<const float*>(args[r.in_arg[i]]) : nullptr;
+    a.in_scalar[i] = r.in_is_scalar[i];
+  }
+  for (int i = 0; i < r.n_out; ++i) {
+    a.out[i] = args ? static_cast<float*>(args[r.out_arg[i]]) : nullptr;
+    a.out_scalar[i] = r.out_is_scalar[i];
+  }
+  a.n_code = static_cast<int>(r.code.size());
+  for (size_t i = 0; i < r.code.size(); ++i) a.code[i] = r.code[i];
+  a.n_vregs = r.n_vregs;
+  a.n_sregs = r.n_sregs;
+  a.cols = r.cols;
+  a.softmax = r.softmax;
+  a.row_begin = 0;
+  a.row_end = r.rows;
+  return a;
+}
+
 int launch_plan(const xt::Plan& p, void* const* args, int64_t b0, int64_t b1, cudaStream_t stream) {
   using namespace xt;
   const int64_t g0 = p.grid[0];
@@ -173,21 +218,7 @@ int launch_plan(const xt::Plan& p, void* const* args, int64_t b0, int64_t b1, cu
   switch (p.family) {
     case Family::Ew: {
       const EwPlan& e = p.ew;
-      dev::EwArgs a{};
-      for (int i = 0; i < e.n_in; ++i) {
-        a.in[i] = args[e.in_arg[i]];
-        a.in_elem[i] = elem_code(e.in_elem[i]);
-        a.in_bcast[i] = e.in_bcast[i] ? 1 : 0;
-      }
-      a.bcast_period = e.bcast_period;
-      for (int i = 0; i < e.n_out; ++i) {
-        a.out[i] = args[e.out_arg[i]];
-        a.out_elem[i] = elem_code(e.out_elem[i]);
-      }
-      a.n_in = e.n_in;
-      a.n_out = e.n_out;
-      a.n_code = static_cast<int>(e.code.size());
-      for (size_t i = 0; i < e.code.size(); ++i) a.code[i] = e.code[i];
+      dev::EwArgs a = ew_args_of(e, args);
       if (full) {
         a.begin = 0;
         a.end = e.numel;
@@ -203,21 +234,7 @@ int launch_plan(const xt::Plan& p, void* const* args, int64_t b0, int64_t b1, cu
     }
     case Family::Rows: {
       const RowPlan& r = p.rows;
-      dev::RowArgs a{};
-      for (int i = 0; i < r.n_in; ++i) {
-        a.in[i] = static_cast<const float*>(args[r.in_arg[i]]);
-        a.in_scalar[i] = r.in_is_scalar[i];
-      }
-      for (int i = 0; i < r.n_out; ++i) {
-        a.out[i] = static_cast<float*>(args[r.out_arg[i]]);
-        a.out_scalar[i] = r.out_is_scalar[i];
-      }
-      a.n_code = static_cast<int>(r.code.size());
-      for (size_t i = 0; i < r.code.size(); ++i) a.code[i] = r.code[i];
-      a.n_vregs = r.n_vregs;
-      a.n_sregs = r.n_sregs;
-      a.cols = r.cols;
-      a.softmax = r.softmax;
+      dev::RowArgs a = row_args_of(r, args);
       if (full) {
         a.row_begin = 0;
         a.row_end = r.rows;
@@ -610,6 +627,40 @@ int xt_set_sm_budget(int sms) {
   if (sms < 0) return fail(XT_EARGUMENT, "xt_set_sm_budget: negative SM count");
   t_sm_budget = sms;
   return XT_OK;
+}
+
+int xt_generated_source(const xt_module* module, const char* func, char** out_text) {
+  if (!module || !out_text) return fail(XT_EARGUMENT, "xt_generated_source: null argument");
+  const xt::Func* f = find_func(module, func);
+  if (!f) return fail(XT_EARGUMENT, std::string("xt_generated_source: no function @") + (func ? func : "(first)"));
+  try {
+    auto p = get_plan(module, *f);
+    std::string text;
+    if (p->family == xt::Family::Ew)
+      text = xt::jit::ew_source(ew_args_of(p->ew, nullptr));
+    else if (p->family == xt::Family::Rows && !p->rows.softmax)
+      text = xt::jit::rows_source(row_args_of(p->rows, nullptr));
+    else
+      return fail(XT_EUNSUPPORTED, "xt_generated_source: @" + p->func + " runs a compiled kernel ('" +
+                                       xt::family_name(p->family) + "' family)");
+    char* buf = static_cast<char*>(std::malloc(text.size() + 1));
+    if (!buf) return fail(XT_EARGUMENT, "xt_generated_source: out of host memory");
+    std::memcpy(buf, text.c_str(), text.size() + 1);
+    *out_text = buf;
+    return XT_OK;
+  } catch (const xt::Error& e) {
+    return fail(e);
+  }
+}
+
+int xt_compile_generated(const char* source, size_t* out_cubin_bytes) {
+  if (!source || !out_cubin_bytes) return fail(XT_EARGUMENT, "xt_compile_generated: null argument");
+  try {
+    *out_cubin_bytes = xt::jit::compile(source).size();
+    return XT_OK;
+  } catch (const xt::Error& e) {
+    return fail(e);
+  }
 }
 
 int xt_set_wait_limit_ns(uint64_t ns) {

@@ -1,0 +1,48 @@
+// Kernels generated per Block program (ew and rows families), compiled at
+// run time with NVRTC for sm_100a.
+//
+// The planner turns an elementwise or row program into a short register
+// program (plan.h: Instr).  Instead of interpreting it on the GPU, the host
+// writes it out as straight-line CUDA C++ -- each value a register, each op
+// the op_math.cuh function applied in place -- compiles it once per program
+// and device, and launches the cubin.  Programs are cached by their code,
+// element types and shapes, so a program compiles once per process.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <string>
+
+#include "kernels.h"
+
+namespace xt {
+namespace jit {
+
+// CUDA source of the ew kernels for a program (its code, element types and
+// broadcast flags): ``xt_ew_v`` (4 * kEwVec elements per thread and pass, for
+// aligned arrays) and ``xt_ew_s`` (one element per thread, any alignment).
+std::string ew_source(const dev::EwArgs& a);
+// CUDA source of the rows kernels for a program of rows of ``a.cols``
+// columns: ``xt_rows_v`` (float4 accesses, cols % 4 == 0 on 16-byte aligned
+// rows) and ``xt_rows_s`` (element accesses).
+std::string rows_source(const dev::RowArgs& a);
+// Whether a rows program fits the generated kernels' registers (wider ones
+// run the shared-memory interpreter).
+bool rows_fit(const dev::RowArgs& a);
+
+// Compiles ``source`` with NVRTC for sm_100a; returns the cubin.  Throws
+// xt::Error (kCudaError) with NVRTC's log on failure or when NVRTC cannot be
+// loaded.  Needs no GPU.
+std::string compile(const std::string& source);
+
+// Launches the generated ew / rows kernels for ``a`` on ``stream`` (compiling
+// and loading them on first use on the current device).
+cudaError_t launch_ew(const dev::EwArgs& a, cudaStream_t stream);
+cudaError_t launch_rows(const dev::RowArgs& a, cudaStream_t stream);
+
+constexpr int kEwVec = 2;          // float4 groups per thread and pass in xt_ew_v
+constexpr int kEwThreads = 256;
+constexpr int kRowsPerCta = 4;     // one warp per row
+
+}  // namespace jit
+}  // namespace xt

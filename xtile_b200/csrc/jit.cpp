@@ -1,0 +1,294 @@
+// Run-time compilation and launch of the generated ew / rows kernels
+// (codegen.h): NVRTC, loaded with dlopen from the CUDA toolkit, compiles a
+// program's source to an sm_100a cubin; the driver API (resolved through the
+// runtime's entry-point query, so the library needs no link against
+// libcuda) loads it once per device and launches it with programmatic
+// dependent launch, like every other kernel of this library.
+//
+// A missing NVRTC is an error at the first launch of an ew or rows program
+// (with the reason); there is no fallback.
+#include <cuda.h>
+#include <dlfcn.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "codegen.h"
+#include "ir.h"
+
+namespace xt {
+namespace jit {
+namespace {
+
+// ------------------------------------------------------------------ NVRTC
+typedef int (*CreateFn)(void**, const char*, const char*, int, const char* const*, const char* const*);
+typedef int (*CompileFn)(void*, int, const char* const*);
+typedef int (*SizeFn)(void*, size_t*);
+typedef int (*GetFn)(void*, char*);
+typedef int (*DestroyFn)(void**);
+typedef const char* (*ErrStrFn)(int);
+
+struct Nvrtc {
+  CreateFn create = nullptr;
+  CompileFn compile = nullptr;
+  SizeFn cubin_size = nullptr, log_size = nullptr;
+  GetFn cubin = nullptr, log = nullptr;
+  DestroyFn destroy = nullptr;
+  ErrStrFn err = nullptr;
+  std::string why;  // empty when loaded
+};
+
+const Nvrtc& nvrtc() {
+  static Nvrtc n = [] {
+    Nvrtc r;
+    std::vector<std::string> names;
+    if (const char* home = std::getenv("CUDA_HOME")) names.push_back(std::string(home) + "/lib64/libnvrtc.so.12");
+    names.push_back("/usr/local/cuda/lib64/libnvrtc.so.12");
+    names.push_back("libnvrtc.so.12");
+    names.push_back("libnvrtc.so");
+    void* h = nullptr;
+    for (const std::string& n : names)
+      if ((h = dlopen(n.c_str(), RTLD_NOW | RTLD_LOCAL)) != nullptr) break;
+    if (!h) {
+      r.why = "NVRTC (libnvrtc.so.12) could not be loaded: set CUDA_HOME to the CUDA toolkit";
+      return r;
+    }
+    r.create = reinterpret_cast<CreateFn>(dlsym(h, "nvrtcCreateProgram"));
+    r.compile = reinterpret_cast<CompileFn>(dlsym(h, "nvrtcCompileProgram"));
+    r.cubin_size = reinterpret_cast<SizeFn>(dlsym(h, "nvrtcGetCUBINSize"));
+    r.cubin = reinterpret_cast<GetFn>(dlsym(h, "nvrtcGetCUBIN"));
+    r.log_size = reinterpret_cast<SizeFn>(dlsym(h, "nvrtcGetProgramLogSize"));
+    r.log = reinterpret_cast<GetFn>(dlsym(h, "nvrtcGetProgramLog"));
+    r.destroy = reinterpret_cast<DestroyFn>(dlsym(h, "nvrtcDestroyProgram"));
+    r.err = reinterpret_cast<ErrStrFn>(dlsym(h, "nvrtcGetErrorString"));
+    if (!r.create || !r.compile || !r.cubin_size || !r.cubin || !r.log_size || !r.log || !r.destroy || !r.err)
+      r.why = "NVRTC is missing an entry point";
+    return r;
+  }();
+  return n;
+}
+
+// ------------------------------------------------------------------ driver
+typedef CUresult (*ModuleLoadDataFn)(CUmodule*, const void*);
+typedef CUresult (*ModuleGetFunctionFn)(CUfunction*, CUmodule, const char*);
+typedef CUresult (*LaunchKernelExFn)(const CUlaunchConfig*, CUfunction, void**, void**);
+typedef CUresult (*GetErrorStringFn)(CUresult, const char**);
+
+template <class F>
+F driver_fn(const char* name) {
+  void* f = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &f, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return reinterpret_cast<F>(f);
+}
+
+struct Driver {
+  ModuleLoadDataFn load = driver_fn<ModuleLoadDataFn>("cuModuleLoadData");
+  ModuleGetFunctionFn get = driver_fn<ModuleGetFunctionFn>("cuModuleGetFunction");
+  LaunchKernelExFn launch = driver_fn<LaunchKernelExFn>("cuLaunchKernelEx");
+  GetErrorStringFn err = driver_fn<GetErrorStringFn>("cuGetErrorString");
+};
+
+const Driver& driver() {
+  static Driver d;
+  return d;
+}
+
+std::string cu_error(CUresult r) {
+  const char* s = nullptr;
+  if (driver().err) driver().err(r, &s);
+  return s ? s : ("CUresult " + std::to_string(static_cast<int>(r)));
+}
+
+// ------------------------------------------------------------------ cache
+struct Program {
+  std::string cubin;
+  std::map<int, CUmodule> modules;                          // per device
+  std::map<std::pair<int, std::string>, CUfunction> fns;    // (device, kernel name)
+};
+
+std::mutex g_mu;
+std::unordered_map<std::string, std::unique_ptr<Program>> g_programs;
+
+// The fixed part of a program's launch arguments: what its generated source
+// depends on.
+template <class Args>
+std::string key_of(char family, const Args& a, const Instr* code, int n_code, const std::string& extra) {
+  std::string k(1, family);
+  k.append(reinterpret_cast<const char*>(code), sizeof(Instr) * static_cast<size_t>(n_code));
+  k += extra;
+  (void)a;
+  return k;
+}
+
+// Kernel ``name`` of the program (``key``; ``make`` writes its source) on
+// the current device, compiled and loaded on first use.
+template <class Make>
+CUfunction function(const std::string& key, Make make, const char* name) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) throw Error(kCudaError, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lock(g_mu);
+  auto it = g_programs.find(key);
+  if (it == g_programs.end()) {
+    auto p = std::make_unique<Program>();
+    p->cubin = compile(make());
+    it = g_programs.emplace(key, std::move(p)).first;
+  }
+  Program& p = *it->second;
+  auto f = p.fns.find({dev, name});
+  if (f != p.fns.end()) return f->second;
+  const Driver& d = driver();
+  if (!d.load || !d.get || !d.launch) throw Error(kCudaError, "the CUDA driver lacks cuModuleLoadData / cuLaunchKernelEx");
+  // the device's primary context, current on this thread, receives the module
+  e = cudaSetDevice(dev);
+  if (e != cudaSuccess) throw Error(kCudaError, std::string("context set-up: ") + cudaGetErrorString(e));
+  auto m = p.modules.find(dev);
+  if (m == p.modules.end()) {
+    CUmodule mod = nullptr;
+    CUresult r = d.load(&mod, p.cubin.data());
+    if (r != CUDA_SUCCESS) throw Error(kCudaError, "loading a generated kernel: " + cu_error(r));
+    m = p.modules.emplace(dev, mod).first;
+  }
+  CUfunction fn = nullptr;
+  CUresult r = d.get(&fn, m->second, name);
+  if (r != CUDA_SUCCESS) throw Error(kCudaError, std::string("generated kernel ") + name + ": " + cu_error(r));
+  p.fns[{dev, name}] = fn;
+  return fn;
+}
+
+cudaError_t launch(CUfunction fn, unsigned grid, unsigned block, cudaStream_t stream, void* params) {
+  CUlaunchAttribute attr[1];
+  attr[0].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+  attr[0].value.programmaticStreamSerializationAllowed = 1;
+  CUlaunchConfig cfg{};
+  cfg.gridDimX = grid;
+  cfg.gridDimY = cfg.gridDimZ = 1;
+  cfg.blockDimX = block;
+  cfg.blockDimY = cfg.blockDimZ = 1;
+  cfg.sharedMemBytes = 0;
+  cfg.hStream = reinterpret_cast<CUstream>(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* args[] = {params};
+  CUresult r = driver().launch(&cfg, fn, args, nullptr);
+  if (r != CUDA_SUCCESS) throw Error(kCudaError, "launching a generated kernel: " + cu_error(r));
+  return cudaSuccess;
+}
+
+unsigned grid_of(int64_t items, int per_block) {
+  int64_t b = (items + per_block - 1) / per_block;
+  if (b < 1) b = 1;
+  if (b > 0x7fffffff) b = 0x7fffffff;
+  return static_cast<unsigned>(b);
+}
+
+// kernel parameter blocks: the layout of XtEwArgs / XtRowArgs in the source
+struct EwParams {
+  const void* in[kMaxSlots];
+  void* out[kMaxSlots];
+  int64_t begin, end, period;
+};
+struct RowParams {
+  const float* in[kMaxSlots];
+  float* out[kMaxSlots];
+  int64_t row_begin, row_end;
+};
+
+}  // namespace
+
+std::string compile(const std::string& source) {
+  const Nvrtc& n = nvrtc();
+  if (!n.why.empty()) throw Error(kCudaError, n.why);
+  void* prog = nullptr;
+  int st = n.create(&prog, source.c_str(), "xt_generated.cu", 0, nullptr, nullptr);
+  if (st != 0) throw Error(kCudaError, std::string("nvrtcCreateProgram: ") + n.err(st));
+  const char* opts[] = {"-arch=sm_100a", "-std=c++17", "-lineinfo"};
+  st = n.compile(prog, 3, opts);
+  std::string log;
+  size_t log_n = 0;
+  if (n.log_size(prog, &log_n) == 0 && log_n > 1) {
+    log.resize(log_n);
+    n.log(prog, &log[0]);
+  }
+  if (st != 0) {
+    n.destroy(&prog);
+    throw Error(kCudaError, std::string("NVRTC failed on a generated kernel: ") + n.err(st) + "\n" + log);
+  }
+  size_t size = 0;
+  n.cubin_size(prog, &size);
+  std::string cubin(size, '\0');
+  n.cubin(prog, &cubin[0]);
+  n.destroy(&prog);
+  return cubin;
+}
+
+cudaError_t launch_ew(const dev::EwArgs& a, cudaStream_t stream) {
+  const int64_t n = a.end - a.begin;
+  if (n <= 0) return cudaSuccess;
+  std::string extra;
+  for (int k = 0; k < kMaxSlots; ++k) {
+    extra += static_cast<char>(k < a.n_in ? a.in_elem[k] : 255);
+    extra += static_cast<char>(k < a.n_in ? a.in_bcast[k] : 0);
+    extra += static_cast<char>(k < a.n_out ? a.out_elem[k] : 255);
+  }
+  const std::string key = key_of('e', a, a.code, a.n_code, extra);
+  // the vector kernel: a range starting at a multiple of 4 elements, arrays
+  // aligned to 4 elements of their type, broadcast rows a multiple of 4 long
+  bool v4 = a.begin % 4 == 0 && a.bcast_period % 4 == 0;
+  for (int k = 0; k < a.n_in && v4; ++k)
+    v4 = reinterpret_cast<uintptr_t>(a.in[k]) % (a.in_elem[k] == dev::kF32 ? 16 : a.in_elem[k] == dev::kBF16 ? 8 : 4) == 0;
+  for (int k = 0; k < a.n_out && v4; ++k)
+    v4 = reinterpret_cast<uintptr_t>(a.out[k]) % (a.out_elem[k] == dev::kF32 ? 16 : a.out_elem[k] == dev::kBF16 ? 8 : 4) == 0;
+  EwParams p{};
+  for (int k = 0; k < kMaxSlots; ++k) {
+    p.in[k] = a.in[k];
+    p.out[k] = a.out[k];
+  }
+  p.begin = a.begin;
+  p.end = a.end;
+  p.period = a.bcast_period > 0 ? a.bcast_period : 1;
+  if (v4) {
+    const int64_t groups = n / (4 * kEwVec);
+    CUfunction f = function(key, [&] { return ew_source(a); }, "xt_ew_v");
+    return launch(f, grid_of(groups > 0 ? groups : 1, kEwThreads), kEwThreads, stream, &p);
+  }
+  CUfunction f = function(key, [&] { return ew_source(a); }, "xt_ew_s");
+  return launch(f, grid_of(n, kEwThreads), kEwThreads, stream, &p);
+}
+
+cudaError_t launch_rows(const dev::RowArgs& a, cudaStream_t stream) {
+  const int64_t rows = a.row_end - a.row_begin;
+  if (rows <= 0) return cudaSuccess;
+  std::string extra(reinterpret_cast<const char*>(&a.cols), sizeof a.cols);
+  extra += static_cast<char>(a.n_vregs);
+  for (int k = 0; k < kMaxSlots; ++k) {
+    extra += static_cast<char>(a.in_scalar[k]);
+    extra += static_cast<char>(a.out_scalar[k]);
+  }
+  const std::string key = key_of('r', a, a.code, a.n_code, extra);
+  bool vec = a.cols % 4 == 0;
+  for (int k = 0; k < kMaxSlots && vec; ++k) {
+    if (a.in[k] && !a.in_scalar[k]) vec = (reinterpret_cast<uintptr_t>(a.in[k]) & 15) == 0;
+    if (vec && a.out[k] && !a.out_scalar[k]) vec = (reinterpret_cast<uintptr_t>(a.out[k]) & 15) == 0;
+  }
+  RowParams p{};
+  for (int k = 0; k < kMaxSlots; ++k) {
+    p.in[k] = a.in[k];
+    p.out[k] = a.out[k];
+  }
+  p.row_begin = a.row_begin;
+  p.row_end = a.row_end;
+  CUfunction f = function(key, [&] { return rows_source(a); }, vec ? "xt_rows_v" : "xt_rows_s");
+  return launch(f, grid_of(rows, kRowsPerCta), 32 * kRowsPerCta, stream, &p);
+}
+
+}  // namespace jit
+}  // namespace xt

@@ -1,41 +1,40 @@
-// Scalar element operations shared by the interpreter kernels (ew, rows,
-// tile): the xt unary and binary ops on f32 values and element loads/stores
-// of f32, bf16 and int8 arrays.
-//
-// f32 arithmetic is IEEE round-to-nearest with no contraction (the __f*_rn
-// intrinsics), so add/sub/mul/reciprocal/rsqrt match the CPU oracle bit for
-// bit; ftoi rounds half to even and saturates to [-128, 127], NaN -> 0.
+// Scalar element operations of the compiled interpreter kernels (tile, and
+// the ew / rows forms compiled ahead of time): the xt unary and binary ops on
+// f32 values, dispatched on an opcode, and element loads/stores of f32, bf16
+// and int8 arrays.  The arithmetic itself is op_math.cuh's, shared with the
+// kernels generated per program at run time.
 #pragma once
 
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include "../kernels.h"
+#include "op_math.cuh"
 
 namespace xt {
 namespace dev {
 
 __device__ __forceinline__ float unary_op(uint8_t op, float x) {
   switch (op & 0x7f) {
-    case kExp: return expf(x);
-    case kCos: return cosf(x);
-    case kSin: return sinf(x);
-    case kRecip: return __frcp_rn(x);
-    case kRsqrt: return __frcp_rn(__fsqrt_rn(x));
-    case kSigmoid: return __frcp_rn(__fadd_rn(1.0f, expf(-x)));
-    case kTanh: return tanhf(x);
-    case kSilu: return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
-    case kItof: return x;
-    case kFtoi: return x != x ? 0.0f : fminf(fmaxf(rintf(x), -128.0f), 127.0f);
+    case kExp: return xt_exp(x);
+    case kCos: return xt_cos(x);
+    case kSin: return xt_sin(x);
+    case kRecip: return xt_recip(x);
+    case kRsqrt: return xt_rsqrt(x);
+    case kSigmoid: return xt_sigmoid(x);
+    case kTanh: return xt_tanh(x);
+    case kSilu: return xt_silu(x);
+    case kItof: return xt_itof(x);
+    case kFtoi: return xt_ftoi(x);
     default: return x;
   }
 }
 
 __device__ __forceinline__ float binary_op(uint8_t op, float a, float b) {
   switch (op & 0x7f) {
-    case kAdd: case kBcastAdd: return __fadd_rn(a, b);
-    case kSub: case kBcastSub: return __fsub_rn(a, b);
-    case kMul: case kBcastMul: return __fmul_rn(a, b);
+    case kAdd: case kBcastAdd: return xt_add(a, b);
+    case kSub: case kBcastSub: return xt_sub(a, b);
+    case kMul: case kBcastMul: return xt_mul(a, b);
     default: return a;
   }
 }

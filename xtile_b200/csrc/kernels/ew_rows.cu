@@ -3,13 +3,13 @@
 // ew:   a flat map over arrays of identical shape.  A single binary
 //       add/sub/mul of two f32 arrays (the kernels/add.py pattern) runs in a
 //       dedicated 128-bit vector kernel; any other register program runs in
-//       an interpreter whose registers stay in registers (operands are picked
-//       by predicated selection, never by dynamic indexing).
+//       a kernel generated for it at run time (codegen.h).
 // rows: programs over whole rows (one warp per row, the row held in
 //       registers, warp-shuffle reductions).  The softmax chain
 //       max -> sub -> exp -> sum -> reciprocal -> mul (kernels/softmax.py,
-//       xtile/dsl.py:354-357) has a dedicated kernel; other row programs use
-//       the interpreter.
+//       xtile/dsl.py:354-357) has a dedicated kernel; other row programs run
+//       in a generated kernel, or, when their live rows exceed the register
+//       file, in the shared-memory interpreter below.
 //
 // f32 arithmetic is IEEE round-to-nearest with no contraction (the __f*_rn
 // intrinsics), so add/sub/mul/reciprocal/rsqrt match the CPU oracle bit for bit.
@@ -19,6 +19,7 @@
 #include "../kernels.h"
 #include "elem_ops.cuh"
 #include "pdl.cuh"
+#include "../codegen.h"
 
 namespace xt {
 namespace dev {
@@ -66,10 +67,8 @@ __global__ void __launch_bounds__(kThreads) ew_binary_f32(const float* __restric
 }
 
 // ---------------------------------------------------------------------------
-// ew: register-program interpreter
+// register selection and float4 op dispatch of the rows interpreter
 // ---------------------------------------------------------------------------
-constexpr int kEwRegs = 8;
-
 template <int N>
 __device__ __forceinline__ float pick(const float (&r)[N], int idx) {
   float v = 0.0f;
@@ -82,64 +81,6 @@ template <int N>
 __device__ __forceinline__ void put(float (&r)[N], int idx, float v) {
 #pragma unroll
   for (int k = 0; k < N; ++k) r[k] = (k == idx) ? v : r[k];
-}
-
-// The program for element i, registers held by predicated selection.
-__device__ __forceinline__ void ew_element(const EwArgs& p, int64_t i) {
-  float r[kEwRegs];
-#pragma unroll
-  for (int k = 0; k < kEwRegs; ++k) r[k] = 0.0f;
-  for (int pc = 0; pc < p.n_code; ++pc) {
-    const Instr ins = p.code[pc];
-    if (ins.op == kLoad) {
-      put(r, ins.dst, load_elem(p.in[ins.a], p.in_elem[ins.a], p.in_bcast[ins.a] ? i % p.bcast_period : i));
-    } else if (ins.op == kStore) {
-      store_elem(p.out[ins.dst], p.out_elem[ins.dst], i, pick(r, ins.a));
-    } else if (ins.op == kAdd || ins.op == kSub || ins.op == kMul) {
-      put(r, ins.dst, binary_op(ins.op, pick(r, ins.a), pick(r, ins.b)));
-    } else {
-      put(r, ins.dst, unary_op(ins.op, pick(r, ins.a)));
-    }
-  }
-}
-
-// One element per thread: any alignment.
-__global__ void __launch_bounds__(kThreads) ew_program(const __grid_constant__ EwArgs p) {
-  griddep_launch_dependents();
-  griddep_wait();
-  int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
-  for (int64_t i = p.begin + static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < p.end;
-       i += stride)
-    ew_element(p, i);
-}
-
-// Four consecutive elements of an array as f32 values: one 16-, 8- or 4-byte
-// load (the array holds whole groups of four at 4-element aligned offsets).
-__device__ __forceinline__ float4 load4(const void* p, uint8_t e, int64_t i) {
-  if (e == kF32) return __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p) + i));
-  if (e == kBF16) {
-    const uint2 u = __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p) + i));
-    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
-                       __uint_as_float(u.y & 0xffff0000u));
-  }
-  const uint32_t w = __ldg(reinterpret_cast<const unsigned int*>(static_cast<const int8_t*>(p) + i));
-  return make_float4(static_cast<float>(static_cast<int8_t>(w)), static_cast<float>(static_cast<int8_t>(w >> 8)),
-                     static_cast<float>(static_cast<int8_t>(w >> 16)), static_cast<float>(static_cast<int8_t>(w >> 24)));
-}
-
-// store_elem's conversions for four consecutive elements, one store.
-__device__ __forceinline__ void store4(void* p, uint8_t e, int64_t i, float4 v) {
-  if (e == kF32) {
-    *reinterpret_cast<float4*>(static_cast<float*>(p) + i) = v;
-  } else if (e == kBF16) {
-    auto b = [](float x) { return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(x))); };
-    *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p) + i) =
-        make_uint2(b(v.x) | (b(v.y) << 16), b(v.z) | (b(v.w) << 16));
-  } else {
-    auto c = [](float x) { return static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(static_cast<int>(x)))); };
-    *reinterpret_cast<unsigned int*>(static_cast<int8_t*>(p) + i) =
-        c(v.x) | (c(v.y) << 8) | (c(v.z) << 16) | (c(v.w) << 24);
-  }
 }
 
 template <uint8_t OP>
@@ -175,77 +116,6 @@ __device__ __forceinline__ float4 binary4(uint8_t op, float4 x, float4 y) {
     case kSub: case kBcastSub: return binary4_of<kSub>(x, y);
     default: return binary4_of<kMul>(x, y);
   }
-}
-
-// 4 * NV elements per thread per pass (NV consecutive float4 groups), for
-// arrays whose range starts at a multiple of 4 elements on aligned pointers.
-// The program's registers live in shared memory, NV float4 slots per
-// register and thread, so an operand is a 16-byte shared load at a computed
-// address instead of a predicated selection over every register; decoding
-// and dispatching an instruction is paid once per 4 * NV elements.  The
-// program's leading loads (n_lead of them) are all issued before any is
-// written to its register, so a thread has every input's bytes in flight at
-// once.  Elements past the last whole group of four run through ew_element.
-template <int NV, int TH = kThreads / NV>  // TH threads: 32 KiB of register slots
-__global__ void __launch_bounds__(TH) ew_program_v4(const __grid_constant__ EwArgs p, int n_lead) {
-  __shared__ float4 rf[kEwRegs * NV * TH];
-  float4* my = rf + threadIdx.x;  // register k, group j of this thread: my[(k * NV + j) * TH]
-  griddep_launch_dependents();
-  griddep_wait();
-  const int64_t n4 = (p.end - p.begin) / 4;
-  const int64_t nv = n4 / NV;  // whole passes; the rest below
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * TH;
-  // broadcast rows: column of this thread's first element, advanced per pass
-  // without a division (the period is a multiple of 4)
-  const int64_t period = p.bcast_period > 0 ? p.bcast_period : 1;
-  const int64_t v_first = static_cast<int64_t>(blockIdx.x) * TH + threadIdx.x;
-  int64_t col = (p.begin + 4 * NV * v_first) % period;
-  const int64_t col_step = (4 * NV * stride) % period;
-  // element index of group j of the pass at element i0, for input slot s
-  auto at = [&](int s, int64_t i0, int j) -> int64_t {
-    if (!p.in_bcast[s]) return i0 + 4 * j;
-    const int64_t c = col + 4 * j;
-    return c >= period ? c - period : c;
-  };
-  for (int64_t v = v_first; v < nv; v += stride) {
-    const int64_t i0 = p.begin + 4 * NV * v;
-    float4 t[kMaxSlots][NV];
-#pragma unroll
-    for (int q = 0; q < kMaxSlots; ++q)
-#pragma unroll
-      for (int j = 0; j < NV; ++j)
-        if (q < n_lead) t[q][j] = load4(p.in[p.code[q].a], p.in_elem[p.code[q].a], at(p.code[q].a, i0, j));
-#pragma unroll
-    for (int q = 0; q < kMaxSlots; ++q)
-#pragma unroll
-      for (int j = 0; j < NV; ++j)
-        if (q < n_lead) my[(p.code[q].dst * NV + j) * TH] = t[q][j];
-    for (int pc = n_lead; pc < p.n_code; ++pc) {
-      const Instr ins = p.code[pc];
-      float4* d = my + ins.dst * NV * TH;
-      const float4* x = my + ins.a * NV * TH;
-      const float4* y = my + ins.b * NV * TH;
-      if (ins.op == kLoad) {
-#pragma unroll
-        for (int j = 0; j < NV; ++j) d[j * TH] = load4(p.in[ins.a], p.in_elem[ins.a], at(ins.a, i0, j));
-      } else if (ins.op == kStore) {
-#pragma unroll
-        for (int j = 0; j < NV; ++j) store4(p.out[ins.dst], p.out_elem[ins.dst], i0 + 4 * j, x[j * TH]);
-      } else if (ins.op == kAdd || ins.op == kSub || ins.op == kMul) {
-#pragma unroll
-        for (int j = 0; j < NV; ++j) d[j * TH] = binary4(ins.op, x[j * TH], y[j * TH]);
-      } else {
-#pragma unroll
-        for (int j = 0; j < NV; ++j) d[j * TH] = unary4(ins.op, x[j * TH]);
-      }
-    }
-    col += col_step;
-    if (col >= period) col -= period;
-  }
-  // the last n % (4 NV) elements
-  const int64_t done = 4 * NV * nv;
-  for (int64_t e = done + static_cast<int64_t>(blockIdx.x) * TH + threadIdx.x; e < p.end - p.begin; e += stride)
-    ew_element(p, p.begin + e);
 }
 
 // ---------------------------------------------------------------------------
@@ -486,21 +356,9 @@ cudaError_t launch_ew(const EwArgs& a, cudaStream_t stream) {
       }
     }
   }
-  // vectorised interpreter: a range starting at a multiple of 4 elements on
-  // pointers aligned to 4 elements of their type
-  bool v4 = a.begin % 4 == 0 && a.n_code <= kMaxInstr && a.bcast_period % 4 == 0;
-  for (int k = 0; k < a.n_in && v4; ++k)
-    v4 = reinterpret_cast<uintptr_t>(a.in[k]) % (a.in_elem[k] == kF32 ? 16 : a.in_elem[k] == kBF16 ? 8 : 4) == 0;
-  for (int k = 0; k < a.n_out && v4; ++k)
-    v4 = reinterpret_cast<uintptr_t>(a.out[k]) % (a.out_elem[k] == kF32 ? 16 : a.out_elem[k] == kBF16 ? 8 : 4) == 0;
-  if (v4) {
-    int n_lead = 0;
-    while (n_lead < a.n_code && n_lead < kMaxSlots && a.code[n_lead].op == kLoad) ++n_lead;
-    const int64_t n8 = n / 8;
-    return PdlLaunch(grid_for(n8 > 0 ? n8 : 1, kThreads / 2, 2 * max_blocks), kThreads / 2, 0, stream)(
-        ew_program_v4<2>, a, n_lead);
-  }
-  return PdlLaunch(grid_for(n, kThreads, max_blocks), kThreads, 0, stream)(ew_program, a);
+  // every other program: its own kernel, generated and compiled at run time
+  (void)max_blocks;
+  return jit::launch_ew(a, stream);
 }
 
 cudaError_t launch_rows(const RowArgs& a, cudaStream_t stream) {
@@ -525,6 +383,10 @@ cudaError_t launch_rows(const RowArgs& a, cudaStream_t stream) {
     if (chunks <= 8) return go(softmax_rows_vec4<8, true>, softmax_rows_vec4<8, false>, 8);
     return go(softmax_rows_vec4<16, true>, softmax_rows_vec4<16, false>, 16);
   }
+  // other row programs: their own kernel, generated and compiled at run time,
+  // when the program's row registers fit the register file; wider ones (three
+  // live rows of more than 1024 columns) run the shared-memory interpreter
+  if (jit::rows_fit(a)) return jit::launch_rows(a, stream);
   bool vec = a.cols % 4 == 0;
   for (int k = 0; k < kMaxSlots && vec; ++k) {
     if (a.in[k] && !a.in_scalar[k]) vec = (reinterpret_cast<uintptr_t>(a.in[k]) & 15) == 0;

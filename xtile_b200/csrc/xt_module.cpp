@@ -221,6 +221,28 @@ PYBIND11_MODULE(_xtile, m) {
       },
       py::arg("sms"));
   m.def(
+      "generated_source",
+      [](py::object module, py::object func) {
+        std::string name;
+        if (!func.is_none()) name = func.cast<std::string>();
+        char* text = nullptr;
+        int st = xt_generated_source(unwrap(module), func.is_none() ? nullptr : name.c_str(), &text);
+        if (st != XT_OK) raise_status(st, "generated_source");
+        std::string s(text);
+        xt_string_free(text);
+        return s;
+      },
+      py::arg("module"), py::arg("func") = py::none());
+  m.def(
+      "compile_generated",
+      [](const std::string& source) {
+        size_t n = 0;
+        int st = xt_compile_generated(source.c_str(), &n);
+        if (st != XT_OK) raise_status(st, "compile_generated");
+        return n;
+      },
+      py::arg("source"));
+  m.def(
       "set_wait_limit_ns",
       [](uint64_t ns) {
         if (xt_set_wait_limit_ns(ns) != XT_OK) throw std::invalid_argument(xt_last_error());
