@@ -773,9 +773,12 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference", "torch"],
                     help="b200: this backend; reference: the reference's CPU path; torch: the vendor library "
                          "(cuBLAS, cuDNN) through PyTorch on one GPU, for context")
-    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+    ap.add_argument("--gather", default="peer", choices=["peer", "dma", "nccl"],
                     help="sharded_matmul on N>1 GPUs: ranks store their rows straight into rank 0's output "
-                         "over NVLink (peer), or compute locally and gather with NCCL")
+                         "over NVLink from the GEMM (peer), compute slabs locally and push each to rank 0 with "
+                         "the copy engines (dma), or compute locally and gather with NCCL")
+    ap.add_argument("--slabs", type=int, default=3,
+                    help="dma gather: slabs per rank (each slab's copy overlaps the next slab's GEMM)")
     ap.add_argument("--root-share", type=float, default=None,
                     help="peer gather: rank 0's fraction of the Grid (default: balanced against its NVLink ingress)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -825,7 +828,9 @@ def main() -> None:
         w["config"]["parallelism"] = f"{world} independent replicas"
     if sharded and (grid0 % world or w["out_shape"][0] % grid0):
         raise SystemExit(f"bench: grid0={grid0} does not split evenly over {world} ranks")
-    peer = sharded and world > 1 and args.gather == "peer"
+    # peer and dma: rank 0's output arrays are mapped into every rank (CUDA IPC)
+    peer = sharded and world > 1 and args.gather in ("peer", "dma")
+    dma = peer and args.gather == "dma"
     # equal ranges: compute-only scaling (output left in place) and the NCCL gather
     even_lo, even_hi = bid0_share(grid0, world, rank) if sharded else (0, grid0)
     rows_per_block = w["out_shape"][0] // grid0
@@ -880,28 +885,66 @@ def main() -> None:
         out_bytes = w["out_shape"][0] * w["out_shape"][1] * 4
         tflops = plan["flops"] / (gemm_ms * 1e-3) / 1e12
         rates = {"gemm_tflops_1gpu": round(tflops, 1), "gemm_ms_1gpu": round(gemm_ms, 4), "ingest_gbs": ingest}
+        # the ingest rate of the sender this run uses
+        how = "copy_engines" if dma else "sm_stores"
+        rates["sender"] = how
         root_share = args.root_share if args.root_share is not None else gather_root_share(
-            world, plan["flops"], out_bytes, tflops=tflops, ingest_gbs=ingest["sm_stores"])
-        r_ms = out_bytes / (ingest["sm_stores"] * 1e9) * 1e3
+            world, plan["flops"], out_bytes, tflops=tflops, ingest_gbs=ingest[how])
+        r_ms = out_bytes / (ingest[how] * 1e9) * 1e3
         rates["bound_ms"] = round(gemm_ms * r_ms / (gemm_ms + r_ms), 4)  # T*R/(T+R): no split does better
         rates["bound_note"] = ("T*R/(T+R): T the one-GPU GEMM, R rank 0 taking in the whole output at the "
-                               "measured SM-store ingest rate")
+                               f"measured ingest rate of the sender used ({how})")
     lo, hi = bid0_share(grid0, world, rank, root_share) if sharded else (0, grid0)
     shares = [bid0_share(grid0, world, r, root_share) for r in range(world)] if sharded else [(0, grid0)]
     if peer:
         b0 = shares[0][1]
+        how = (f"the other ranks compute {args.slabs} slabs each locally and push each finished slab into rank 0's "
+               f"output over NVLink with one cudaMemcpyAsync (copy engines, CUDA IPC)" if dma else
+               "each rank's kernel stores its C rows into rank 0's output over NVLink (CUDA IPC)")
         w["config"]["parallelism"] = (f"bid0 split over {world} GPUs, rank 0 {b0} of {grid0} Blocks, the others "
-                                      f"{(grid0 - b0) // (world - 1)}-{-(-(grid0 - b0) // (world - 1))}; each "
-                                      f"rank's kernel stores its C rows into rank 0's output over NVLink (CUDA IPC)")
+                                      f"{(grid0 - b0) // (world - 1)}-{-(-(grid0 - b0) // (world - 1))}; {how}")
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     computed = [torch.cuda.Event() for _ in range(n_sets)]
     gathered = [torch.cuda.Event() for _ in range(n_sets)]
+    # dma gather: this rank's bid0 range in slabs, one event per slab
+    slabs = [(lo + k * (hi - lo) // args.slabs, lo + (k + 1) * (hi - lo) // args.slabs)
+             for k in range(max(1, args.slabs))] if dma and rank != 0 else []
+    slabs = [s for s in slabs if s[1] > s[0]]
+    slab_done = [torch.cuda.Event() for _ in slabs]
+    cudart = _cudart(torch) if dma else None
+    row_bytes = w["out_shape"][1] * 4
+
+    def push_slab(o, tgt, a, b):
+        off = a * rows_per_block * row_bytes
+        rc = cudart.cudaMemcpyAsync(tgt.data_ptr() + off, o.data_ptr() + off, (b - a) * rows_per_block * row_bytes,
+                                    4, comm.cuda_stream)  # cudaMemcpyDefault: device to peer device
+        if rc != 0:
+            raise RuntimeError(f"cudaMemcpyAsync of a slab to rank 0 failed: {rc}")
 
     def step(i, rng=(lo, hi)):
         ins, o = sets[i % n_sets]
         xt.launch(mod, *launch_arrays(w, ins, o), bid0_range=rng)
 
     def sharded_step(i, start=None, end=None):
+        if dma and rank != 0:
+            # GEMM slab by slab into the local output; the copy engines push
+            # each finished slab to rank 0 while the next slab computes
+            ins, o = sets[i % n_sets]
+            if i >= n_sets:
+                stream.wait_event(gathered[i % n_sets])  # that step's pushes have read o
+            if start is not None:
+                start.record(stream)
+            for (a, b), ev in zip(slabs, slab_done):
+                xt.launch(mod, *launch_arrays(w, ins, o), bid0_range=(a, b))
+                ev.record(stream)
+                comm.wait_event(ev)
+                push_slab(o, targets[i % n_sets], a, b)
+            if end is not None:
+                end.record(stream)
+            gathered[i % n_sets].record(comm)
+            stream.wait_event(gathered[i % n_sets])  # every row has reached rank 0 ...
+            dist.all_reduce(flag)  # ... before the step's barrier
+            return
         if peer:
             ins, o = sets[i % n_sets][0], targets[i % n_sets]
             if start is not None:
@@ -1145,7 +1188,9 @@ def main() -> None:
                    else "working set larger than L2",
                    "timing": ("CUDA-graph replay of K launches, events recorded inside the graph"
                               if not sharded else "eager launches, events around each launch" if world == 1 else
-                              ("eager launches; rows stored into rank 0's output over NVLink, one-element "
+                              ("eager launches; slabs pushed into rank 0's output by the copy engines, "
+                               "one-element all-reduce per step" if dma else
+                               "eager launches; rows stored into rank 0's output over NVLink, one-element "
                                "all-reduce per step" if peer else
                                "eager launches; step i's NCCL gather overlaps step i+1's compute"))},
         "roofline": roofline,
