@@ -166,9 +166,11 @@ def test_gather_check_covers_every_shard_and_the_boundary_rows():
 def test_close_enough_modes():
     import numpy as np
     x = np.array([0.25, 0.5], np.float32)
-    assert bench.close_enough(x, x.copy(), "GB/s", "f32")["ok"]
-    assert bench.close_enough(x, x * (1 + 1e-4), "GB/s", "f32")["tolerance"].startswith("|d|/ref")
-    assert not bench.close_enough(x, x * (1 + 1e-4), "GB/s", "f32")["ok"]
+    assert bench.close_enough(x, x.copy(), "softmax")["ok"]
+    assert not bench.close_enough(x, x * (1 + 1e-4), "softmax")["ok"]
     y = np.array([-1.5, 2.0], np.float32)
-    assert not bench.close_enough(y, np.nextafter(y, np.inf), "GB/s", "f32")["ok"]  # bit-exact for add
-    assert bench.close_enough(y * 1.001, y, "TFLOP/s", "bf16")["ok"]
+    assert not bench.close_enough(y, np.nextafter(y, np.inf), "bit-exact")["ok"]  # add: one ulp is a failure
+    assert bench.close_enough(y, np.nextafter(y, np.inf), "transcendental")["ok"]  # silu: one ulp is fine
+    assert not bench.close_enough(y, y * 1.001, "transcendental")["ok"]
+    assert bench.close_enough(y * 1.001, y, "bf16")["ok"]
+    assert bench.tolerance_of({"dtype": "bf16"}) == "bf16" and bench.tolerance_of({"dtype": "f32"}) == "bit-exact"
