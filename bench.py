@@ -470,6 +470,30 @@ def gather_root_share(world: int, flops: float, out_bytes: float, tflops: float 
     return m / (t + m)
 
 
+def gather_step_ms(f: float, world: int, t_ms: float, r_ms: float, slabs: int = 0) -> float:
+    """Modelled step time with rank 0 computing a fraction ``f`` of the Grid.
+
+    ``t_ms``: the whole GEMM on one GPU; ``r_ms``: rank 0 taking in the whole
+    output.  Rank 0 computes f*T.  The other ranks' rows reach rank 0 at the
+    ingest rate: during their GEMM (stores from the epilogue, ``slabs`` 0),
+    or (copy engines, ``slabs`` S) only once a rank's first slab is done, and
+    the last slab's copy follows the rank's last GEMM slab.
+    """
+    if world == 1:
+        return t_ms
+    other = (1 - f) * t_ms / (world - 1)
+    if slabs <= 0:
+        return max(f * t_ms, (1 - f) * r_ms, other)
+    return max(f * t_ms, other / slabs + (1 - f) * r_ms, other + (1 - f) * r_ms / slabs)
+
+
+def plan_root_blocks(grid0: int, world: int, t_ms: float, r_ms: float, slabs: int = 0) -> int:
+    """Rank 0's Block count minimising ``gather_step_ms`` (each other rank keeps at least one Block)."""
+    best = min(range(1, grid0 - (world - 1) + 1),
+               key=lambda b: gather_step_ms(b / grid0, world, t_ms, r_ms, slabs))
+    return best
+
+
 def nccl_gather(out, rows_per_rank, world, rank, dist):
     if world == 1:
         return
@@ -795,11 +819,13 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference", "torch"],
                     help="b200: this backend; reference: the reference's CPU path; torch: the vendor library "
                          "(cuBLAS, cuDNN) through PyTorch on one GPU, for context")
-    ap.add_argument("--gather", default="peer", choices=["peer", "dma", "nccl"],
+    ap.add_argument("--gather", default="auto", choices=["auto", "peer", "dma", "nccl"],
                     help="sharded_matmul on N>1 GPUs: ranks store their rows straight into rank 0's output "
                          "over NVLink from the GEMM (peer), compute slabs locally and push each to rank 0 with "
-                         "the copy engines (dma), or compute locally and gather with NCCL")
-    ap.add_argument("--slabs", type=int, default=3,
+                         "the copy engines (dma), or compute locally and gather with NCCL; auto: peer on 2 GPUs, "
+                         "dma on more (rank 0's ingress binds from 3 GPUs on, where the copy engines deliver "
+                         "about twice the rows per second of SM-issued stores from one sender)")
+    ap.add_argument("--slabs", type=int, default=4,
                     help="dma gather: slabs per rank (each slab's copy overlaps the next slab's GEMM)")
     ap.add_argument("--root-share", type=float, default=None,
                     help="peer gather: rank 0's fraction of the Grid (default: balanced against its NVLink ingress)")
@@ -810,6 +836,8 @@ def main() -> None:
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.gather == "auto":
+        args.gather = "peer" if world <= 2 else "dma"
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     import torch
@@ -910,9 +938,10 @@ def main() -> None:
         # the ingest rate of the sender this run uses
         how = "copy_engines" if dma else "sm_stores"
         rates["sender"] = how
-        root_share = args.root_share if args.root_share is not None else gather_root_share(
-            world, plan["flops"], out_bytes, tflops=tflops, ingest_gbs=ingest[how])
         r_ms = out_bytes / (ingest[how] * 1e9) * 1e3
+        n_slabs = args.slabs if dma else 0
+        root_share = args.root_share if args.root_share is not None else (
+            plan_root_blocks(grid0, world, gemm_ms, r_ms, n_slabs) / grid0)
         rates["bound_ms"] = round(gemm_ms * r_ms / (gemm_ms + r_ms), 4)  # T*R/(T+R): no split does better
         rates["bound_note"] = ("T*R/(T+R): T the one-GPU GEMM, R rank 0 taking in the whole output at the "
                                f"measured ingest rate of the sender used ({how})")
@@ -1232,10 +1261,14 @@ def main() -> None:
         # rank 0's ingress of the others' rows, or another rank's share
         f = shares[0][1] / grid0
         t_ms, r_ms = rates["gemm_ms_1gpu"], w["out_shape"][0] * w["out_shape"][1] * 4 / (
-            rates["ingest_gbs"]["sm_stores"] * 1e9) * 1e3
-        terms = {"rank 0's own share of the GEMM": f * t_ms, "rank 0's NVLink ingress of the other ranks' rows":
-                 (1 - f) * r_ms, "the other ranks' shares of the GEMM": (1 - f) * t_ms / (world - 1)}
+            rates["ingest_gbs"][rates["sender"]] * 1e9) * 1e3
+        n_sl = args.slabs if dma else 0
+        other = (1 - f) * t_ms / (world - 1)
+        terms = {"rank 0's own share of the GEMM": f * t_ms,
+                 "rank 0's NVLink ingress of the other ranks' rows": (other / n_sl if n_sl else 0.0) + (1 - f) * r_ms,
+                 "the other ranks' shares of the GEMM": other + ((1 - f) * r_ms / n_sl if n_sl else 0.0)}
         rates["model_ms"] = {k: round(v, 4) for k, v in terms.items()}
+        rates["model_step_ms"] = round(gather_step_ms(f, world, t_ms, r_ms, n_sl), 4)
         rates["limiter"] = max(terms, key=terms.get)
         rates["efficiency_vs_bound"] = round(rates["bound_ms"] / ms_per_step, 4)
         line["gather_rates"] = rates

@@ -188,3 +188,19 @@ def test_rank_that_leaves_between_steps_fails_the_next_collective():
             p.terminate()
     assert kind != "completed"
     assert secs < 60
+
+
+def test_plan_root_blocks_minimises_the_step_model():
+    # one-GPU GEMM 3.18 ms, rank 0 ingesting the whole output in 1.42 ms
+    t, r = 3.18, 1.42
+    for world, slabs in ((2, 0), (4, 0), (8, 0), (4, 4), (8, 4)):
+        b0 = bench.plan_root_blocks(128, world, t, r, slabs)
+        best = bench.gather_step_ms(b0 / 128, world, t, r, slabs)
+        assert all(bench.gather_step_ms(b / 128, world, t, r, slabs) >= best - 1e-12 for b in range(1, 128 - world + 2))
+    # copy-engine slabs: more ranks finish their first slab sooner, so 8 GPUs model faster than 4
+    s4 = bench.gather_step_ms(bench.plan_root_blocks(128, 4, t, r, 4) / 128, 4, t, r, 4)
+    s8 = bench.gather_step_ms(bench.plan_root_blocks(128, 8, t, r, 4) / 128, 8, t, r, 4)
+    assert s8 < s4
+    # with stores from the GEMM itself the bound is T*R/(T+R) at any world >= 3
+    s = bench.gather_step_ms(bench.plan_root_blocks(128, 8, t, r, 0) / 128, 8, t, r, 0)
+    assert s >= t * r / (t + r) - 1e-9
