@@ -747,35 +747,28 @@ def _cudart(torch):
     return None
 
 
-def measure_ingest(xt, torch, dev, dist, rank: int, world: int, src, target, rows: tuple, flag,
-                   reps: int = 3) -> dict:
+def measure_ingest(torch, dev, dist, rank: int, src, target, rows: tuple, flag, gemm_send, reps: int = 3) -> dict:
     """Rate at which rank 0 takes in rows over NVLink while every other rank
     sends its rows [rows[0], rows[1]) at once, measured on rank 0 between two
-    all-reduces that bracket the transfer (max over none needed: rank 0's
-    interval covers every sender).  Two senders: this repository's ew kernel
-    (a load/store Block program whose output is rank 0's array, the same
-    SM-issued stores the GEMM's epilogue makes) and the copy engines (one
-    cudaMemcpyAsync per rank, device to peer device)."""
-    dsl = load_dsl()
-    A = dsl.Array
-    n_rows, n_cols = src.shape
+    all-reduces that bracket the transfer (rank 0's interval covers every
+    sender, so no maximum over ranks is needed).  Two senders:
 
-    @dsl.kernel
-    def copy_rows(inp, out, trow, col):
-        i = dsl.bid(0)
-        dsl.store(out, index=(i, 0), tile=dsl.load(inp, index=(i, 0), shape=(trow, col)))
-
-    trow = 32
-    mod = xt.parse(dsl.trace_text(copy_rows, args=(A((n_rows, n_cols), dsl.float32), A((n_rows, n_cols), dsl.float32),
-                                                   trow, n_cols), grid=(n_rows // trow, 1, 1), double_buffering=True))
+    * ``gemm_stores``: ``gemm_send()`` launches the sharded GEMM for this
+      rank's Blocks with rank 0's array as its output, so the rows go out as
+      the GEMM's epilogue stores them (128-byte TMA row segments) while it
+      computes; when the GEMM itself takes longer than the transfer (two
+      GPUs) this is a lower bound on the store rate;
+    * ``copy_engines``: one cudaMemcpyAsync per rank, device to peer device.
+    """
     lo, hi = rows
+    n_cols = src.shape[1]
     nbytes = (hi - lo) * n_cols * 4
     total = torch.tensor([float(nbytes if rank else 0)], device=dev)
     dist.all_reduce(total)
     cudart = _cudart(torch)
     stream = torch.cuda.current_stream(dev)
     res = {}
-    for how in ("sm_stores", "copy_engines"):
+    for how in ("gemm_stores", "copy_engines"):
         if how == "copy_engines" and cudart is None:
             continue
         best = None
@@ -785,8 +778,8 @@ def measure_ingest(xt, torch, dev, dist, rank: int, world: int, src, target, row
             dist.all_reduce(flag)
             e0.record(stream)
             if rank != 0 and hi > lo:
-                if how == "sm_stores":
-                    xt.launch(mod, src, target, bid0_range=(lo // trow, hi // trow))
+                if how == "gemm_stores":
+                    gemm_send()
                 else:
                     off = lo * n_cols * 4
                     rc = cudart.cudaMemcpyAsync(target.data_ptr() + off, src.data_ptr() + off, nbytes, 4,
@@ -799,7 +792,7 @@ def measure_ingest(xt, torch, dev, dist, rank: int, world: int, src, target, row
             ms = e0.elapsed_time(e1)
             best = ms if best is None else min(best, ms)
         t = torch.tensor([best], device=dev)
-        dist.broadcast(t, src=0)  # rank 0's interval is the one that covers every sender
+        dist.broadcast(t, src=0)
         res[how] = round(total.item() / (t.item() * 1e-3) / 1e9, 1)
     res["bytes"] = int(total.item())
     res["how"] = ("rank 0 times, between two all-reduces, every other rank sending its equal share of the "
@@ -823,9 +816,9 @@ def main() -> None:
                     help="sharded_matmul on N>1 GPUs: ranks store their rows straight into rank 0's output "
                          "over NVLink from the GEMM (peer), compute slabs locally and push each to rank 0 with "
                          "the copy engines (dma), or compute locally and gather with NCCL; auto: peer on 2 GPUs, "
-                         "dma on more (rank 0's ingress binds from 3 GPUs on, where the copy engines deliver "
-                         "about twice the rows per second of SM-issued stores from one sender)")
-    ap.add_argument("--slabs", type=int, default=4,
+                         "dma on more (rank 0's NVLink ingress binds from 3 GPUs on; the copy engines fill it, measured "
+                         "778 GB/s, and the slabs let rank 0 keep a smaller share)")
+    ap.add_argument("--slabs", type=int, default=6,
                     help="dma gather: slabs per rank (each slab's copy overlaps the next slab's GEMM)")
     ap.add_argument("--root-share", type=float, default=None,
                     help="peer gather: rank 0's fraction of the Grid (default: balanced against its NVLink ingress)")
@@ -910,10 +903,11 @@ def main() -> None:
         if rank != 0:
             targets = [xt.PeerArray.open(h, tuple(w["out_shape"]), w["out_dtype"]) for h in box[0]]
 
-    # ---- peer gather: rank 0's share of the Grid from rates measured here.
+    # ---- row gather: rank 0's share of the Grid from rates measured here.
     # T: the whole GEMM on one GPU (every rank times its equal share; the
-    # slowest share times N).  R: rank 0 taking in the whole output at the
-    # ingest rate of SM-issued stores from all other ranks at once.
+    # slowest share times N).  R: rank 0 taking in the whole output from all
+    # other ranks at once, at the measured rate of the sender this run uses
+    # (the GEMM's own stores, or the copy engines).
     rates = None
     root_share = None
     if peer:
@@ -931,12 +925,13 @@ def main() -> None:
         gemm_ms = t.item() * world
         src = sets[1][1]  # a local buffer of the output's shape (rank 0's is never sent)
         rows = (even_lo * rows_per_block, even_hi * rows_per_block)
-        ingest = measure_ingest(xt, torch, dev, dist, rank, world, src, targets[0], rows, flag)
+        ingest = measure_ingest(torch, dev, dist, rank, src, targets[0], rows, flag, lambda: xt.launch(
+            mod, *launch_arrays(w, sets[0][0], targets[0]), bid0_range=(even_lo, even_hi)))
         out_bytes = w["out_shape"][0] * w["out_shape"][1] * 4
         tflops = plan["flops"] / (gemm_ms * 1e-3) / 1e12
         rates = {"gemm_tflops_1gpu": round(tflops, 1), "gemm_ms_1gpu": round(gemm_ms, 4), "ingest_gbs": ingest}
         # the ingest rate of the sender this run uses
-        how = "copy_engines" if dma else "sm_stores"
+        how = "copy_engines" if dma else "gemm_stores"
         rates["sender"] = how
         r_ms = out_bytes / (ingest[how] * 1e9) * 1e3
         n_slabs = args.slabs if dma else 0
