@@ -78,8 +78,8 @@ NCU_TRAFFIC_BYTES: dict[str, float] = {
     "sharded_matmul": 6_210_000_000 + 1_060_000_000,
     "transpose": 134_227_712 + 88_921_088,
     "matmul_i8": 215_210_496 + 55_281_408,
-    "silu": 134_347_776 + 91_669_760,
-    "row_center": 134_287_104 + 86_616_320,
+    "silu": 134_240_512 + 84_709_376,
+    "row_center": 134_223_360 + 78_821_120,
 }
 
 
