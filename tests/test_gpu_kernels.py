@@ -485,6 +485,34 @@ def test_conv_bf16_shapes(shape, kshape, tile, pad, dil):
     bf16_close(got, ref)
 
 
+@pytest.mark.parametrize("sms,shape,dtype", [
+    (8, (6, 20, 30, 64), torch.bfloat16),    # 6 strips x 3 tiles on 8 CTAs: 2 waves and a partial one
+    (6, (5, 17, 45, 64), torch.bfloat16),    # odd sizes
+    (4, (3, 16, 32, 64), torch.int8),        # int8, exact
+])
+def test_conv_window_several_waves(sms, shape, dtype):
+    # Few CTAs (an SM budget): each CTA runs several tiles through its window
+    # ring and both accumulators, the last wave partial.
+    n, h, w, c = shape
+    g = gen(9)
+    if dtype == torch.int8:
+        x = torch.randint(-16, 16, shape, generator=g, dtype=torch.int8)
+        f = torch.randint(-16, 16, (3, 3, c, 64), generator=g, dtype=torch.int8)
+    else:
+        x = (torch.randn(*shape, generator=g) * 0.1).to(dtype)
+        f = (torch.randn(3, 3, c, 64, generator=g) * 0.1).to(dtype)
+    out = torch.full((n, h, w, 64), float("nan"), device=DEV)
+    with xt.sm_budget(sms):
+        m = xt.run(conv2d_tiles, args=(x.to(DEV), f.to(DEV), out, h, w, c, 64, 3, 3, 1, 1, 1, 1), grid=(n, 1, 1))
+    assert m.plan()["family"] == "conv"
+    ref = oracle(m, [x, f, torch.zeros(n, h, w, 64)])[2]
+    got = host(out)
+    if dtype == torch.int8:
+        assert np.array_equal(got, ref)
+    else:
+        bf16_close(got, ref)
+
+
 def test_conv_int8_two_images_bit_exact():
     # two images, stacked taps with kind::i8
     got, ref = conv_case((2, 16, 32, 128), (3, 3, 128, 64), (16, 32), torch.int8, 8)
