@@ -86,3 +86,53 @@ def free_port():
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_rows_stored_into_rank0_over_nvlink():
     mp.start_processes(worker, args=(2, free_port()), nprocs=2, join=True, start_method="spawn")
+
+
+def leave_worker(rank, world, port):
+    # a rank leaves between steps; the other learns of it through the
+    # heartbeat before launching the next collective, reads the communicator's
+    # asynchronous error and aborts the communicator with nothing in flight
+    from xtile_b200 import ranks
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    ranks.init_nccl(dev, timeout_s=20.0, blocking=False)
+    hb = ranks.Heartbeat(rank, world)
+    t = torch.ones(4, device=dev)
+    for step in range(3):
+        if rank == 1 and step == 1:
+            torch.cuda.synchronize()
+            os._exit(0)
+        hb.beat(step)
+        try:
+            hb.wait_all(step, deadline_s=3.0)
+        except ranks.PeerLost:
+            assert step == 1
+            try:
+                ranks.check(dev)  # the peer's exit may already show as a remote error
+            except RuntimeError:
+                pass
+            ranks.abort(dev)
+            return
+        dist.all_reduce(t)
+        torch.cuda.synchronize()
+        assert t[0].item() == 2 ** (step + 1)
+    raise AssertionError("the lost rank went unnoticed")
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_nccl_rank_leaving_between_steps_is_noticed_on_the_host():
+    ctx = mp.get_context("spawn")
+    port = free_port()
+    procs = [ctx.Process(target=leave_worker, args=(r, 2, port)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.terminate()
+    assert codes == [0, 0], codes

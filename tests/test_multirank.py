@@ -204,3 +204,41 @@ def test_plan_root_blocks_minimises_the_step_model():
     # with stores from the GEMM itself the bound is T*R/(T+R) at any world >= 3
     s = bench.gather_step_ms(bench.plan_root_blocks(128, 8, t, r, 0) / 128, 8, t, r, 0)
     assert s >= t * r / (t + r) - 1e-9
+
+
+def heartbeat_worker(rank, world, port, result_q):
+    import datetime
+
+    from xtile_b200 import ranks
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    hb = ranks.Heartbeat(rank, world)
+    t = torch.ones(4)
+    for step in range(3):
+        if rank == 1 and step == 1:
+            os._exit(0)  # leaves between steps, before announcing step 1
+        hb.beat(step)
+        try:
+            hb.wait_all(step, deadline_s=2.0)
+        except ranks.PeerLost as e:
+            result_q.put(("lost", step, str(e)))
+            return  # the survivor stops before launching the step's collective
+        dist.all_reduce(t)
+    result_q.put(("done", 3, ""))
+
+
+def test_heartbeat_notices_a_rank_that_left_before_the_next_collective():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=heartbeat_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    kind, step, msg = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.terminate()
+    assert kind == "lost" and step == 1 and "ranks [1]" in msg
