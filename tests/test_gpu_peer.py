@@ -97,7 +97,7 @@ def leave_worker(rank, world, port):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    ranks.init_nccl(dev, timeout_s=20.0, blocking=False)
+    ranks.init_nccl(dev, timeout_s=20.0, blocking=False, rank=rank, world_size=world)
     hb = ranks.Heartbeat(rank, world)
     t = torch.ones(4, device=dev)
     for step in range(3):

@@ -27,16 +27,18 @@ class PeerLost(RuntimeError):
     """A peer did not reach a step within the heartbeat deadline."""
 
 
-def init_nccl(device, timeout_s: float = 30.0, blocking: bool = False):
-    """NCCL process group for ``device`` (rank and world size from the
-    environment, as torchrun sets them); returns the group."""
+def init_nccl(device, timeout_s: float = 30.0, blocking: bool = False, rank: int | None = None,
+              world_size: int | None = None):
+    """NCCL process group for ``device``; ``rank`` and ``world_size`` default
+    to the environment's (torchrun sets them).  Returns the group."""
     import torch.distributed as dist
     from torch._C._distributed_c10d import ProcessGroupNCCL
 
     opts = ProcessGroupNCCL.Options()
     opts.config.blocking = blocking
+    kw = {} if rank is None else {"rank": rank, "world_size": world_size}
     dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=timeout_s),
-                            pg_options=opts)
+                            pg_options=opts, **kw)
     return dist.group.WORLD
 
 
