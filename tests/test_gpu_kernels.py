@@ -111,7 +111,7 @@ def ew_mixed(x, y, out, out2, trow, col):
     xt.store(out2, index=(i, 0), tile=xt.sigmoid(t) + xt.tanh(b))
 
 
-def test_ew_interpreter_program():
+def test_ew_generated_program():
     g = gen(2)
     a = torch.randn(300, 50, generator=g)
     b = torch.randn(300, 50, generator=g)
@@ -134,10 +134,10 @@ def ew_int8(q, r, y, yq, trow, col):
     xt.store(yq, index=(i, 0), tile=xt.astype(t, dtype=xt.int8))
 
 
-def test_ew_interpreter_int8_casts_tail_and_shards_bit_exact():
+def test_ew_generated_int8_casts_tail_and_shards_bit_exact():
     # 7 x 13 = 91 elements: 22 groups of four (4-byte int8 and 16-byte f32
     # accesses) and a tail of 3; a bid0 shard starting at element 13 runs the
-    # one-element interpreter.  ftoi rounds half to even and saturates.
+    # element-at-a-time kernel.  ftoi rounds half to even and saturates.
     g = gen(29)
     q = torch.randint(-128, 128, (7, 13), generator=g, dtype=torch.int8)
     r = torch.randn(7, 13, generator=g) * 3
@@ -163,9 +163,9 @@ def ew_copy(x, y, trow, col):
 
 @pytest.mark.parametrize("shape,trow", [((64, 200), 16), ((9, 35), 3)])
 def test_ew_bf16_copy_bit_exact(shape, trow):
-    # bf16 through the ew interpreter: 8-byte groups of four; 9 x 35 = 315
+    # bf16 through the generated ew kernel: 8-byte groups of four; 9 x 35 = 315
     # elements leave a 3-element tail, and its bid0 shard starting at element
-    # 105 takes the one-element form; values pass through f32 and come back
+    # 105 takes the element-at-a-time kernel; values pass through f32 and come back
     # bit for bit
     x = torch.randn(*shape, generator=gen(31)).to(torch.bfloat16)
     y = torch.zeros(*shape, dtype=torch.bfloat16, device=DEV)
