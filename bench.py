@@ -1064,10 +1064,16 @@ def main() -> None:
         total_ms = t_begin.elapsed_time(t_end)
         kernel_ms = statistics.fmean(s.elapsed_time(e) for s, e in zip(starts, ends))
     del graph
+    # this repository's kernels launched in the timed region, summed over ranks
+    # (a rank pushing slabs launches one GEMM per slab)
+    launches = args.steps * (len(slabs) if dma and rank != 0 else 1)
     if dist:
         t = torch.tensor([total_ms, kernel_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms, kernel_ms = t.tolist()
+        n = torch.tensor([float(launches)], device=dev)
+        dist.all_reduce(n)
+        launches = int(n.item())
     clock = clocks.summary()
     err = xt.device_error()
 
@@ -1241,7 +1247,7 @@ def main() -> None:
                                "eager launches; step i's NCCL gather overlaps step i+1's compute"))},
         "roofline": roofline,
         "clocks": clock,
-        "gpu_launches": args.steps,
+        "gpu_launches": launches,
         "device_error": err,
     }
     if compute is not None:
