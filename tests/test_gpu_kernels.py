@@ -222,7 +222,7 @@ def row_stats(x, y, mx, trow, col):
 
 
 @pytest.mark.parametrize("rows,cols", [(96, 200), (64, 1024), (50, 37), (33, 128), (40, 2048), (20, 1531)])
-def test_row_program_interpreter(rows, cols):
+def test_row_program_generated(rows, cols):
     # cols a multiple of 4: float4 accesses; 37 and 1531 columns: element
     # accesses with a guard per element (partial last chunk of every row)
     x = torch.randn(rows, cols, generator=gen(4)) + 3
