@@ -1125,13 +1125,26 @@ def main() -> None:
         # keep a copy-in from overwriting inputs a kernel still reads and a
         # kernel from overwriting a result still being copied out.  Every step
         # moves all of its inputs in and its whole result out.
-        e_streams = [torch.cuda.Stream(dev) for _ in range(3)] if world == 1 else None
+        # The same pipeline on N GPUs when the rows reach rank 0 without a
+        # collective (peer and dma modes; the launch stores straight into rank
+        # 0's output): every rank copies its inputs in and launches, rank 0
+        # copies the whole result out.  A second one-element all-reduce before
+        # each launch keeps every rank from writing an output set of rank 0's
+        # before rank 0 has copied that set's previous result out.
+        e_streams = [torch.cuda.Stream(dev) for _ in range(3)] if (world == 1 or peer or not sharded) else None
         if e_streams:
             e_note = ("three streams (copy in, launch, copy out) over two buffer sets: step j+1's "
                       "host-to-device copies overlap step j's device-to-host copy")
-            e_sets = [sets[0], ([torch.empty_like(t) for t in ins], torch.empty_like(o))]
+            if peer:
+                e_note += ("; on N GPUs every rank's launch stores into rank 0's output (with --gather dma "
+                           "too: the GEMM's own stores), rank 0 copies the whole result out, two one-element "
+                           "all-reduces per step order the sets")
+                e_sets = [(ins, targets[0]), ([torch.empty_like(t) for t in ins], targets[1])]
+            else:
+                e_sets = [sets[0], ([torch.empty_like(t) for t in ins], torch.empty_like(o))]
             host_outs = [host_out, torch.empty_like(host_out).pin_memory()]
             ev_in, ev_k, ev_out = ([torch.cuda.Event() for _ in range(2)] for _ in range(3))
+            flag2 = torch.zeros(1, device=dev)
 
         def e2e_step_pipe(j):
             b = j % 2
@@ -1149,14 +1162,19 @@ def main() -> None:
                 ev_in[b].record(s_in)
             with torch.cuda.stream(s_k):
                 s_k.wait_event(ev_in[b])
-                if j >= 2:
+                if j >= 2 and host_outs[b].numel():
                     s_k.wait_event(ev_out[b])  # step j - 2's result has been copied out
+                if peer and j >= 2:
+                    dist.all_reduce(flag2)  # ... on rank 0, before any rank writes set b again
                 xt.launch(mod, *launch_arrays(w, e_ins, e_o), bid0_range=(lo, hi))
+                if peer:
+                    dist.all_reduce(flag)  # every rank's rows are in rank 0's set b
                 ev_k[b].record(s_k)
-            with torch.cuda.stream(s_out):
-                s_out.wait_event(ev_k[b])
-                host_outs[b].copy_(e_o, non_blocking=True)
-                ev_out[b].record(s_out)
+            if host_outs[b].numel():
+                with torch.cuda.stream(s_out):
+                    s_out.wait_event(ev_k[b])
+                    host_outs[b].copy_(e_o, non_blocking=True)
+                    ev_out[b].record(s_out)
 
         def e2e_step():
             if sharded:
