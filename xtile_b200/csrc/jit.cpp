@@ -118,13 +118,12 @@ std::mutex g_mu;
 std::unordered_map<std::string, std::unique_ptr<Program>> g_programs;
 
 // The fixed part of a program's launch arguments: what its generated source
-// depends on.
-template <class Args>
-std::string key_of(char family, const Args& a, const Instr* code, int n_code, const std::string& extra) {
+// depends on (the family, the register code, and ``extra``: element types,
+// broadcast flags, row width).
+std::string key_of(char family, const Instr* code, int n_code, const std::string& extra) {
   std::string k(1, family);
   k.append(reinterpret_cast<const char*>(code), sizeof(Instr) * static_cast<size_t>(n_code));
   k += extra;
-  (void)a;
   return k;
 }
 
@@ -239,7 +238,7 @@ cudaError_t launch_ew(const dev::EwArgs& a, cudaStream_t stream) {
     extra += static_cast<char>(k < a.n_in ? a.in_bcast[k] : 0);
     extra += static_cast<char>(k < a.n_out ? a.out_elem[k] : 255);
   }
-  const std::string key = key_of('e', a, a.code, a.n_code, extra);
+  const std::string key = key_of('e', a.code, a.n_code, extra);
   // the vector kernel: a range starting at a multiple of 4 elements, arrays
   // aligned to 4 elements of their type, broadcast rows a multiple of 4 long
   bool v4 = a.begin % 4 == 0 && a.bcast_period % 4 == 0;
@@ -273,7 +272,7 @@ cudaError_t launch_rows(const dev::RowArgs& a, cudaStream_t stream) {
     extra += static_cast<char>(a.in_scalar[k]);
     extra += static_cast<char>(a.out_scalar[k]);
   }
-  const std::string key = key_of('r', a, a.code, a.n_code, extra);
+  const std::string key = key_of('r', a.code, a.n_code, extra);
   bool vec = a.cols % 4 == 0;
   for (int k = 0; k < kMaxSlots && vec; ++k) {
     if (a.in[k] && !a.in_scalar[k]) vec = (reinterpret_cast<uintptr_t>(a.in[k]) & 15) == 0;
