@@ -271,6 +271,22 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
             tol = "bit-exact"
         return dict(text=text, inputs=inputs, work=work, tolerance=tol, out_shape=(R, C), out_dtype=torch.float32, unit="GB/s", dtype="f32",
                     config={"workload": name, "shape": [R, C], "block_tile": tile, "grid": grid})
+    if name == "col_sums":
+        # not a BASELINE configuration: a tile program (column sums of 64 x 32
+        # tiles, float64 accumulation) over a 128 MiB f32 array
+        @xt.kernel
+        def col_sums(x, out, tm, tn):
+            i, j = xt.bid(0), xt.bid(1)
+            t = xt.load(x, index=(i, j), shape=(tm, tn))
+            xt.store(out, index=(i, j), tile=xt.sum(t, axis=0))
+
+        R, C, tm, tn = 16384, 2048, 64, 32
+        x = torch.randn(R, C, generator=g(9))
+        text = xt.trace_text(col_sums, args=(A((R, C), xt.float32), A((R // tm, C), xt.float32), tm, tn),
+                             grid=(R // tm, C // tn, 1), double_buffering=True)
+        return dict(text=text, inputs=[x], work=(R * C + R // tm * C) * 4, tolerance="sum", out_shape=(R // tm, C),
+                    out_dtype=torch.float32, unit="GB/s", dtype="f32",
+                    config={"workload": name, "shape": [R, C], "block_tile": [tm, tn], "grid": [R // tm, C // tn, 1]})
     raise SystemExit(f"unknown workload {name}")
 
 
@@ -554,6 +570,7 @@ TOLERANCES = {
     "bit-exact": "bit-exact",
     "softmax": "|d|/ref <= 1e-5",
     "transcendental": "|d| <= 1e-5 |ref| + 1e-6",
+    "sum": "|d| <= 1e-6 |ref| + 1e-6",
     "bf16": "max|d|/max|ref| <= 1e-2 and |d| <= 1e-2|ref| + 1e-2 rms(ref)",
 }
 
@@ -562,7 +579,9 @@ def tolerance_of(w: dict) -> str:
     """The parity bar of a workload's path: exact f32 arithmetic (add, sub,
     mul, max, data movement) bit-exact; the row softmax 1e-5 relative per
     element; programs with f32 transcendentals (their CUDA math functions
-    against the oracle's float64 ones) 1e-5 relative plus 1e-6; bf16
+    against the oracle's float64 ones) 1e-5 relative plus 1e-6; tile sums
+    (float64 accumulation in another order than numpy's) 1e-6 relative plus
+    1e-6; bf16
     tensor-core work with f32 accumulation 1e-2 of the output's scale."""
     return w.get("tolerance", "bf16" if w["dtype"] == "bf16" else "bit-exact")
 
@@ -583,10 +602,11 @@ def close_enough(got, ref, tol: str) -> dict:
     if tol == "softmax":
         rel = float(np.max(d / r))
         return {"ok": bool(np.all(r > 0) and rel <= 1e-5), "max_rel": rel, "tolerance": TOLERANCES[tol]}
-    if tol == "transcendental":
+    if tol in ("transcendental", "sum"):
+        rtol, atol = (1e-5, 1e-6) if tol == "transcendental" else (1e-6, 1e-6)
         ok = bool(np.all(np.isfinite(g) == np.isfinite(r)))
         fin = np.isfinite(r)
-        ok = ok and bool(np.all(d[fin] <= 1e-5 * np.abs(r[fin]) + 1e-6))
+        ok = ok and bool(np.all(d[fin] <= rtol * np.abs(r[fin]) + atol))
         rel = float(np.max(d[fin] / np.maximum(np.abs(r[fin]), 1e-30))) if fin.any() else 0.0
         return {"ok": ok, "max_rel": rel, "tolerance": TOLERANCES[tol]}
     same = bool(np.array_equal(got.view(np.uint32), ref.view(np.uint32)))
@@ -808,7 +828,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="sharded_matmul",
                     choices=["add", "softmax", "matmul", "conv2d", "sharded_matmul", "transpose", "silu",
-                             "row_center", "row_bias", "matmul_i8"])
+                             "row_center", "row_bias", "matmul_i8", "col_sums"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference", "torch"],
                     help="b200: this backend; reference: the reference's CPU path; torch: the vendor library "
                          "(cuBLAS, cuDNN) through PyTorch on one GPU, for context")
@@ -1355,6 +1375,9 @@ def run_torch_library(args, torch) -> None:
         lib = "torch.addcmul(r, x, r, out=)"
         fn = lambda i: torch.addcmul(sets[i % n_sets][1], sets[i % n_sets][0], sets[i % n_sets][1],  # noqa: E731
                                      out=outs[i % n_sets])
+    elif name == "col_sums":
+        lib = "torch.sum over the 64-row tiles (f32 accumulation, out=)"
+        fn = lambda i: torch.sum(sets[i % n_sets][0].view(256, 64, 2048), dim=1, out=outs[i % n_sets])  # noqa: E731
     else:
         lib = "cuDNN via torch.nn.functional.conv2d, channels-last bf16 in, bf16 out"
         fn = lambda i: torch.nn.functional.conv2d(sets[i % n_sets][0], sets[i % n_sets][1], padding=1)  # noqa: E731

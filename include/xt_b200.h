@@ -135,9 +135,10 @@ int xt_device_error(uint32_t* out_code);
  * GEMM rounds the budget down to an even number (its CTAs come in pairs). */
 int xt_set_sm_budget(int sms);
 
-/* No counterpart in the reference.  Elementwise and row programs (other than
- * the dedicated add and softmax kernels) run in kernels generated for the
- * program and compiled at their first launch with NVRTC for sm_100a.
+/* No counterpart in the reference.  Elementwise, row and tile programs
+ * (other than those the dedicated add, softmax and data-movement kernels
+ * run) run in kernels generated for the program and compiled at their first
+ * launch with NVRTC for sm_100a.
  * xt_generated_source gives that CUDA source for ``func`` (NULL: the first)
  * in a malloc'ed string (free with xt_string_free); XT_EUNSUPPORTED for
  * programs that run a compiled kernel.  xt_compile_generated compiles such a

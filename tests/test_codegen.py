@@ -1,11 +1,12 @@
-"""The per-program kernels of the ew and rows families, generated and compiled
-for sm_100a on the CPU (NVRTC needs no GPU).
+"""The per-program kernels of the ew, rows and tile families, generated and
+compiled for sm_100a on the CPU (NVRTC needs no GPU).
 
-Every elementwise or row program among the 36 seeded random programs of the
-GPU parity test, row programs of several widths and programs with
-bf16 / int8 arrays and casts must produce source that NVRTC compiles for
-sm_100a.  What the kernels compute is checked on a GPU against the oracle
-(``tests/test_gpu_random_programs.py``, ``tests/test_gpu_kernels.py``).
+Every elementwise, row or tile program among the 36 seeded random programs
+of the GPU parity test, row programs of several widths, the tile programs of
+the tile GPU tests and programs with bf16 / int8 arrays and casts must
+produce source that NVRTC compiles for sm_100a.  What the kernels compute is
+checked on a GPU against the oracle (``tests/test_gpu_random_programs.py``,
+``tests/test_gpu_kernels.py``, ``tests/test_gpu_tile.py``).
 """
 import pytest
 
@@ -34,7 +35,7 @@ def test_random_program_compiles(seed):
         fam = m.plan()["family"]
     except RuntimeError:
         pytest.skip("beyond every family's limits")
-    if fam not in ("ew", "rows"):
+    if fam not in ("ew", "rows", "tile"):
         with pytest.raises(RuntimeError, match="runs a compiled kernel"):
             generated(m)
         return
@@ -113,3 +114,50 @@ def test_softmax_keeps_its_dedicated_kernel():
 def test_compile_errors_carry_the_log():
     with pytest.raises(RuntimeError, match="(?s)NVRTC failed.*not_a_function.*undefined"):
         native.compile_generated("extern \"C\" __global__ void k() { not_a_function(); }")
+
+
+import tests.test_gpu_tile as tile_cases  # noqa: E402
+
+RANK4_PERMUTE = """func.func @r(%x: memref<4x6x10x12xf32>, %y: memref<4x10x6x12xf32>) attributes {xt.grid = array<i32: 2, 1, 2>} {
+  %bid:3 = xt.get_tile_block_id : i32, i32, i32
+  %zero = arith.constant 0 : i32
+  %t = xt.load(%x, %bid#0, %zero, %bid#2, %zero) : (memref<4x6x10x12xf32>, i32, i32, i32, i32) -> tensor<2x6x5x12xf32>
+  %p = xt.permute(%t) {permutation = [0, 2, 1, 3]} : tensor<2x6x5x12xf32> -> tensor<2x5x6x12xf32>
+  %u = xt.mul(%p, %p) : tensor<2x5x6x12xf32>, tensor<2x5x6x12xf32> -> tensor<2x5x6x12xf32>
+  xt.store(%u, %y, %bid#0, %bid#2, %zero, %zero) : (tensor<2x5x6x12xf32>, memref<4x10x6x12xf32>, i32, i32, i32, i32) -> ()
+  func.return
+}"""
+
+
+@pytest.mark.parametrize("case", ["col_stats", "col_vector_ops", "i8_wrap", "row_stats_tiles", "rank4"])
+def test_tile_programs_compile(case):
+    F, I8 = xt.float32, xt.int8
+    if case == "col_stats":
+        # column sums and maxima: 64 x 32 tiles, 64-thread CTAs, float4
+        # loads, each column's 64 rows split over two threads
+        m = xt.convert(tile_cases.col_stats, args=(A((16384, 2048), F), A((256, 2048), F), A((256, 2048), F), 64, 32),
+                       grid=(256, 64, 1))
+        want = ("xt_ld4_f32_kept", "xt_st4_f32", "static_cast<double>", "__launch_bounds__(64)", "xt_red_f64[part")
+    elif case == "col_vector_ops":
+        m = xt.convert(tile_cases.col_vector_ops, args=(A((96, 1024), F), A((96, 1), F), A((96, 1024), F), 8, 512),
+                       grid=(12, 2, 1))
+        want = ("xt_sigmoid", "__launch_bounds__(128)")  # 4096-element tiles
+    elif case == "i8_wrap":
+        m = xt.convert(tile_cases.i8_wrap, args=(A((64, 96), I8), A((1, 96), I8), A((64, 96), I8), 32, 48),
+                       grid=(2, 2, 1))
+        want = ("xt_wrap_i8", "xt_ld4_i8", "xt_st4_i8")
+    elif case == "row_stats_tiles":
+        # a ragged edge along both dims: limits computed per Block
+        m = xt.convert(tile_cases.row_stats_tiles, args=(A((100, 70), F), A((100, 3), F), A((100, 3), F), 32, 32),
+                       grid=(4, 3, 1))
+        want = ("const int l", "xt_max_nan")
+    else:
+        # rank-4 tiles with leading dims above 1: rows unravel into (i0, i1, i2)
+        m = xt.parse(RANK4_PERMUTE)
+        want = ("xt_ld1_f32", "i0 = q / 30", "xt_mul")
+    assert m.plan()["family"] == "tile"
+    src = generated(m)
+    for w in want:
+        assert w in src, w
+    assert "switch" not in src.split("xt_warp_sum")[-1]
+    assert compiles(m)

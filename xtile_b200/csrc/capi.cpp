@@ -209,6 +209,26 @@ xt::dev::RowArgs row_args_of(const xt::RowPlan& r, void* const* args) {
   return a;
 }
 
+// Launch arguments of a tile plan (every Block of the grid); ``args`` null
+// leaves the pointers null.
+xt::dev::TileArgs tile_args_of(const xt::Plan& p, void* const* args) {
+  const xt::TilePlan& t = p.tile;
+  xt::dev::TileArgs a{};
+  for (int i = 0; i < t.n_args; ++i) {
+    a.arr[i] = args ? args[t.arg[i]] : nullptr;
+    a.elem[i] = elem_code(t.arg_elem[i]);
+    for (int d = 0; d < xt::kTileRank; ++d) a.shape[i][d] = t.arg_shape[i][d];
+  }
+  for (size_t i = 0; i < t.vals.size(); ++i) a.vals[i] = t.vals[i];
+  for (size_t i = 0; i < t.ops.size(); ++i) a.ops[i] = t.ops[i];
+  a.n_ops = static_cast<int>(t.ops.size());
+  a.smem_floats = t.smem_floats;
+  for (int k = 0; k < 3; ++k) a.grid[k] = p.grid[k];
+  a.bid0_begin = 0;
+  a.bid0_end = p.grid[0];
+  return a;
+}
+
 int launch_plan(const xt::Plan& p, void* const* args, int64_t b0, int64_t b1, cudaStream_t stream) {
   using namespace xt;
   const int64_t g0 = p.grid[0];
@@ -302,19 +322,7 @@ int launch_plan(const xt::Plan& p, void* const* args, int64_t b0, int64_t b1, cu
       return err == cudaSuccess ? XT_OK : cuda_fail(err, "conv kernel launch");
     }
     case Family::Tile: {
-      const TilePlan& t = p.tile;
-      dev::TileArgs a{};
-      for (int i = 0; i < t.n_args; ++i) {
-        a.arr[i] = args[t.arg[i]];
-        a.elem[i] = elem_code(t.arg_elem[i]);
-        for (int d = 0; d < kTileRank; ++d) a.shape[i][d] = t.arg_shape[i][d];
-      }
-      for (size_t i = 0; i < t.vals.size(); ++i) a.vals[i] = t.vals[i];
-      for (size_t i = 0; i < t.ops.size(); ++i) a.ops[i] = t.ops[i];
-      a.n_ops = static_cast<int>(t.ops.size());
-      a.smem_floats = t.smem_floats;
-      a.rows = t.rows ? 1 : 0;
-      for (int k = 0; k < 3; ++k) a.grid[k] = p.grid[k];
+      dev::TileArgs a = tile_args_of(p, args);
       a.bid0_begin = clamp64(b0, 0, g0);
       a.bid0_end = clamp64(b1, 0, g0);
       if (a.bid0_end <= a.bid0_begin) return XT_OK;
@@ -640,6 +648,10 @@ int xt_generated_source(const xt_module* module, const char* func, char** out_te
       text = xt::jit::ew_source(ew_args_of(p->ew, nullptr));
     else if (p->family == xt::Family::Rows && !p->rows.softmax)
       text = xt::jit::rows_source(row_args_of(p->rows, nullptr));
+    else if (p->family == xt::Family::Tile) {
+      const xt::dev::TileArgs a = tile_args_of(*p, nullptr);
+      text = xt::jit::tile_source(a, xt::jit::tile_threads(a));
+    }
     else
       return fail(XT_EUNSUPPORTED, "xt_generated_source: @" + p->func + " runs a compiled kernel ('" +
                                        xt::family_name(p->family) + "' family)");

@@ -10,6 +10,8 @@
 #include "codegen.h"
 
 #include <algorithm>
+#include <cstdio>
+#include <cstring>
 #include <set>
 #include <sstream>
 
@@ -341,5 +343,413 @@ std::string rows_source(const dev::RowArgs& a) {
   return s.str();
 }
 
+
+// ---------------------------------------------------------------------------
+// Tile programs.  The generated kernel keeps the interpreter's model -- one
+// CTA per Block, every tile value in its planned shared-memory slot (f32,
+// row-major, rows padded to an odd pitch), the ops in program order with a
+// CTA barrier between them -- but every shape, pitch, slot offset, array
+// stride, tile coordinate and edge limit is a constant of the source.  A
+// value of shape (s0, s1, s2, s3) is s0*s1*s2 rows of s3 elements at one
+// pitch, so each op is a loop of the CTA's threads over (row q, column c)
+// with constant bounds; when the CTA width is a multiple of the row length a
+// thread keeps one column and steps whole rows.  Loads keep up to 8 accesses
+// in flight per thread; accesses whose rows are whole 4-element groups at
+// 4-element array offsets move 4 elements per access in the aligned kernel.
+// Reductions with fewer outputs than threads split each output's elements
+// over several threads and combine the partial results in a fixed order.
+namespace {
+
+struct TileGeom {
+  int64_t s[kTileRank];   // shape
+  int64_t st[kTileRank];  // shared-memory strides (st[3] = 1)
+  int64_t off;
+  int64_t rows() const { return s[0] * s[1] * s[2]; }
+};
+
+TileGeom tile_geom(const TileVal& v) {
+  TileGeom g;
+  for (int d = 0; d < kTileRank; ++d) {
+    g.s[d] = v.shape[d];
+    g.st[d] = d == kTileRank - 1 ? 1 : v.stride[d];
+  }
+  g.off = v.offset;
+  return g;
+}
+
+std::string float_lit(float v) {
+  uint32_t u;
+  std::memcpy(&u, &v, sizeof u);
+  char buf[40];
+  std::snprintf(buf, sizeof buf, "__int_as_float(0x%08x)", u);
+  return buf;
+}
+
+// the multi-index (i0, i1, i2) of row ``q`` (< s0 * s1 * s2) of a value of
+// shape ``s``; dims of size 1 have index 0
+std::string row_index(const int64_t (&s)[kTileRank], const char* q) {
+  std::ostringstream o;
+  const std::string Q(q);
+  const std::string i2 = s[0] == 1 && s[1] == 1 ? Q : s[2] == 1 ? "0" : Q + " % " + std::to_string(s[2]);
+  const std::string above = s[2] == 1 ? Q : "(" + Q + " / " + std::to_string(s[2]) + ")";
+  const std::string i1 = s[1] == 1 ? "0" : s[0] == 1 ? above : above + " % " + std::to_string(s[1]);
+  const std::string i0 = s[0] == 1 ? "0" : Q + " / " + std::to_string(s[2] * s[1]);
+  o << "const int i2 = " << i2 << ", i1 = " << i1 << ", i0 = " << i0 << "; (void)i0; (void)i1; (void)i2;";
+  return o.str();
+}
+
+// i0 * k0 + i1 * k1 + i2 * k2 (+ c * k3), leaving out zero strides and the
+// dims of size 1 in ``s`` (index 0)
+std::string dot(const int64_t (&k)[kTileRank], const int64_t (&s)[kTileRank], const char* c = "c", bool wide = false) {
+  std::ostringstream o;
+  const char* idx[kTileRank] = {"i0", "i1", "i2", c};
+  bool any = false;
+  for (int d = 0; d < kTileRank; ++d) {
+    if (k[d] == 0 || s[d] == 1) continue;
+    o << (any ? " + " : "") << (wide ? "static_cast<xt_i64>(" : "") << idx[d] << (wide ? ")" : "");
+    if (k[d] != 1) o << " * " << k[d];
+    any = true;
+  }
+  if (!any) o << "0";
+  return o.str();
+}
+
+// A load's or store's place in its array: the Block's first element (an
+// expression of the block ids), the array strides, and per dim the number of
+// the tile's elements inside the array when that can be less than the tile
+// (``lim``, empty when the tile always lies inside along that dim).
+struct Access {
+  std::string decl;   // declarations of run-time limits
+  std::string base;   // xt_i64 expression
+  int64_t A[kTileRank];
+  std::string lim[kTileRank];
+  bool vec;           // rows are whole 4-element groups at 4-element offsets
+  std::string inb(const char* c) const {
+    std::string s;
+    const char* idx[kTileRank] = {"i0", "i1", "i2", c};
+    for (int d = 0; d < kTileRank; ++d)
+      if (!lim[d].empty()) s += (s.empty() ? "" : " && ") + std::string(idx[d]) + " < " + lim[d];
+    return s.empty() ? "true" : s;
+  }
+};
+
+Access access_of(const dev::TileArgs& a, const TileOp& op, const TileGeom& v, int n) {
+  const int32_t* ext = a.shape[op.arg];
+  Access g;
+  int64_t run = 1;
+  for (int d = kTileRank - 1; d >= 0; --d) {
+    g.A[d] = run;
+    run *= ext[d];
+  }
+  int64_t cst = 0, mult[3] = {0, 0, 0};
+  std::ostringstream decl;
+  for (int d = 0; d < kTileRank; ++d) {
+    const int cb = op.coord_bid[d];
+    if (cb >= 0) {
+      mult[cb] += v.s[d] * g.A[d];
+      if (a.grid[cb] * v.s[d] > ext[d]) {
+        // a Block past the edge along this dim: its own limit at run time
+        decl << "    const int l" << n << "_" << d << " = static_cast<int>(max(static_cast<xt_i64>(0), min(static_cast<xt_i64>("
+             << v.s[d] << "), static_cast<xt_i64>(" << ext[d] << ") - b" << cb << " * " << v.s[d] << ")));\n";
+        g.lim[d] = "l" + std::to_string(n) + "_" + std::to_string(d);
+      }
+    } else {
+      const int64_t start = static_cast<int64_t>(op.coord[d]) * v.s[d];
+      cst += start * g.A[d];
+      const int64_t left = ext[d] - start;
+      const int64_t lim = left <= 0 ? 0 : std::min(left, v.s[d]);
+      if (lim < v.s[d]) g.lim[d] = std::to_string(lim);
+    }
+  }
+  std::ostringstream base;
+  base << "static_cast<xt_i64>(" << cst << ")";
+  for (int k = 0; k < 3; ++k)
+    if (mult[k]) base << " + b" << k << " * " << mult[k];
+  g.decl = decl.str();
+  g.base = base.str();
+  g.vec = v.s[3] % 4 == 0 && ext[3] % 4 == 0;
+  return g;
+}
+
+const char* ld1(uint8_t e) { return e == dev::kF32 ? "xt_ld1_f32" : e == dev::kBF16 ? "xt_ld1_bf16" : "xt_ld1_i8"; }
+const char* ld4(uint8_t e) { return e == dev::kF32 ? "xt_ld4_f32_kept" : e == dev::kBF16 ? "xt_ld4_bf16" : "xt_ld4_i8"; }
+const char* st1(uint8_t e) { return e == dev::kF32 ? "xt_st1_f32" : e == dev::kBF16 ? "xt_st1_bf16" : "xt_st1_i8"; }
+const char* st4(uint8_t e) { return e == dev::kF32 ? "xt_st4_f32" : e == dev::kBF16 ? "xt_st4_bf16" : "xt_st4_i8"; }
+
+// A loop of the CTA's ``th`` threads over the rows x width index space,
+// defining ``q`` and ``cv`` (the column, or 4-column group) for ``body``.
+void loop_rows(std::ostringstream& s, int th, int64_t rows, int64_t width, const std::string& body) {
+  if (th % width == 0) {
+    s << "    {\n      const int cv = t % " << width << ";\n#pragma unroll 4\n      for (int q = t / " << width << "; q < "
+      << rows << "; q += " << th / width << ") {\n" << body << "      }\n    }\n";
+  } else {
+    s << "#pragma unroll 4\n    for (int e = t; e < " << rows * width << "; e += " << th << ") {\n      const int q = e / "
+      << width << ", cv = e % " << width << ";\n" << body << "    }\n";
+  }
+}
+
+// A load: up to 8 accesses in flight per thread before their shared-memory
+// stores.  ``vec``: 4 elements per access.
+void emit_load(std::ostringstream& s, const dev::TileArgs& a, const TileOp& op, const TileGeom& v, const Access& g,
+               int th, bool vec) {
+  const int64_t width = vec ? v.s[3] / 4 : v.s[3], rows = v.rows();
+  const uint8_t e = a.elem[op.arg];
+  const char* T = vec ? "float4" : "float";
+  const char* zero = vec ? "make_float4(0.f, 0.f, 0.f, 0.f)" : "0.0f";
+  const std::string col = vec ? "const int c = 4 * cv;" : "const int c = cv;";
+  const std::string addr = "gb + " + dot(g.A, v.s, "c", true);
+  const std::string ld = std::string(vec ? ld4(e) : ld1(e)) + "(p.arr[" + std::to_string(op.arg) + "], " + addr + ")";
+  std::ostringstream st;  // the shared-memory store of v[u] at row q, column c
+  const std::string sm = "xt_sm + " + std::to_string(v.off) + " + q * " + std::to_string(v.st[2]) + " + c";
+  if (vec)
+    st << "{ float* d = " << sm << "; d[0] = v[u].x; d[1] = v[u].y; d[2] = v[u].z; d[3] = v[u].w; }";
+  else
+    st << "xt_sm[" << v.off << " + q * " << v.st[2] << " + c] = v[u];";
+  if (th % width == 0) {
+    const int64_t rs = th / width;
+    const int64_t kb = std::min<int64_t>(8, (rows + rs - 1) / rs);
+    s << "    {\n      const int cv = t % " << width << "; " << col << "\n"
+      << "      for (int q0 = t / " << width << "; q0 < " << rows << "; q0 += " << kb * rs << ") {\n"
+      << "        " << T << " v[" << kb << "];\n#pragma unroll\n"
+      << "        for (int u = 0; u < " << kb << "; ++u) {\n          const int q = q0 + u * " << rs << "; "
+      << row_index(v.s, "q") << "\n          v[u] = (q < " << rows << " && " << g.inb("c") << ") ? " << ld << " : "
+      << zero << ";\n        }\n#pragma unroll\n"
+      << "        for (int u = 0; u < " << kb << "; ++u) {\n          const int q = q0 + u * " << rs << ";\n"
+      << "          if (q < " << rows << ") " << st.str() << "\n        }\n      }\n    }\n";
+  } else {
+    const int64_t n = rows * width;
+    const int64_t kb = std::min<int64_t>(8, (n + th - 1) / th);
+    s << "    for (int e0 = t; e0 < " << n << "; e0 += " << kb * th << ") {\n"
+      << "      " << T << " v[" << kb << "];\n#pragma unroll\n"
+      << "      for (int u = 0; u < " << kb << "; ++u) {\n        const int e = e0 + u * " << th << ", q = e / " << width
+      << ", cv = e % " << width << "; " << col << " " << row_index(v.s, "q") << "\n"
+      << "        v[u] = (e < " << n << " && " << g.inb("c") << ") ? " << ld << " : " << zero << ";\n      }\n#pragma unroll\n"
+      << "      for (int u = 0; u < " << kb << "; ++u) {\n        const int e = e0 + u * " << th << ", q = e / " << width
+      << ", cv = e % " << width << "; " << col << "\n        if (e < " << n << ") " << st.str() << "\n      }\n    }\n";
+  }
+}
+
+// A store of tile ``v`` reading shared memory at ``rd_off`` through the
+// strides ``rd`` (its own slot, or a folded permute's operand).
+void emit_store(std::ostringstream& s, const dev::TileArgs& a, const TileOp& op, const TileGeom& v, int64_t rd_off,
+                const int64_t (&rd)[kTileRank], const Access& g, int th, bool vec) {
+  const uint8_t e = a.elem[op.arg];
+  const std::string arr = "p.arr[" + std::to_string(op.arg) + "]";
+  std::ostringstream b;
+  b << "        const int c = " << (vec ? "4 * cv" : "cv") << "; " << row_index(v.s, "q") << "\n";
+  b << "        if (" << g.inb("c") << ") {\n          const int r = " << rd_off << " + " << dot(rd, v.s) << ";\n";
+  if (vec)
+    b << "          " << st4(e) << "(" << arr << ", gb + " << dot(g.A, v.s, "c", true) << ", make_float4(xt_sm[r], xt_sm[r + "
+      << rd[3] << "], xt_sm[r + " << 2 * rd[3] << "], xt_sm[r + " << 3 * rd[3] << "]));\n";
+  else
+    b << "          " << st1(e) << "(" << arr << ", gb + " << dot(g.A, v.s, "c", true) << ", xt_sm[r]);\n";
+  b << "        }\n";
+  loop_rows(s, th, v.rows(), vec ? v.s[3] / 4 : v.s[3], b.str());
+}
+
+// Threads sharing one output of a reduction with ``outs`` outputs over ``n``
+// elements: a power of two that fits the CTA and leaves each thread at
+// least 4 elements, or 1.
+int64_t reduce_parts(int64_t outs, int64_t n, int th) {
+  int64_t k = 1;
+  while (outs * k * 2 <= th && k * 2 * 4 <= n) k *= 2;
+  return k;
+}
+
+// Accumulates src[j * step] for j = first, first + stride, ... < n into
+// ``acc`` (double sum, or float max with NaN propagating) with four
+// independent accumulators combined in a fixed order.
+void emit_accumulate(std::ostringstream& s, bool sum, int64_t n, int64_t step, int64_t stride, const char* first) {
+  const int64_t count = (n + stride - 1) / stride, groups = (count + 3) / 4;
+  const char* T = sum ? "double" : "float";
+  const char* init = sum ? "0.0" : "__int_as_float(0xff800000)";
+  s << "        " << T << " a0 = " << init << ", a1 = " << init << ", a2 = " << init << ", a3 = " << init << ";\n"
+    << "#pragma unroll 4\n        for (int k = 0; k < " << groups << "; ++k) {\n"
+    << "          const int j = " << first << " + k * " << 4 * stride << ";\n";
+  for (int u = 0; u < 4; ++u) {
+    const std::string j = u ? "j + " + std::to_string(u * stride) : std::string("j");
+    s << "          if (" << j << " < " << n << ") a" << u << " = "
+      << (sum ? "a" + std::to_string(u) + " + static_cast<double>(src[(" + j + ") * " + std::to_string(step) + "])"
+              : "xt_max_nan(a" + std::to_string(u) + ", src[(" + j + ") * " + std::to_string(step) + "])")
+      << ";\n";
+  }
+  s << "        }\n        const " << T << " acc = "
+    << (sum ? "(a0 + a1) + (a2 + a3)" : "xt_max_nan(xt_max_nan(a0, a1), xt_max_nan(a2, a3))") << ";\n";
+}
+
+// first float of the split reductions' partial results (8-byte aligned)
+int64_t red_offset(const dev::TileArgs& a) { return (a.smem_floats + 1) & ~1; }
+
+}  // namespace
+
+int tile_smem_floats(const dev::TileArgs& a, int th) {
+  bool reduces = false;
+  for (int o = 0; o < a.n_ops; ++o) reduces = reduces || a.ops[o].kind == kTReduce;
+  return static_cast<int>(red_offset(a)) + (reduces ? 2 * th : 0);
+}
+
+int tile_threads(const dev::TileArgs& a) {
+  int64_t most = 0;
+  for (int v = 0; v < kTileMaxVals; ++v) most = std::max<int64_t>(most, a.vals[v].numel);
+  return most <= 2048 ? 64 : most <= 4096 ? 128 : 256;
+}
+
+std::string tile_source(const dev::TileArgs& a, int th) {
+  if (a.n_ops <= 0 || a.n_ops > kTileMaxOps) fail("tile program length");
+  if (th != 64 && th != 128 && th != 256) fail("tile CTA width");
+  std::ostringstream s;
+  s << kOpMath << kHelpers;
+  s << "struct XtTileArgs { void* arr[" << kTileMaxArgs << "]; xt_i64 bid0_begin; };\n"
+       "extern __shared__ __align__(16) float xt_sm[];\n"
+       "__device__ __forceinline__ float xt_wrap_i8(float x) {\n"
+       "  return static_cast<float>(static_cast<signed char>(static_cast<int>(x)));\n}\n"
+       "// the larger of two values; a NaN operand gives NaN, as np.max\n"
+       "__device__ __forceinline__ float xt_max_nan(float r, float v) { return (v != v || v > r) ? v : r; }\n";
+  // partial results of split reductions, after the planned slots
+  s << "#define xt_red_f64 reinterpret_cast<double*>(xt_sm + " << red_offset(a) << ")\n"
+    << "#define xt_red_f32 (xt_sm + " << red_offset(a) << ")\n";
+  s << "template <bool V>\n__device__ __forceinline__ void xt_tile_body(const XtTileArgs& p) {\n"
+       "  const int t = threadIdx.x;\n"
+       "  const xt_i64 b0 = p.bid0_begin + blockIdx.x, b1 = blockIdx.y, b2 = blockIdx.z;\n"
+       "  (void)b0; (void)b1; (void)b2;\n";
+  for (int o = 0; o < a.n_ops; ++o) {
+    const TileOp& op = a.ops[o];
+    s << "  {  // op " << o << "\n";
+    switch (op.kind) {
+      case kTLoad: {
+        const TileGeom v = tile_geom(a.vals[op.dst]);
+        const Access g = access_of(a, op, v, o);
+        s << g.decl << "    const xt_i64 gb = " << g.base << ";\n";
+        if (g.vec) {
+          s << "    if (V) {\n";
+          emit_load(s, a, op, v, g, th, true);
+          s << "    } else {\n";
+        }
+        emit_load(s, a, op, v, g, th, false);
+        if (g.vec) s << "    }\n";
+        break;
+      }
+      case kTStore: {
+        const TileGeom v = tile_geom(a.vals[op.a]);
+        const Access g = access_of(a, op, v, o);
+        int64_t rd[kTileRank], rd_off;
+        if (op.code == 1) {
+          const TileGeom src = tile_geom(a.vals[op.b]);
+          rd_off = src.off;
+          for (int d = 0; d < kTileRank; ++d) rd[d] = src.st[op.perm[d]];
+        } else {
+          rd_off = v.off;
+          for (int d = 0; d < kTileRank; ++d) rd[d] = v.st[d];
+        }
+        s << g.decl << "    const xt_i64 gb = " << g.base << ";\n";
+        if (g.vec) {
+          s << "    if (V) {\n";
+          emit_store(s, a, op, v, rd_off, rd, g, th, true);
+          s << "    } else {\n";
+        }
+        emit_store(s, a, op, v, rd_off, rd, g, th, false);
+        if (g.vec) s << "    }\n";
+        break;
+      }
+      case kTConst: {
+        const TileGeom d = tile_geom(a.vals[op.dst]);
+        loop_rows(s, th, d.rows(), d.s[3],
+                  "        xt_sm[" + std::to_string(d.off) + " + q * " + std::to_string(d.st[2]) + " + cv] = " +
+                      float_lit(op.value) + ";\n");
+        break;
+      }
+      case kTUnary: {
+        const TileGeom d = tile_geom(a.vals[op.dst]), x = tile_geom(a.vals[op.a]);
+        const char* fn = unary_fn(op.code);
+        if (!fn) fail("unary opcode " + std::to_string(op.code) + " in a tile program");
+        loop_rows(s, th, d.rows(), d.s[3],
+                  "        xt_sm[" + std::to_string(d.off) + " + q * " + std::to_string(d.st[2]) + " + cv] = " + fn +
+                      "(xt_sm[" + std::to_string(x.off) + " + q * " + std::to_string(x.st[2]) + " + cv]);\n");
+        break;
+      }
+      case kTBinary: {
+        const TileGeom d = tile_geom(a.vals[op.dst]), x = tile_geom(a.vals[op.a]), y = tile_geom(a.vals[op.b]);
+        const char* fn = binary_fn(op.code);
+        if (!fn || !is_binary(op.code)) fail("binary opcode " + std::to_string(op.code) + " in a tile program");
+        // broadcast dims (size 1) contribute no stride
+        int64_t sx[kTileRank], sy[kTileRank];
+        for (int k = 0; k < kTileRank; ++k) {
+          sx[k] = x.s[k] == 1 ? 0 : x.st[k];
+          sy[k] = y.s[k] == 1 ? 0 : y.st[k];
+        }
+        std::ostringstream b;
+        b << "        const int c = cv; " << row_index(d.s, "q") << "\n"
+          << "        const float r = " << fn << "(xt_sm[" << x.off << " + " << dot(sx, d.s) << "], xt_sm[" << y.off << " + "
+          << dot(sy, d.s) << "]);\n"
+          << "        xt_sm[" << d.off << " + q * " << d.st[2] << " + c] = " << (a.vals[op.dst].i8 ? "xt_wrap_i8(r)" : "r")
+          << ";\n";
+        loop_rows(s, th, d.rows(), d.s[3], b.str());
+        break;
+      }
+      case kTReduce: {
+        const TileGeom d = tile_geom(a.vals[op.dst]), x = tile_geom(a.vals[op.a]);
+        if (op.axis >= kTileRank) fail("reduction axis");
+        const int64_t n = x.s[op.axis], step = x.st[op.axis], outs = d.rows() * d.s[3];
+        const bool sum = op.code != 0;
+        const int64_t parts = reduce_parts(outs, n, th);
+        // output o: row q, column c; the reduced dim's index is 0 in its multi-index
+        const std::string at = "        const int q = o / " + std::to_string(d.s[3]) + ", c = o % " +
+                               std::to_string(d.s[3]) + "; " + row_index(d.s, "q") + "\n" +
+                               "        const float* src = xt_sm + " + std::to_string(x.off) + " + " + dot(x.st, d.s) + ";\n";
+        const std::string put = "        xt_sm[" + std::to_string(d.off) + " + q * " + std::to_string(d.st[2]) + " + c] = ";
+        if (parts == 1) {
+          s << "#pragma unroll 2\n    for (int o = t; o < " << outs << "; o += " << th << ") {\n" << at;
+          emit_accumulate(s, sum, n, step, 1, "0");
+          s << put << (sum ? "static_cast<float>(acc);\n" : "acc;\n") << "    }\n";
+          break;
+        }
+        // ``parts`` threads per output, each over every parts-th element from
+        // its own; their partial results combine in a fixed order
+        s << "    {\n      const int o = t % " << outs << ", part = t / " << outs << ";\n"
+          << "      if (part < " << parts << ") {\n" << at;
+        emit_accumulate(s, sum, n, step, parts, "part");
+        s << "        " << (sum ? "xt_red_f64" : "xt_red_f32") << "[part * " << outs << " + o] = acc;\n      }\n"
+          << "      __syncthreads();\n"
+          << "      if (t < " << outs << ") {\n        const int o = t, q = o / " << d.s[3] << ", c = o % " << d.s[3]
+          << ";\n        " << (sum ? "double" : "float") << " acc = " << (sum ? "xt_red_f64" : "xt_red_f32") << "[o];\n"
+          << "#pragma unroll\n        for (int k = 1; k < " << parts << "; ++k) "
+          << (sum ? "acc += xt_red_f64[k * " + std::to_string(outs) + " + o];\n"
+                  : "acc = xt_max_nan(acc, xt_red_f32[k * " + std::to_string(outs) + " + o]);\n")
+          << put << (sum ? "static_cast<float>(acc);\n" : "acc;\n") << "      }\n    }\n";
+        break;
+      }
+      case kTReshape: {
+        const TileGeom d = tile_geom(a.vals[op.dst]), x = tile_geom(a.vals[op.a]);
+        std::ostringstream b;
+        b << "        const int e = q * " << d.s[3] << " + cv;\n"
+          << "        xt_sm[" << d.off << " + q * " << d.st[2] << " + cv] = xt_sm[" << x.off << " + e / " << x.s[3]
+          << " * " << x.st[2] << " + e % " << x.s[3] << "];\n";
+        loop_rows(s, th, d.rows(), d.s[3], b.str());
+        break;
+      }
+      case kTPermute: {
+        const TileGeom d = tile_geom(a.vals[op.dst]), x = tile_geom(a.vals[op.a]);
+        // dst dim k is src dim perm[k]
+        int64_t ss[kTileRank];
+        for (int k = 0; k < kTileRank; ++k) ss[k] = x.st[op.perm[k]];
+        std::ostringstream b;
+        b << "        const int c = cv; " << row_index(d.s, "q") << "\n"
+          << "        xt_sm[" << d.off << " + q * " << d.st[2] << " + c] = xt_sm[" << x.off << " + " << dot(ss, d.s) << "];\n";
+        loop_rows(s, th, d.rows(), d.s[3], b.str());
+        break;
+      }
+      default:
+        fail("tile op kind " + std::to_string(op.kind));
+    }
+    s << "  }\n";
+    if (o + 1 < a.n_ops) s << "  __syncthreads();\n";
+  }
+  s << "}\n";
+  for (int v = 1; v >= 0; --v)
+    s << "extern \"C\" __global__ void __launch_bounds__(" << th << ") " << (v ? "xt_tile_v" : "xt_tile_s")
+      << "(const XtTileArgs p) {\n  xt_pdl_launch();\n  xt_pdl_wait();\n  xt_tile_body<" << (v ? "true" : "false")
+      << ">(p);\n}\n";
+  return s.str();
+}
 }  // namespace jit
 }  // namespace xt

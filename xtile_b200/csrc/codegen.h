@@ -1,5 +1,5 @@
-// Kernels generated per Block program (ew and rows families), compiled at
-// run time with NVRTC for sm_100a.
+// Kernels generated per Block program (ew, rows and tile families),
+// compiled at run time with NVRTC for sm_100a.
 //
 // The planner turns an elementwise or row program into a short register
 // program (plan.h: Instr).  Instead of interpreting it on the GPU, the host
@@ -30,6 +30,19 @@ std::string rows_source(const dev::RowArgs& a);
 // run the shared-memory interpreter).
 bool rows_fit(const dev::RowArgs& a);
 
+// CUDA source of the tile-program kernels for ``a`` run by ``threads``
+// threads per CTA: ``xt_tile_v`` (accesses whose rows are whole 4-element
+// groups move 4 elements at a time; every array 16-byte aligned) and
+// ``xt_tile_s`` (element accesses).
+std::string tile_source(const dev::TileArgs& a, int threads);
+// The CTA width for a tile program: 64 threads when every tile holds at
+// most 2048 elements, 128 for at most 4096, else 256.
+int tile_threads(const dev::TileArgs& a);
+// Shared memory (floats) of the tile kernel for ``a`` at ``threads``
+// threads: the planned slots, then one double per thread for the partial
+// results of reductions when the program reduces.
+int tile_smem_floats(const dev::TileArgs& a, int threads);
+
 // Compiles ``source`` with NVRTC for sm_100a; returns the cubin.  Throws
 // xt::Error (kCudaError) with NVRTC's log on failure or when NVRTC cannot be
 // loaded.  Needs no GPU.
@@ -39,6 +52,7 @@ std::string compile(const std::string& source);
 // and loading them on first use on the current device).
 cudaError_t launch_ew(const dev::EwArgs& a, cudaStream_t stream);
 cudaError_t launch_rows(const dev::RowArgs& a, cudaStream_t stream);
+cudaError_t launch_tile(const dev::TileArgs& a, cudaStream_t stream);
 
 constexpr int kEwVec = 2;          // float4 groups per thread and pass in xt_ew_v
 constexpr int kEwThreads = 256;

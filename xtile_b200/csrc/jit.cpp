@@ -1,11 +1,11 @@
-// Run-time compilation and launch of the generated ew / rows kernels
+// Run-time compilation and launch of the generated ew / rows / tile kernels
 // (codegen.h): NVRTC, loaded with dlopen from the CUDA toolkit, compiles a
 // program's source to an sm_100a cubin; the driver API (resolved through the
 // runtime's entry-point query, so the library needs no link against
 // libcuda) loads it once per device and launches it with programmatic
 // dependent launch, like every other kernel of this library.
 //
-// A missing NVRTC is an error at the first launch of an ew or rows program
+// A missing NVRTC is an error at the first launch of a generated program
 // (with the reason); there is no fallback.
 #include <cuda.h>
 #include <dlfcn.h>
@@ -79,6 +79,7 @@ typedef CUresult (*ModuleLoadDataFn)(CUmodule*, const void*);
 typedef CUresult (*ModuleGetFunctionFn)(CUfunction*, CUmodule, const char*);
 typedef CUresult (*LaunchKernelExFn)(const CUlaunchConfig*, CUfunction, void**, void**);
 typedef CUresult (*GetErrorStringFn)(CUresult, const char**);
+typedef CUresult (*FuncSetAttributeFn)(CUfunction, CUfunction_attribute, int);
 
 template <class F>
 F driver_fn(const char* name) {
@@ -94,6 +95,7 @@ struct Driver {
   ModuleGetFunctionFn get = driver_fn<ModuleGetFunctionFn>("cuModuleGetFunction");
   LaunchKernelExFn launch = driver_fn<LaunchKernelExFn>("cuLaunchKernelEx");
   GetErrorStringFn err = driver_fn<GetErrorStringFn>("cuGetErrorString");
+  FuncSetAttributeFn set_attr = driver_fn<FuncSetAttributeFn>("cuFuncSetAttribute");
 };
 
 const Driver& driver() {
@@ -128,9 +130,11 @@ std::string key_of(char family, const Instr* code, int n_code, const std::string
 }
 
 // Kernel ``name`` of the program (``key``; ``make`` writes its source) on
-// the current device, compiled and loaded on first use.
+// the current device, compiled and loaded on first use.  ``smem``: the
+// dynamic shared memory its launches use, opted into above 48 KiB when the
+// function is loaded.
 template <class Make>
-CUfunction function(const std::string& key, Make make, const char* name) {
+CUfunction function(const std::string& key, Make make, const char* name, int smem = 0) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) throw Error(kCudaError, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
@@ -159,20 +163,26 @@ CUfunction function(const std::string& key, Make make, const char* name) {
   CUfunction fn = nullptr;
   CUresult r = d.get(&fn, m->second, name);
   if (r != CUDA_SUCCESS) throw Error(kCudaError, std::string("generated kernel ") + name + ": " + cu_error(r));
+  if (smem > 48 * 1024) {
+    if (!d.set_attr) throw Error(kCudaError, "the CUDA driver lacks cuFuncSetAttribute");
+    r = d.set_attr(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, smem);
+    if (r != CUDA_SUCCESS) throw Error(kCudaError, std::string("generated kernel ") + name + " shared memory: " + cu_error(r));
+  }
   p.fns[{dev, name}] = fn;
   return fn;
 }
 
-cudaError_t launch(CUfunction fn, unsigned grid, unsigned block, cudaStream_t stream, void* params) {
+cudaError_t launch(CUfunction fn, dim3 grid, unsigned block, cudaStream_t stream, void* params, unsigned smem = 0) {
   CUlaunchAttribute attr[1];
   attr[0].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
   attr[0].value.programmaticStreamSerializationAllowed = 1;
   CUlaunchConfig cfg{};
-  cfg.gridDimX = grid;
-  cfg.gridDimY = cfg.gridDimZ = 1;
+  cfg.gridDimX = grid.x;
+  cfg.gridDimY = grid.y;
+  cfg.gridDimZ = grid.z;
   cfg.blockDimX = block;
   cfg.blockDimY = cfg.blockDimZ = 1;
-  cfg.sharedMemBytes = 0;
+  cfg.sharedMemBytes = smem;
   cfg.hStream = reinterpret_cast<CUstream>(stream);
   cfg.attrs = attr;
   cfg.numAttrs = 1;
@@ -200,6 +210,45 @@ struct RowParams {
   float* out[kMaxSlots];
   int64_t row_begin, row_end;
 };
+struct TileParams {
+  void* arr[kTileMaxArgs];
+  int64_t bid0_begin;
+};
+
+// Everything a tile program's source depends on, field by field (its ops,
+// values, array element types and shapes, grid and CTA width).
+std::string tile_key(const dev::TileArgs& a, int th) {
+  std::string k(1, 't');
+  auto put = [&](int64_t v) { k.append(reinterpret_cast<const char*>(&v), sizeof v); };
+  put(th);
+  put(a.n_ops);
+  put(a.smem_floats);
+  for (int i = 0; i < 3; ++i) put(a.grid[i]);
+  for (int i = 0; i < kTileMaxArgs; ++i) {
+    put(a.elem[i]);
+    for (int d = 0; d < kTileRank; ++d) put(a.shape[i][d]);
+  }
+  for (int v = 0; v < kTileMaxVals; ++v) {
+    const TileVal& t = a.vals[v];
+    for (int d = 0; d < kTileRank; ++d) put((static_cast<int64_t>(t.shape[d]) << 32) | static_cast<uint32_t>(t.stride[d]));
+    put((static_cast<int64_t>(t.offset) << 32) | static_cast<uint32_t>(t.numel));
+    put(t.i8);
+  }
+  for (int o = 0; o < a.n_ops; ++o) {
+    const TileOp& t = a.ops[o];
+    const int64_t fields[7] = {t.kind, t.code, t.dst, t.a, t.b, t.arg, t.axis};
+    int64_t packed = 0;
+    for (int f = 0; f < 7; ++f) packed |= fields[f] << (8 * f);
+    put(packed);
+    for (int d = 0; d < kTileRank; ++d)
+      put(static_cast<int64_t>(t.perm[d]) | (static_cast<int64_t>(t.coord_bid[d]) & 0xff) << 8 |
+          static_cast<int64_t>(t.coord[d]) << 16);
+    uint32_t bits;
+    std::memcpy(&bits, &t.value, sizeof bits);
+    put(bits);
+  }
+  return k;
+}
 
 }  // namespace
 
@@ -257,10 +306,10 @@ cudaError_t launch_ew(const dev::EwArgs& a, cudaStream_t stream) {
   if (v4) {
     const int64_t groups = n / (4 * kEwVec);
     CUfunction f = function(key, [&] { return ew_source(a); }, "xt_ew_v");
-    return launch(f, grid_of(groups > 0 ? groups : 1, kEwThreads), kEwThreads, stream, &p);
+    return launch(f, dim3(grid_of(groups > 0 ? groups : 1, kEwThreads)), kEwThreads, stream, &p);
   }
   CUfunction f = function(key, [&] { return ew_source(a); }, "xt_ew_s");
-  return launch(f, grid_of(n, kEwThreads), kEwThreads, stream, &p);
+  return launch(f, dim3(grid_of(n, kEwThreads)), kEwThreads, stream, &p);
 }
 
 cudaError_t launch_rows(const dev::RowArgs& a, cudaStream_t stream) {
@@ -286,7 +335,25 @@ cudaError_t launch_rows(const dev::RowArgs& a, cudaStream_t stream) {
   p.row_begin = a.row_begin;
   p.row_end = a.row_end;
   CUfunction f = function(key, [&] { return rows_source(a); }, vec ? "xt_rows_v" : "xt_rows_s");
-  return launch(f, grid_of(rows, kRowsPerCta), 32 * kRowsPerCta, stream, &p);
+  return launch(f, dim3(grid_of(rows, kRowsPerCta)), 32 * kRowsPerCta, stream, &p);
+}
+
+cudaError_t launch_tile(const dev::TileArgs& a, cudaStream_t stream) {
+  const int64_t gx = a.bid0_end - a.bid0_begin;
+  if (gx <= 0) return cudaSuccess;
+  if (gx > 0x7fffffff || a.grid[1] > 65535 || a.grid[2] > 65535) return cudaErrorInvalidValue;
+  const int th = tile_threads(a);
+  const std::string key = tile_key(a, th);
+  // the aligned kernel: every array 16-byte aligned
+  bool aligned = true;
+  for (int i = 0; i < kTileMaxArgs; ++i) aligned = aligned && (reinterpret_cast<uintptr_t>(a.arr[i]) & 15) == 0;
+  TileParams p{};
+  for (int i = 0; i < kTileMaxArgs; ++i) p.arr[i] = a.arr[i];
+  p.bid0_begin = a.bid0_begin;
+  const int smem = tile_smem_floats(a, th) * static_cast<int>(sizeof(float));
+  CUfunction f = function(key, [&] { return tile_source(a, th); }, aligned ? "xt_tile_v" : "xt_tile_s", smem);
+  return launch(f, dim3(static_cast<unsigned>(gx), static_cast<unsigned>(a.grid[1]), static_cast<unsigned>(a.grid[2])),
+                th, stream, &p, static_cast<unsigned>(smem));
 }
 
 }  // namespace jit

@@ -51,7 +51,6 @@ struct TileArgs {
   TileOp ops[kTileMaxOps];
   int n_ops;
   int32_t smem_floats;
-  uint8_t rows;                  // every tile is R x C with C dividing the CTA width
   int64_t grid[3];
   int64_t bid0_begin, bid0_end;  // Blocks [bid0_begin, bid0_end) along xt.bid(0)
 };

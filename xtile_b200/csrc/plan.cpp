@@ -496,9 +496,6 @@ class Classifier {
         if (grid_[k] > 1 && !used.count(k))
           unsupported("Blocks along grid axis " + std::to_string(k) + " would store the same tile");
     }
-    p.rows = true;
-    for (const TileVal& v : p.vals)
-      p.rows = p.rows && v.shape[0] == 1 && v.shape[1] == 1 && 256 % v.shape[3] == 0;
     return p;
   }
 

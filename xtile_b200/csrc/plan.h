@@ -146,7 +146,6 @@ struct TilePlan {
   std::vector<TileVal> vals;
   std::vector<TileOp> ops;
   int32_t smem_floats = 0;
-  bool rows = false;                     // every tile is 1 x 1 x R x C with C dividing 256
 };
 
 struct Plan {
