@@ -14,9 +14,11 @@ Workloads are the BASELINE configurations (synthetic, seeded inputs):
                   (--gather nccl: an NCCL gather; the default workload)
   transpose, silu, row_center, row_bias
                   not BASELINE configurations: the data-movement kernel and the
-                  ew and rows interpreters on f32 programs over 128 MiB
+                  generated ew and rows kernels on f32 programs over 128 MiB
   matmul_i8       not a BASELINE configuration: the reference's int8
                   kernels/matmul.py program (scale, bias, int8 out) at 8192^3
+  col_sums        not a BASELINE configuration: a generated tile kernel
+                  (column sums of 64 x 32 tiles of a 128 MiB f32 array)
 
 A step is one launch of the workload's Block program over its whole Grid
 (for sharded_matmul: every rank's share plus the gather).  ``value`` is the
@@ -80,6 +82,7 @@ NCU_TRAFFIC_BYTES: dict[str, float] = {
     "matmul_i8": 215_210_496 + 55_281_408,
     "silu": 134_240_512 + 84_709_376,
     "row_center": 134_223_360 + 78_821_120,
+    "col_sums": 134_223_360 + 4_445_056,
 }
 
 
@@ -226,9 +229,9 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
                     config={"workload": name, "M": M, "N": N, "K": K, "block_tile": [64, 64], "k_step": K,
                             "grid": [M // 64, N // 64, 1], "epilogue": "t * scale + bias, int8 (round half even, saturate)"})
     if name in ("silu", "row_center", "row_bias"):
-        # not BASELINE configurations: the ew and rows program interpreters
+        # not BASELINE configurations: the generated ew and rows kernels
         # on HBM-bound f32 programs over 128 MiB arrays (row_bias: a
-        # broadcast row, which the ew interpreter reads as element i mod C)
+        # broadcast row, which the ew kernel reads as element i mod C)
         R, C = (32768, 1024) if name == "row_center" else (16384, 2048)
         x = torch.randn(R, C, generator=g(6))
         F = xt.float32

@@ -129,19 +129,26 @@ RANK4_PERMUTE = """func.func @r(%x: memref<4x6x10x12xf32>, %y: memref<4x10x6x12x
 }"""
 
 
-@pytest.mark.parametrize("case", ["col_stats", "col_vector_ops", "i8_wrap", "row_stats_tiles", "rank4"])
+@pytest.mark.parametrize("case", ["col_stats", "col_vector_ops", "wide", "i8_wrap", "row_stats_tiles", "rank4"])
 def test_tile_programs_compile(case):
     F, I8 = xt.float32, xt.int8
     if case == "col_stats":
-        # column sums and maxima: 64 x 32 tiles, 64-thread CTAs, float4
-        # loads, each column's 64 rows split over two threads
+        # column sums and maxima: 64 x 32 tiles, 128-thread CTAs, float4
+        # loads into unpadded rows, each column's 64 rows split over four
+        # threads
         m = xt.convert(tile_cases.col_stats, args=(A((16384, 2048), F), A((256, 2048), F), A((256, 2048), F), 64, 32),
                        grid=(256, 64, 1))
-        want = ("xt_ld4_f32_kept", "xt_st4_f32", "static_cast<double>", "__launch_bounds__(64)", "xt_red_f64[part")
+        want = ("xt_ld4_f32_kept", "xt_st4_f32", "static_cast<double>", "__launch_bounds__(128)", "xt_red_f64[part",
+                "*reinterpret_cast<float4*>(xt_sm + 0 + q * 32 + c) = v[u]")
     elif case == "col_vector_ops":
         m = xt.convert(tile_cases.col_vector_ops, args=(A((96, 1024), F), A((96, 1), F), A((96, 1024), F), 8, 512),
                        grid=(12, 2, 1))
         want = ("xt_sigmoid", "__launch_bounds__(128)")  # 4096-element tiles
+    elif case == "wide":
+        # 8192-element tiles: 256-thread CTAs
+        m = xt.convert(tile_cases.col_vector_ops, args=(A((96, 1024), F), A((96, 1), F), A((96, 1024), F), 16, 512),
+                       grid=(6, 2, 1))
+        want = ("__launch_bounds__(256)",)
     elif case == "i8_wrap":
         m = xt.convert(tile_cases.i8_wrap, args=(A((64, 96), I8), A((1, 96), I8), A((64, 96), I8), 32, 48),
                        grid=(2, 2, 1))

@@ -5,8 +5,9 @@ applies 2-5 random ops (unary sigmoid / tanh / sin / cos / exp of a bounded
 value, binary + - * between tiles, with the broadcast row, or with a per-row
 sum or max reduced from a tile) and stores one or two results.  Depending on
 the ops and tiles the planner picks the ew, rows or tile family, so one set
-of seeds covers the three program interpreters: register slots in shared
-memory, in-place slot reuse, broadcast rows, reductions and partial tiles.
+of seeds covers the three kinds of generated kernel: register programs,
+shared-memory slots with in-place reuse, broadcast rows, reductions and
+partial tiles.
 A program beyond every family's limits (live rows, tile count) is refused by
 the planner and its seed skipped.  Tolerance: |gpu - ref| <= 1e-4 |ref| + 1e-4 (transcendentals within a few
 ulp of numpy's float64 ones, sums in another order); a wrong index, slot or

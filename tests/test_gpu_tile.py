@@ -115,7 +115,7 @@ def row_vector_ops(x, v, y, tm, tn):
 def test_row_vector_broadcast_runs_elementwise(rows, cols, tm):
     # a [1, C] row broadcast over the rows is an elementwise program (the row
     # is element i mod C of the flat map); 37 columns take the one-element
-    # interpreter, 64 and 512 the vectorised one; a bid0 split matches
+    # kernel, 64 and 512 the vectorised one; a bid0 split matches
     x = torch.randn(rows, cols, generator=gen(6))
     v = torch.randn(1, cols, generator=gen(7))
     y = torch.empty(rows, cols, device=DEV)
@@ -142,10 +142,10 @@ def col_vector_ops(x, c, y, tm, tn):
 @pytest.mark.parametrize("rows,cols,tm,tn", [(128, 128, 32, 64), (128, 256, 32, 128), (64, 512, 16, 256),
                                              (96, 1024, 8, 512)])
 def test_column_vector_broadcast_tile_cta_widths(rows, cols, tm, tn):
-    # a (tm, 1) column broadcast over tiles narrower than a row runs in the
-    # tile interpreter; CTA widths by tile: 32x64 (2048 elements) 64 threads,
-    # 32x128 128 threads, 16x256 256 threads (row-only variant); 8x512 runs
-    # the general variant with 128 threads
+    # a (tm, 1) column broadcast over tiles narrower than a row is a tile
+    # program; its generated kernel runs 128 threads for the 2048- and
+    # 4096-element tiles (32x64, 32x128, 16x256, 8x512: one or several rows
+    # per warp)
     x = torch.randn(rows, cols, generator=gen(6))
     c = torch.randn(rows, 1, generator=gen(7))
     y = torch.empty(rows, cols, device=DEV)
@@ -209,8 +209,8 @@ def test_int8_arithmetic_wraps_bit_exact():
     assert np.array_equal(host(y), ref)
 
 
-def test_rank4_permute_general_walker():
-    # rank-4 tiles with non-unit leading dims take the general (walker) path
+def test_rank4_permute_leading_dims():
+    # rank-4 tiles with non-unit leading dims: rows unravel into three indices
     text = """func.func @r(%x: memref<4x6x10x12xf32>, %y: memref<4x10x6x12xf32>) attributes {xt.grid = array<i32: 2, 1, 2>} {
   %bid:3 = xt.get_tile_block_id : i32, i32, i32
   %zero = arith.constant 0 : i32
@@ -313,7 +313,7 @@ def test_large_grid_axis0_reductions():
 
 
 def test_large_grid_rank4_permute_general_path():
-    # rank-4 tiles with a non-unit leading dim (general walker path) on a grid
+    # rank-4 tiles with a non-unit leading dim on a grid
     # of (40, 1, 80) = 3200 Blocks
     text = """func.func @r(%x: memref<80x6x320x12xf32>, %y: memref<80x320x6x12xf32>) attributes {xt.grid = array<i32: 40, 1, 80>} {
   %bid:3 = xt.get_tile_block_id : i32, i32, i32

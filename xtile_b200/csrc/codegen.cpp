@@ -1,12 +1,14 @@
-// Source generation for the per-program ew and rows kernels (codegen.h).
+// Source generation for the per-program ew, rows and tile kernels
+// (codegen.h).
 //
-// The generated text is the register program of plan.h written out: every
-// program register becomes a local variable (an array of float4 groups in
-// the vector kernels), every instruction one statement applying the
-// op_math.cuh function, whose text is embedded at the top of each source.
-// The semantics are therefore those of the compiled interpreters, op for op;
-// what changes is that nothing is decoded or dispatched per element and the
-// values stay in registers.
+// For ew and rows programs the generated text is the register program of
+// plan.h written out: every program register becomes a local variable (an
+// array of float4 groups in the vector kernels), every instruction one
+// statement applying the op_math.cuh function, whose text is embedded at the
+// top of each source.  The semantics are those of the register program, op
+// for op; nothing is decoded or dispatched per element and the values stay
+// in registers.  Tile programs are written out op by op over shared-memory
+// slots (below).
 #include "codegen.h"
 
 #include <algorithm>
@@ -14,6 +16,7 @@
 #include <cstring>
 #include <set>
 #include <sstream>
+#include <vector>
 
 #include "ir.h"
 
@@ -345,8 +348,7 @@ std::string rows_source(const dev::RowArgs& a) {
 
 
 // ---------------------------------------------------------------------------
-// Tile programs.  The generated kernel keeps the interpreter's model -- one
-// CTA per Block, every tile value in its planned shared-memory slot (f32,
+// Tile programs.  One CTA per Block, every tile value in its planned shared-memory slot (f32,
 // row-major, rows padded to an odd pitch), the ops in program order with a
 // CTA barrier between them -- but every shape, pitch, slot offset, array
 // stride, tile coordinate and edge limit is a constant of the source.  A
@@ -367,14 +369,50 @@ struct TileGeom {
   int64_t rows() const { return s[0] * s[1] * s[2]; }
 };
 
-TileGeom tile_geom(const TileVal& v) {
+// ``compact``: rows at a pitch of exactly one row (the slot's planned pitch
+// is one float longer for even rows)
+TileGeom tile_geom(const TileVal& v, bool compact) {
   TileGeom g;
-  for (int d = 0; d < kTileRank; ++d) {
-    g.s[d] = v.shape[d];
-    g.st[d] = d == kTileRank - 1 ? 1 : v.stride[d];
+  for (int d = 0; d < kTileRank; ++d) g.s[d] = v.shape[d];
+  if (compact) {
+    g.st[3] = 1;
+    g.st[2] = g.s[3];
+    g.st[1] = g.s[2] * g.st[2];
+    g.st[0] = g.s[1] * g.st[1];
+  } else {
+    for (int d = 0; d < kTileRank; ++d) g.st[d] = d == kTileRank - 1 ? 1 : v.stride[d];
   }
   g.off = v.offset;
   return g;
+}
+
+// Which values keep their rows at a pitch of one row.  The planner pads
+// even rows to an odd pitch so that a warp walking down a column hits 32
+// banks; values that no op walks down a column (the operands of permutes,
+// of stores that read through a permutation and of reductions along the
+// last dim) drop the pad: a warp's row-major accesses then touch
+// consecutive words, and 4-element groups are 16-byte aligned.  A value
+// computed in place of its operand keeps the operand's pitch.
+std::vector<bool> compact_values(const dev::TileArgs& a) {
+  std::vector<bool> c(kTileMaxVals, true);
+  for (int o = 0; o < a.n_ops; ++o) {
+    const TileOp& op = a.ops[o];
+    if (op.kind == kTPermute || (op.kind == kTReduce && op.axis == kTileRank - 1)) c[op.a] = false;
+    if (op.kind == kTStore && op.code == 1) c[op.b] = false;
+  }
+  for (bool changed = true; changed;) {
+    changed = false;
+    for (int o = 0; o < a.n_ops; ++o) {
+      const TileOp& op = a.ops[o];
+      if (op.kind != kTUnary && op.kind != kTBinary) continue;
+      for (int x : {static_cast<int>(op.a), op.kind == kTBinary ? static_cast<int>(op.b) : -1}) {
+        if (x < 0 || a.vals[x].offset != a.vals[op.dst].offset || c[x] == c[op.dst]) continue;
+        c[x] = c[op.dst] = false;
+        changed = true;
+      }
+    }
+  }
+  return c;
 }
 
 std::string float_lit(float v) {
@@ -501,7 +539,9 @@ void emit_load(std::ostringstream& s, const dev::TileArgs& a, const TileOp& op, 
   const std::string ld = std::string(vec ? ld4(e) : ld1(e)) + "(p.arr[" + std::to_string(op.arg) + "], " + addr + ")";
   std::ostringstream st;  // the shared-memory store of v[u] at row q, column c
   const std::string sm = "xt_sm + " + std::to_string(v.off) + " + q * " + std::to_string(v.st[2]) + " + c";
-  if (vec)
+  if (vec && v.st[2] % 4 == 0 && v.off % 4 == 0)
+    st << "*reinterpret_cast<float4*>(" << sm << ") = v[u];";
+  else if (vec)
     st << "{ float* d = " << sm << "; d[0] = v[u].x; d[1] = v[u].y; d[2] = v[u].z; d[3] = v[u].w; }";
   else
     st << "xt_sm[" << v.off << " + q * " << v.st[2] << " + c] = v[u];";
@@ -538,7 +578,12 @@ void emit_store(std::ostringstream& s, const dev::TileArgs& a, const TileOp& op,
   std::ostringstream b;
   b << "        const int c = " << (vec ? "4 * cv" : "cv") << "; " << row_index(v.s, "q") << "\n";
   b << "        if (" << g.inb("c") << ") {\n          const int r = " << rd_off << " + " << dot(rd, v.s) << ";\n";
-  if (vec)
+  bool aligned4 = rd[3] == 1 && rd_off % 4 == 0;
+  for (int d = 0; d < kTileRank - 1; ++d) aligned4 = aligned4 && (v.s[d] == 1 || rd[d] % 4 == 0);
+  if (vec && aligned4)
+    b << "          " << st4(e) << "(" << arr << ", gb + " << dot(g.A, v.s, "c", true)
+      << ", *reinterpret_cast<const float4*>(xt_sm + r));\n";
+  else if (vec)
     b << "          " << st4(e) << "(" << arr << ", gb + " << dot(g.A, v.s, "c", true) << ", make_float4(xt_sm[r], xt_sm[r + "
       << rd[3] << "], xt_sm[r + " << 2 * rd[3] << "], xt_sm[r + " << 3 * rd[3] << "]));\n";
   else
@@ -591,7 +636,7 @@ int tile_smem_floats(const dev::TileArgs& a, int th) {
 int tile_threads(const dev::TileArgs& a) {
   int64_t most = 0;
   for (int v = 0; v < kTileMaxVals; ++v) most = std::max<int64_t>(most, a.vals[v].numel);
-  return most <= 2048 ? 64 : most <= 4096 ? 128 : 256;
+  return most <= 4096 ? 128 : 256;
 }
 
 std::string tile_source(const dev::TileArgs& a, int th) {
@@ -608,6 +653,11 @@ std::string tile_source(const dev::TileArgs& a, int th) {
   // partial results of split reductions, after the planned slots
   s << "#define xt_red_f64 reinterpret_cast<double*>(xt_sm + " << red_offset(a) << ")\n"
     << "#define xt_red_f32 (xt_sm + " << red_offset(a) << ")\n";
+  const std::vector<bool> compact = compact_values(a);
+  auto tile_geom = [&](const TileVal& v) {
+    const int idx = static_cast<int>(&v - a.vals);
+    return xt::jit::tile_geom(v, compact[idx]);
+  };
   s << "template <bool V>\n__device__ __forceinline__ void xt_tile_body(const XtTileArgs& p) {\n"
        "  const int t = threadIdx.x;\n"
        "  const xt_i64 b0 = p.bid0_begin + blockIdx.x, b1 = blockIdx.y, b2 = blockIdx.z;\n"

@@ -35,8 +35,9 @@ bool rows_fit(const dev::RowArgs& a);
 // groups move 4 elements at a time; every array 16-byte aligned) and
 // ``xt_tile_s`` (element accesses).
 std::string tile_source(const dev::TileArgs& a, int threads);
-// The CTA width for a tile program: 64 threads when every tile holds at
-// most 2048 elements, 128 for at most 4096, else 256.
+// The CTA width for a tile program: 128 threads when every tile holds at
+// most 4096 elements, else 256 (column sums of 64 x 32 tiles: 4391 GB/s with
+// 64 threads, 5979 with 128, 5124 with 256).
 int tile_threads(const dev::TileArgs& a);
 // Shared memory (floats) of the tile kernel for ``a`` at ``threads``
 // threads: the planned slots, then one double per thread for the partial

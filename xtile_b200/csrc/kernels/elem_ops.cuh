@@ -1,8 +1,7 @@
-// Scalar element operations of the compiled interpreter kernels (tile, and
-// the ew / rows forms compiled ahead of time): the xt unary and binary ops on
-// f32 values, dispatched on an opcode, and element loads/stores of f32, bf16
-// and int8 arrays.  The arithmetic itself is op_math.cuh's, shared with the
-// kernels generated per program at run time.
+// Scalar element operations of the compiled rows interpreter (the rows
+// programs too wide for the generated kernels): the xt unary and binary ops
+// on f32 values, dispatched on an opcode.  The arithmetic itself is
+// op_math.cuh's, shared with the kernels generated per program at run time.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -37,18 +36,6 @@ __device__ __forceinline__ float binary_op(uint8_t op, float a, float b) {
     case kMul: case kBcastMul: return xt_mul(a, b);
     default: return a;
   }
-}
-
-__device__ __forceinline__ float load_elem(const void* p, uint8_t e, int64_t i) {
-  if (e == kF32) return __ldg(static_cast<const float*>(p) + i);
-  if (e == kBF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
-  return static_cast<float>(static_cast<const int8_t*>(p)[i]);
-}
-
-__device__ __forceinline__ void store_elem(void* p, uint8_t e, int64_t i, float v) {
-  if (e == kF32) static_cast<float*>(p)[i] = v;
-  else if (e == kBF16) static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
-  else static_cast<int8_t*>(p)[i] = static_cast<int8_t>(static_cast<int>(v));
 }
 
 }  // namespace dev
