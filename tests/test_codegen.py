@@ -11,7 +11,7 @@ checked on a GPU against the oracle (``tests/test_gpu_random_programs.py``,
 import pytest
 
 import xtile as xt
-from tests.test_gpu_random_programs import random_program
+from tests.test_gpu_random_programs import random_program, tile_program_module
 from xtile_b200._native import native
 
 A = xt.Array
@@ -167,4 +167,29 @@ def test_tile_programs_compile(case):
     for w in want:
         assert w in src, w
     assert "switch" not in src.split("xt_warp_sum")[-1]
+    assert compiles(m)
+
+
+@pytest.mark.parametrize("seed", range(48))
+def test_random_tile_program_compiles(seed):
+    m, _, _ = tile_program_module(seed)
+    try:
+        fam = m.plan()["family"]
+    except RuntimeError:
+        pytest.skip("beyond every family's limits")
+    if fam not in ("ew", "rows", "tile"):
+        pytest.skip(f"runs the compiled {fam} kernel")
+    assert compiles(m)
+
+
+def test_elementwise_ops_share_one_pass():
+    # load, load, (t * c - c), sigmoid, store: the three elementwise ops run
+    # as one pass with their intermediate results in registers; the two
+    # loads need no barrier between them: two barriers in all
+    F = xt.float32
+    m = xt.convert(tile_cases.col_vector_ops, args=(A((16384, 2048), F), A((16384, 1), F), A((16384, 2048), F), 32, 64),
+                   grid=(512, 32, 1))
+    body = generated(m).split("template <bool V>")[1]
+    assert "ops 2-4: one pass" in body
+    assert body.count("__syncthreads") == 2
     assert compiles(m)

@@ -12,6 +12,12 @@ A program beyond every family's limits (live rows, tile count) is refused by
 the planner and its seed skipped.  Tolerance: |gpu - ref| <= 1e-4 |ref| + 1e-4 (transcendentals within a few
 ulp of numpy's float64 ones, sums in another order); a wrong index, slot or
 lane would be off by O(1).
+
+A second generator (``random_tile_program``) aims at the tile family:
+column and row broadcasts, reductions along either axis combined back by
+broadcasting, and tiles ragged along the rows; it covers the generated tile
+kernel's single-pass runs of elementwise ops, its reductions split over
+threads and its slot reuse.
 """
 import numpy as np
 import pytest
@@ -99,6 +105,95 @@ def test_random_program_matches_oracle(seed):
     arrays = [x.numpy(), y.numpy(), v.numpy(), refs[0], refs[1]]
     xt_oracle.run(m.source_text, arrays)
     for got, ref in ((out, arrays[3]), (out2, arrays[4])):
+        got = got.cpu().numpy()
+        assert np.all(np.isfinite(got) == np.isfinite(ref)), m.plan()["family"]
+        ok = np.isfinite(ref)
+        assert np.all(np.abs(got[ok] - ref[ok]) <= 1e-4 * np.abs(ref[ok]) + 1e-4), m.plan()["family"]
+    assert xt.device_error() == 0
+
+
+def random_tile_program(seed):
+    """A seeded Block program for the tile family: (tm, tn) tiles of [R, C]
+    arrays (ragged along the rows for R = 40), 2-6 ops among unary ops,
+    binaries between the last two values, a (tm, 1) column or (1, tn) row
+    broadcast, and reductions along axis 0 or 1 combined back by
+    broadcasting (2-4 ops: a program holds at most 16 tiles); one or two
+    stores."""
+    rng = np.random.default_rng(1000 + seed)
+    R, C = [(64, 64), (96, 128), (128, 256), (40, 72)][rng.integers(4)]
+    tn = [C, C // 2, C // 4][rng.integers(3)]
+    tm = [8, 16, 32][rng.integers(3)]
+    ops = []
+    for _ in range(int(rng.integers(2, 5))):
+        r = rng.random()
+        if r < 0.25:
+            ops.append(("unary", int(rng.integers(len(UNARY)))))
+        elif r < 0.45:
+            ops.append(("binary", int(rng.integers(3))))
+        elif r < 0.6:
+            ops.append(("col", int(rng.integers(3))))
+        elif r < 0.7:
+            ops.append(("row", int(rng.integers(3))))
+        else:
+            ops.append(("reduce", int(rng.integers(2)), int(rng.integers(2)), int(rng.integers(3))))
+    two_stores = bool(rng.random() < 0.5)
+
+    @xt.kernel
+    def prog(x, y, v, col, out, out2, tm, tn):
+        i, j = xt.bid(0), xt.bid(1)
+        vals = [xt.load(x, index=(i, j), shape=(tm, tn)), xt.load(y, index=(i, j), shape=(tm, tn))]
+        c = r = None  # the column and row, loaded once
+        for op in ops:
+            t = vals[-1]
+            if op[0] == "unary":
+                vals.append(UNARY[op[1]](t))
+            elif op[0] == "binary":
+                o = vals[-2]
+                vals.append([t + o, t - o, t * o][op[1]])
+            elif op[0] == "col":
+                if c is None:
+                    c = xt.load(col, index=(i, 0), shape=(tm, 1))
+                vals.append([t + c, t - c, t * c][op[1]])
+            elif op[0] == "row":
+                if r is None:
+                    r = xt.load(v, index=(0, j), shape=(1, tn))
+                vals.append([t + r, t - r, t * r][op[1]])
+            else:
+                _, axis, fn, comb = op
+                s = xt.sum(t, axis=axis) if fn == 0 else xt.max(t, axis=axis)
+                vals.append([t + s, t - s, t * s][comb])
+        xt.store(out, index=(i, j), tile=vals[-1])
+        xt.store(out2, index=(i, j), tile=vals[-2] if two_stores else vals[0])
+
+    return prog, R, C, tm, tn
+
+
+def tile_program_module(seed):
+    prog, R, C, tm, tn = random_tile_program(seed)
+    A, F = xt.Array, xt.float32
+    m = xt.convert(prog, args=(A((R, C), F), A((R, C), F), A((1, C), F), A((R, 1), F), A((R, C), F), A((R, C), F),
+                               tm, tn), grid=(-(-R // tm), C // tn, 1), double_buffering=True)
+    return m, R, C
+
+
+@pytest.mark.parametrize("seed", range(48))
+def test_random_tile_program_matches_oracle(seed):
+    m, R, C = tile_program_module(seed)
+    try:
+        m.plan()
+    except RuntimeError as e:  # beyond every family's limits: refused loudly
+        pytest.skip(str(e)[:120])
+    g = torch.Generator().manual_seed(2000 + seed)
+    x = torch.randn(R, C, generator=g)
+    y = torch.randn(R, C, generator=g)
+    v = torch.randn(1, C, generator=g)
+    col = torch.randn(R, 1, generator=g)
+    out = torch.full((R, C), float("nan"), device=DEV)
+    out2 = torch.full((R, C), float("nan"), device=DEV)
+    xt.launch(m, x.to(DEV), y.to(DEV), v.to(DEV), col.to(DEV), out, out2)
+    arrays = [x.numpy(), y.numpy(), v.numpy(), col.numpy(), np.zeros((R, C), np.float32), np.zeros((R, C), np.float32)]
+    xt_oracle.run(m.source_text, arrays)
+    for got, ref in ((out, arrays[4]), (out2, arrays[5])):
         got = got.cpu().numpy()
         assert np.all(np.isfinite(got) == np.isfinite(ref)), m.plan()["family"]
         ok = np.isfinite(ref)

@@ -622,6 +622,100 @@ void emit_accumulate(std::ostringstream& s, bool sum, int64_t n, int64_t step, i
     << (sum ? "(a0 + a1) + (a2 + a3)" : "xt_max_nan(xt_max_nan(a0, a1), xt_max_nan(a2, a3))") << ";\n";
 }
 
+// The end of the run of elementwise ops (const, unary, binary) from ``o``
+// that can share one pass over their common result shape with no barrier
+// between them: a thread then handles the same elements in every op, so an
+// op reading the result of an earlier op of the run reads what that thread
+// itself computed.  The run stops before an op whose result has another
+// shape, that reads a result of the run along a broadcast dim (another
+// thread's element), or whose result slot overlaps shared memory that the
+// run has read or written other than at the same element of a same-shaped,
+// same-pitch value (a slot the planner recycled while other threads may
+// still be reading its previous value).
+template <class Ew, class Same, class Reads>
+int elementwise_run(const dev::TileArgs& a, int o, const std::vector<bool>& compact, Ew elementwise, Same same_shape,
+                    Reads reads) {
+  struct Touch {
+    int64_t lo, hi, pitch;
+    int val;
+    bool own;  // accessed only at the thread's own elements
+  };
+  auto geom = [&](int v) { return tile_geom(a.vals[v], compact[v]); };
+  auto touch = [&](int v, bool own) {
+    const TileGeom g = geom(v);
+    return Touch{g.off, g.off + g.rows() * g.st[2], g.st[2], v, own};
+  };
+  const int shape_of = a.ops[o].dst;
+  std::vector<Touch> touched;
+  std::set<int> made;
+  int e = o;
+  for (; e < a.n_ops; ++e) {
+    const TileOp& op = a.ops[e];
+    if (!elementwise(op) || !same_shape(op.dst, shape_of)) break;
+    bool ok = true;
+    for (int x : reads(op))
+      if (made.count(x) && !same_shape(x, shape_of)) ok = false;
+    const Touch w = touch(op.dst, true);
+    for (const Touch& t : touched) {
+      const bool overlap = w.lo < t.hi && t.lo < w.hi;
+      const bool same_element = t.own && t.lo == w.lo && t.pitch == w.pitch;
+      if (overlap && !same_element) ok = false;
+    }
+    if (!ok && e > o) break;
+    for (int x : reads(op))
+      if (!made.count(x)) touched.push_back(touch(x, same_shape(x, shape_of)));
+    touched.push_back(w);
+    made.insert(op.dst);
+  }
+  return e;
+}
+
+// Ops [o, e) (a run from elementwise_run) as one loop over their result
+// shape: each result a register; a result goes to its shared-memory slot
+// only when an op after the run reads it.
+void emit_elementwise(std::ostringstream& s, const dev::TileArgs& a, int o, int e, int th,
+                      const std::vector<bool>& compact, const std::vector<std::vector<int>>& readers) {
+  auto geom = [&](int v) { return tile_geom(a.vals[v], compact[v]); };
+  const TileGeom S = geom(a.ops[o].dst);
+  std::set<int> made;
+  std::ostringstream b;
+  b << "        const int c = cv; " << row_index(S.s, "q") << "\n";
+  auto operand = [&](int x) {
+    if (made.count(x)) return "r" + std::to_string(x);
+    const TileGeom g = geom(x);
+    int64_t sx[kTileRank];  // broadcast dims (size 1) contribute no stride
+    for (int k = 0; k < kTileRank; ++k) sx[k] = g.s[k] == 1 ? 0 : g.st[k];
+    return "xt_sm[" + std::to_string(g.off) + " + " + dot(sx, S.s) + "]";
+  };
+  for (int j = o; j < e; ++j) {
+    const TileOp& op = a.ops[j];
+    std::string expr;
+    if (op.kind == kTConst) {
+      expr = float_lit(op.value);
+    } else if (op.kind == kTUnary) {
+      const char* fn = unary_fn(op.code);
+      if (!fn) fail("unary opcode " + std::to_string(op.code) + " in a tile program");
+      expr = std::string(fn) + "(" + operand(op.a) + ")";
+    } else {
+      const char* fn = binary_fn(op.code);
+      if (!fn || !is_binary(op.code)) fail("binary opcode " + std::to_string(op.code) + " in a tile program");
+      expr = std::string(fn) + "(" + operand(op.a) + ", " + operand(op.b) + ")";
+      if (a.vals[op.dst].i8) expr = "xt_wrap_i8(" + expr + ")";
+    }
+    b << "        const float r" << int(op.dst) << " = " << expr << ";  // op " << j << "\n";
+    made.insert(op.dst);
+    bool later = false;
+    for (int r : readers[op.dst]) later = later || r >= e;
+    if (later) {
+      const TileGeom d = geom(op.dst);
+      b << "        xt_sm[" << d.off << " + q * " << d.st[2] << " + c] = r" << int(op.dst) << ";\n";
+    }
+  }
+  s << "  {  // ops " << o << "-" << e - 1 << ": one pass\n";
+  loop_rows(s, th, S.rows(), S.s[3], b.str());
+  s << "  }\n";
+}
+
 // first float of the split reductions' partial results (8-byte aligned)
 int64_t red_offset(const dev::TileArgs& a) { return (a.smem_floats + 1) & ~1; }
 
@@ -662,8 +756,52 @@ std::string tile_source(const dev::TileArgs& a, int th) {
        "  const int t = threadIdx.x;\n"
        "  const xt_i64 b0 = p.bid0_begin + blockIdx.x, b1 = blockIdx.y, b2 = blockIdx.z;\n"
        "  (void)b0; (void)b1; (void)b2;\n";
-  for (int o = 0; o < a.n_ops; ++o) {
+  // the ops reading each value, and whether each op is elementwise
+  std::vector<std::vector<int>> readers(kTileMaxVals);
+  auto reads = [&](const TileOp& op) {
+    std::vector<int> r;
+    if (op.kind == kTStore) r.push_back(op.code == 1 ? op.b : op.a);
+    if (op.kind == kTUnary || op.kind == kTBinary || op.kind == kTReduce || op.kind == kTReshape || op.kind == kTPermute)
+      r.push_back(op.a);
+    if (op.kind == kTBinary) r.push_back(op.b);
+    return r;
+  };
+  for (int o = 0; o < a.n_ops; ++o)
+    for (int x : reads(a.ops[o])) readers[x].push_back(o);
+  auto elementwise = [&](const TileOp& op) { return op.kind == kTConst || op.kind == kTUnary || op.kind == kTBinary; };
+  auto same_shape = [&](int u, int v) {
+    for (int d = 0; d < kTileRank; ++d)
+      if (a.vals[u].shape[d] != a.vals[v].shape[d]) return false;
+    return true;
+  };
+  // loads since the last barrier (slot ranges): a load following only
+  // loads needs no barrier before it when its slot is disjoint from theirs
+  // (loads read no shared memory)
+  std::vector<std::pair<int64_t, int64_t>> loaded;
+  bool only_loads = true;
+  for (int o = 0; o < a.n_ops;) {
     const TileOp& op = a.ops[o];
+    bool barrier = o > 0;
+    if (op.kind == kTLoad) {
+      const TileGeom g = tile_geom(a.vals[op.dst]);
+      const std::pair<int64_t, int64_t> r{g.off, g.off + g.rows() * g.st[2]};
+      bool disjoint = only_loads;
+      for (const auto& l : loaded) disjoint = disjoint && (r.second <= l.first || l.second <= r.first);
+      if (disjoint) barrier = false;
+      if (barrier) loaded.clear();
+      loaded.push_back(r);
+      only_loads = true;
+    } else {
+      loaded.clear();
+      only_loads = false;
+    }
+    if (barrier) s << "  __syncthreads();\n";
+    if (elementwise(op)) {
+      const int e = elementwise_run(a, o, compact, elementwise, same_shape, reads);
+      emit_elementwise(s, a, o, e, th, compact, readers);
+      o = e;
+      continue;
+    }
     s << "  {  // op " << o << "\n";
     switch (op.kind) {
       case kTLoad: {
@@ -699,41 +837,6 @@ std::string tile_source(const dev::TileArgs& a, int th) {
         }
         emit_store(s, a, op, v, rd_off, rd, g, th, false);
         if (g.vec) s << "    }\n";
-        break;
-      }
-      case kTConst: {
-        const TileGeom d = tile_geom(a.vals[op.dst]);
-        loop_rows(s, th, d.rows(), d.s[3],
-                  "        xt_sm[" + std::to_string(d.off) + " + q * " + std::to_string(d.st[2]) + " + cv] = " +
-                      float_lit(op.value) + ";\n");
-        break;
-      }
-      case kTUnary: {
-        const TileGeom d = tile_geom(a.vals[op.dst]), x = tile_geom(a.vals[op.a]);
-        const char* fn = unary_fn(op.code);
-        if (!fn) fail("unary opcode " + std::to_string(op.code) + " in a tile program");
-        loop_rows(s, th, d.rows(), d.s[3],
-                  "        xt_sm[" + std::to_string(d.off) + " + q * " + std::to_string(d.st[2]) + " + cv] = " + fn +
-                      "(xt_sm[" + std::to_string(x.off) + " + q * " + std::to_string(x.st[2]) + " + cv]);\n");
-        break;
-      }
-      case kTBinary: {
-        const TileGeom d = tile_geom(a.vals[op.dst]), x = tile_geom(a.vals[op.a]), y = tile_geom(a.vals[op.b]);
-        const char* fn = binary_fn(op.code);
-        if (!fn || !is_binary(op.code)) fail("binary opcode " + std::to_string(op.code) + " in a tile program");
-        // broadcast dims (size 1) contribute no stride
-        int64_t sx[kTileRank], sy[kTileRank];
-        for (int k = 0; k < kTileRank; ++k) {
-          sx[k] = x.s[k] == 1 ? 0 : x.st[k];
-          sy[k] = y.s[k] == 1 ? 0 : y.st[k];
-        }
-        std::ostringstream b;
-        b << "        const int c = cv; " << row_index(d.s, "q") << "\n"
-          << "        const float r = " << fn << "(xt_sm[" << x.off << " + " << dot(sx, d.s) << "], xt_sm[" << y.off << " + "
-          << dot(sy, d.s) << "]);\n"
-          << "        xt_sm[" << d.off << " + q * " << d.st[2] << " + c] = " << (a.vals[op.dst].i8 ? "xt_wrap_i8(r)" : "r")
-          << ";\n";
-        loop_rows(s, th, d.rows(), d.s[3], b.str());
         break;
       }
       case kTReduce: {
@@ -792,7 +895,7 @@ std::string tile_source(const dev::TileArgs& a, int th) {
         fail("tile op kind " + std::to_string(op.kind));
     }
     s << "  }\n";
-    if (o + 1 < a.n_ops) s << "  __syncthreads();\n";
+    ++o;
   }
   s << "}\n";
   for (int v = 1; v >= 0; --v)
