@@ -184,12 +184,13 @@ def test_random_tile_program_compiles(seed):
 
 def test_elementwise_ops_share_one_pass():
     # load, load, (t * c - c), sigmoid, store: the three elementwise ops run
-    # as one pass with their intermediate results in registers; the two
-    # loads need no barrier between them: two barriers in all
+    # as one pass with their intermediate results in registers, four columns
+    # (a float4) per step; the two loads need no barrier between them: two
+    # barriers in all
     F = xt.float32
     m = xt.convert(tile_cases.col_vector_ops, args=(A((16384, 2048), F), A((16384, 1), F), A((16384, 2048), F), 32, 64),
                    grid=(512, 32, 1))
     body = generated(m).split("template <bool V>")[1]
-    assert "ops 2-4: one pass" in body
+    assert "ops 2-4: one pass, 4 columns per step" in body
     assert body.count("__syncthreads") == 2
     assert compiles(m)

@@ -677,42 +677,98 @@ void emit_elementwise(std::ostringstream& s, const dev::TileArgs& a, int o, int 
                       const std::vector<bool>& compact, const std::vector<std::vector<int>>& readers) {
   auto geom = [&](int v) { return tile_geom(a.vals[v], compact[v]); };
   const TileGeom S = geom(a.ops[o].dst);
+  // whether a result is read after the run (and so goes to its slot)
+  auto later = [&](int v) {
+    for (int r : readers[v])
+      if (r >= e) return true;
+    return false;
+  };
+  // broadcast dims (size 1) contribute no stride
+  auto strides = [&](int x, int64_t (&sx)[kTileRank]) {
+    const TileGeom g = geom(x);
+    for (int k = 0; k < kTileRank; ++k) sx[k] = g.s[k] == 1 ? 0 : g.st[k];
+    return g;
+  };
+  // Four consecutive columns per step when the rows hold whole 4-element
+  // groups and every shared-memory access of the run is 16-byte aligned or
+  // a broadcast along the columns.
+  bool vec = S.s[3] % 4 == 0;
+  {
+    std::set<int> made;
+    for (int j = o; j < e && vec; ++j) {
+      const TileOp& op = a.ops[j];
+      std::vector<int> xs;
+      if (op.kind != kTConst) xs.push_back(op.a);
+      if (op.kind == kTBinary) xs.push_back(op.b);
+      for (int x : xs) {
+        if (made.count(x)) continue;
+        int64_t sx[kTileRank];
+        const TileGeom g = strides(x, sx);
+        if (sx[3] == 0) continue;  // one value per row: read once, used four times
+        vec = vec && g.off % 4 == 0;
+        for (int k = 0; k < kTileRank - 1; ++k) vec = vec && sx[k] % 4 == 0;
+      }
+      made.insert(op.dst);
+      if (later(op.dst)) {
+        const TileGeom d = geom(op.dst);
+        vec = vec && d.off % 4 == 0 && d.st[2] % 4 == 0;
+      }
+    }
+  }
   std::set<int> made;
   std::ostringstream b;
-  b << "        const int c = cv; " << row_index(S.s, "q") << "\n";
+  b << "        const int c = " << (vec ? "4 * cv" : "cv") << "; " << row_index(S.s, "q") << "\n";
   auto operand = [&](int x) {
     if (made.count(x)) return "r" + std::to_string(x);
-    const TileGeom g = geom(x);
-    int64_t sx[kTileRank];  // broadcast dims (size 1) contribute no stride
-    for (int k = 0; k < kTileRank; ++k) sx[k] = g.s[k] == 1 ? 0 : g.st[k];
-    return "xt_sm[" + std::to_string(g.off) + " + " + dot(sx, S.s) + "]";
+    int64_t sx[kTileRank];
+    const TileGeom g = strides(x, sx);
+    const std::string at = std::to_string(g.off) + " + " + dot(sx, S.s);
+    if (!vec) return "xt_sm[" + at + "]";
+    if (sx[3] == 0) {
+      const std::string one = "xt_sm[" + at + "]";
+      return "make_float4(" + one + ", " + one + ", " + one + ", " + one + ")";
+    }
+    return "*reinterpret_cast<const float4*>(xt_sm + " + at + ")";
+  };
+  const char* T = vec ? "float4" : "float";
+  // an operand as a named value (the macros of the vector form use it four times)
+  auto bind = [&](int x, int j, int k) {
+    if (made.count(x)) return "r" + std::to_string(x);
+    const std::string name = "x" + std::to_string(j) + "_" + std::to_string(k);
+    b << "        const " << T << " " << name << " = " << operand(x) << ";\n";
+    return name;
   };
   for (int j = o; j < e; ++j) {
     const TileOp& op = a.ops[j];
     std::string expr;
     if (op.kind == kTConst) {
-      expr = float_lit(op.value);
+      const std::string v = float_lit(op.value);
+      expr = vec ? "make_float4(" + v + ", " + v + ", " + v + ", " + v + ")" : v;
     } else if (op.kind == kTUnary) {
       const char* fn = unary_fn(op.code);
       if (!fn) fail("unary opcode " + std::to_string(op.code) + " in a tile program");
-      expr = std::string(fn) + "(" + operand(op.a) + ")";
+      const std::string x = bind(op.a, j, 0);
+      expr = vec ? "XT_MAP1(" + std::string(fn) + ", " + x + ")" : std::string(fn) + "(" + x + ")";
     } else {
       const char* fn = binary_fn(op.code);
       if (!fn || !is_binary(op.code)) fail("binary opcode " + std::to_string(op.code) + " in a tile program");
-      expr = std::string(fn) + "(" + operand(op.a) + ", " + operand(op.b) + ")";
-      if (a.vals[op.dst].i8) expr = "xt_wrap_i8(" + expr + ")";
+      const std::string x = bind(op.a, j, 0), y = bind(op.b, j, 1);
+      expr = vec ? "XT_MAP2(" + std::string(fn) + ", " + x + ", " + y + ")" : std::string(fn) + "(" + x + ", " + y + ")";
+      if (a.vals[op.dst].i8) expr = vec ? "XT_MAP1(xt_wrap_i8, " + expr + ")" : "xt_wrap_i8(" + expr + ")";
     }
-    b << "        const float r" << int(op.dst) << " = " << expr << ";  // op " << j << "\n";
+    b << "        const " << T << " r" << int(op.dst) << " = " << expr << ";  // op " << j << "\n";
     made.insert(op.dst);
-    bool later = false;
-    for (int r : readers[op.dst]) later = later || r >= e;
-    if (later) {
+    if (later(op.dst)) {
       const TileGeom d = geom(op.dst);
-      b << "        xt_sm[" << d.off << " + q * " << d.st[2] << " + c] = r" << int(op.dst) << ";\n";
+      if (vec)
+        b << "        *reinterpret_cast<float4*>(xt_sm + " << d.off << " + q * " << d.st[2] << " + c) = r" << int(op.dst)
+          << ";\n";
+      else
+        b << "        xt_sm[" << d.off << " + q * " << d.st[2] << " + c] = r" << int(op.dst) << ";\n";
     }
   }
-  s << "  {  // ops " << o << "-" << e - 1 << ": one pass\n";
-  loop_rows(s, th, S.rows(), S.s[3], b.str());
+  s << "  {  // ops " << o << "-" << e - 1 << ": one pass" << (vec ? ", 4 columns per step" : "") << "\n";
+  loop_rows(s, th, S.rows(), vec ? S.s[3] / 4 : S.s[3], b.str());
   s << "  }\n";
 }
 
