@@ -830,32 +830,67 @@ std::string tile_source(const dev::TileArgs& a, int th) {
       if (a.vals[u].shape[d] != a.vals[v].shape[d]) return false;
     return true;
   };
-  // loads since the last barrier (slot ranges): a load following only
-  // loads needs no barrier before it when its slot is disjoint from theirs
-  // (loads read no shared memory)
-  std::vector<std::pair<int64_t, int64_t>> loaded;
-  bool only_loads = true;
+  // Shared memory read and written since the last barrier.  A unit (one op,
+  // or a run of elementwise ops in one pass) needs a barrier before it only
+  // when it writes what was read or written since, or reads what was
+  // written since: its threads may touch other elements than the threads
+  // that did.
+  struct Span {
+    int64_t lo, hi;
+  };
+  std::vector<Span> rd, wr;
+  auto span = [&](int v) {
+    const TileGeom g = tile_geom(a.vals[v]);
+    return Span{g.off, g.off + g.rows() * g.st[2]};
+  };
+  const Span scratch{red_offset(a), red_offset(a) + 2 * th};
+  auto hits = [](const std::vector<Span>& xs, const std::vector<Span>& ys) {
+    for (const Span& x : xs)
+      for (const Span& y : ys)
+        if (x.lo < y.hi && y.lo < x.hi) return true;
+    return false;
+  };
   for (int o = 0; o < a.n_ops;) {
     const TileOp& op = a.ops[o];
-    bool barrier = o > 0;
-    if (op.kind == kTLoad) {
-      const TileGeom g = tile_geom(a.vals[op.dst]);
-      const std::pair<int64_t, int64_t> r{g.off, g.off + g.rows() * g.st[2]};
-      bool disjoint = only_loads;
-      for (const auto& l : loaded) disjoint = disjoint && (r.second <= l.first || l.second <= r.first);
-      if (disjoint) barrier = false;
-      if (barrier) loaded.clear();
-      loaded.push_back(r);
-      only_loads = true;
-    } else {
-      loaded.clear();
-      only_loads = false;
-    }
-    if (barrier) s << "  __syncthreads();\n";
+    const int end = elementwise(op) ? elementwise_run(a, o, compact, elementwise, same_shape, reads) : o + 1;
+    std::vector<Span> r_u, w_u;
     if (elementwise(op)) {
-      const int e = elementwise_run(a, o, compact, elementwise, same_shape, reads);
-      emit_elementwise(s, a, o, e, th, compact, readers);
-      o = e;
+      std::set<int> made;
+      for (int j = o; j < end; ++j) {
+        for (int x : reads(a.ops[j]))
+          if (!made.count(x)) r_u.push_back(span(x));
+        made.insert(a.ops[j].dst);
+        bool later = false;
+        for (int r : readers[a.ops[j].dst]) later = later || r >= end;
+        if (later) w_u.push_back(span(a.ops[j].dst));
+      }
+    } else {
+      for (int x : reads(op)) r_u.push_back(span(x));
+      if (op.kind != kTStore) w_u.push_back(span(op.dst));
+      // global arrays as spans below shared memory: a store orders against
+      // an earlier load or store of the same array by the Block's threads
+      const Span array{-2 - 2 * static_cast<int64_t>(op.arg), -1 - 2 * static_cast<int64_t>(op.arg)};
+      if (op.kind == kTLoad) r_u.push_back(array);
+      if (op.kind == kTStore) w_u.push_back(array);
+      if (op.kind == kTReduce) {
+        const TileVal &dv = a.vals[op.dst], &xv = a.vals[op.a];
+        const int64_t outs = static_cast<int64_t>(dv.numel);
+        if (reduce_parts(outs, xv.shape[op.axis], th) > 1) {
+          r_u.push_back(scratch);
+          w_u.push_back(scratch);
+        }
+      }
+    }
+    if (o > 0 && (hits(w_u, rd) || hits(w_u, wr) || hits(r_u, wr))) {
+      s << "  __syncthreads();\n";
+      rd.clear();
+      wr.clear();
+    }
+    rd.insert(rd.end(), r_u.begin(), r_u.end());
+    wr.insert(wr.end(), w_u.begin(), w_u.end());
+    if (elementwise(op)) {
+      emit_elementwise(s, a, o, end, th, compact, readers);
+      o = end;
       continue;
     }
     s << "  {  // op " << o << "\n";
