@@ -19,6 +19,9 @@ Workloads are the BASELINE configurations (synthetic, seeded inputs):
                   kernels/matmul.py program (scale, bias, int8 out) at 8192^3
   col_sums        not a BASELINE configuration: a generated tile kernel
                   (column sums of 64 x 32 tiles of a 128 MiB f32 array)
+  col_bias        not a BASELINE configuration: a generated tile kernel whose
+                  elementwise ops run as one pass (sigmoid(t * c - c), c a
+                  column broadcast over 32 x 64 tiles)
 
 A step is one launch of the workload's Block program over its whole Grid
 (for sharded_matmul: every rank's share plus the gather).  ``value`` is the
@@ -83,6 +86,7 @@ NCU_TRAFFIC_BYTES: dict[str, float] = {
     "silu": 134_240_512 + 84_709_376,
     "row_center": 134_223_360 + 78_821_120,
     "col_sums": 134_223_360 + 4_445_056,
+    "col_bias": 134_317_056 + 81_739_648,
 }
 
 
@@ -289,6 +293,28 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
                              grid=(R // tm, C // tn, 1), double_buffering=True)
         return dict(text=text, inputs=[x], work=(R * C + R // tm * C) * 4, tolerance="sum", out_shape=(R // tm, C),
                     out_dtype=torch.float32, unit="GB/s", dtype="f32",
+                    config={"workload": name, "shape": [R, C], "block_tile": [tm, tn], "grid": [R // tm, C // tn, 1]})
+    if name == "col_bias":
+        # not a BASELINE configuration: a tile program whose elementwise ops
+        # run as one pass (sigmoid(t * c - c), c a (32, 1) column of a [R, 1]
+        # array) over a 128 MiB f32 array
+        @xt.kernel
+        def col_bias(x, c, out, tm, tn):
+            i, j = xt.bid(0), xt.bid(1)
+            t = xt.load(x, index=(i, j), shape=(tm, tn))
+            s = xt.load(c, index=(i, 0), shape=(tm, 1))
+            xt.store(out, index=(i, j), tile=xt.sigmoid(t * s - s))
+
+        R, C, tm, tn = 16384, 2048, 32, 64
+        x = torch.randn(R, C, generator=g(10))
+        col = torch.randn(R, 1, generator=g(11))
+        F = xt.float32
+        text = xt.trace_text(col_bias, args=(A((R, C), F), A((R, 1), F), A((R, C), F), tm, tn),
+                             grid=(R // tm, C // tn, 1), double_buffering=True)
+        # bytes of every Block's tiles: each of the C / tn Blocks of a row of
+        # tiles loads its (32, 1) column (from L2 after the first)
+        return dict(text=text, inputs=[x, col], work=(2 * R * C + R * (C // tn)) * 4, tolerance="transcendental",
+                    out_shape=(R, C), out_dtype=torch.float32, unit="GB/s", dtype="f32",
                     config={"workload": name, "shape": [R, C], "block_tile": [tm, tn], "grid": [R // tm, C // tn, 1]})
     raise SystemExit(f"unknown workload {name}")
 
@@ -831,7 +857,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="sharded_matmul",
                     choices=["add", "softmax", "matmul", "conv2d", "sharded_matmul", "transpose", "silu",
-                             "row_center", "row_bias", "matmul_i8", "col_sums"])
+                             "row_center", "row_bias", "matmul_i8", "col_sums", "col_bias"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference", "torch"],
                     help="b200: this backend; reference: the reference's CPU path; torch: the vendor library "
                          "(cuBLAS, cuDNN) through PyTorch on one GPU, for context")
@@ -1378,6 +1404,9 @@ def run_torch_library(args, torch) -> None:
         lib = "torch.addcmul(r, x, r, out=)"
         fn = lambda i: torch.addcmul(sets[i % n_sets][1], sets[i % n_sets][0], sets[i % n_sets][1],  # noqa: E731
                                      out=outs[i % n_sets])
+    elif name == "col_bias":
+        lib = "torch: sigmoid(x * c - c) (three kernels)"
+        fn = lambda i: torch.sigmoid((sets[i % n_sets][0] * sets[i % n_sets][1]).sub_(sets[i % n_sets][1]))  # noqa: E731
     elif name == "col_sums":
         lib = "torch.sum over the 64-row tiles (f32 accumulation, out=)"
         fn = lambda i: torch.sum(sets[i % n_sets][0].view(256, 64, 2048), dim=1, out=outs[i % n_sets])  # noqa: E731
