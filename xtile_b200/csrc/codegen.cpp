@@ -786,12 +786,12 @@ int tile_smem_floats(const dev::TileArgs& a, int th) {
 int tile_threads(const dev::TileArgs& a) {
   int64_t most = 0;
   for (int v = 0; v < kTileMaxVals; ++v) most = std::max<int64_t>(most, a.vals[v].numel);
-  return most <= 4096 ? 128 : 256;
+  return most <= 4096 ? 128 : most <= 8192 ? 256 : most <= 16384 ? 512 : 1024;
 }
 
 std::string tile_source(const dev::TileArgs& a, int th) {
   if (a.n_ops <= 0 || a.n_ops > kTileMaxOps) fail("tile program length");
-  if (th != 64 && th != 128 && th != 256) fail("tile CTA width");
+  if (th != 64 && th != 128 && th != 256 && th != 512 && th != 1024) fail("tile CTA width");
   std::ostringstream s;
   s << kOpMath << kHelpers;
   s << "struct XtTileArgs { void* arr[" << kTileMaxArgs << "]; xt_i64 bid0_begin; };\n"
@@ -945,6 +945,42 @@ std::string tile_source(const dev::TileArgs& a, int th) {
           s << "#pragma unroll 2\n    for (int o = t; o < " << outs << "; o += " << th << ") {\n" << at;
           emit_accumulate(s, sum, n, step, 1, "0");
           s << put << (sum ? "static_cast<float>(acc);\n" : "acc;\n") << "    }\n";
+          break;
+        }
+        if (parts >= 32 && op.axis == kTileRank - 1) {
+          // Few outputs along rows (a softmax's row max and sum): an output's
+          // parts in whole warps, each warp reading consecutive words of one
+          // row, combined by a fixed shuffle tree and then across warps
+          // through shared memory.  (With fewer parts, several rows would
+          // share a warp and their words, a row pitch apart, would collide
+          // in the same banks.)
+          const int64_t lanes = 32, warps = parts / lanes;
+          const char* T = sum ? "double" : "float";
+          const char* ident = sum ? "0.0" : "__int_as_float(0xff800000)";
+          auto comb = [&](const std::string& x, const std::string& y) {
+            return sum ? x + " + " + y : "xt_max_nan(" + x + ", " + y + ")";
+          };
+          s << "    {\n      const int o = t / " << parts << ", part = t % " << parts << ";\n"
+            << "      " << T << " part_acc = " << ident << ";\n"
+            << "      if (o < " << outs << ") {\n" << at;
+          emit_accumulate(s, sum, n, step, parts, "part");
+          s << "        part_acc = acc;\n      }\n"
+            << "#pragma unroll\n      for (int off = 1; off < " << lanes << "; off <<= 1)\n"
+            << "        part_acc = " << comb("part_acc", "__shfl_xor_sync(0xffffffffu, part_acc, off)") << ";\n";
+          if (warps == 1) {
+            s << "      if (o < " << outs << " && part == 0) {\n        const int q = o / " << d.s[3] << ", c = o % "
+              << d.s[3] << ";\n        const " << T << " acc = part_acc;\n"
+              << put << (sum ? "static_cast<float>(acc);\n" : "acc;\n") << "      }\n    }\n";
+          } else {
+            const char* red = sum ? "xt_red_f64" : "xt_red_f32";
+            s << "      if (o < " << outs << " && (part & 31) == 0) " << red << "[o * " << warps << " + part / 32] = part_acc;\n"
+              << "      __syncthreads();\n"
+              << "      if (t < " << outs << ") {\n        const int o = t, q = o / " << d.s[3] << ", c = o % " << d.s[3]
+              << ";\n        " << T << " acc = " << red << "[o * " << warps << "];\n"
+              << "#pragma unroll\n        for (int k = 1; k < " << warps << "; ++k) acc = "
+              << comb("acc", std::string(red) + "[o * " + std::to_string(warps) + " + k]") << ";\n"
+              << put << (sum ? "static_cast<float>(acc);\n" : "acc;\n") << "      }\n    }\n";
+          }
           break;
         }
         // ``parts`` threads per output, each over every parts-th element from

@@ -35,9 +35,10 @@ bool rows_fit(const dev::RowArgs& a);
 // groups move 4 elements at a time; every array 16-byte aligned) and
 // ``xt_tile_s`` (element accesses).
 std::string tile_source(const dev::TileArgs& a, int threads);
-// The CTA width for a tile program: 128 threads when every tile holds at
-// most 4096 elements, else 256 (column sums of 64 x 32 tiles: 4391 GB/s with
-// 64 threads, 5979 with 128, 5124 with 256).
+// The CTA width for a tile program by its largest tile: 128 threads up to
+// 4096 elements, 256 up to 8192, 512 up to 16384, else 1024 (column sums of
+// 64 x 32 tiles: 4391 GB/s with 64 threads, 5979 with 128, 5124 with 256;
+// large tiles hold an SM alone and need the loads of many threads in flight).
 int tile_threads(const dev::TileArgs& a);
 // Shared memory (floats) of the tile kernel for ``a`` at ``threads``
 // threads: the planned slots, then one double per thread for the partial
