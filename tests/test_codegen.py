@@ -86,13 +86,42 @@ def row_stats(x, s, y, trow, col):
     xt.store(y, index=(i, 0), tile=xt.exp(t - m) * xt.reciprocal(xt.sum(t, axis=1)))
 
 
-@pytest.mark.parametrize("cols", [16, 37, 1024, 2048])
+@pytest.mark.parametrize("cols", [16, 37, 1024, 2048, 3000, 8192, 16384])
 def test_row_programs_compile_for_any_width(cols):
+    # up to 2048 columns one warp per row; wider rows one CTA per row
     F = xt.float32
     m = xt.convert(row_stats, args=(A((64, cols), F), A((64, 1), F), A((64, cols), F), 2, cols), grid=(32, 1, 1))
     assert m.plan()["family"] == "rows"
     src = generated(m)
-    assert f"#define XT_COLS {cols}" in src and "xt_rows_v" in src and "xt_rows_s" in src
+    kernels = ("xt_rows_v", "xt_rows_s") if cols <= 2048 else ("xt_rows_cv", "xt_rows_cs", "xt_cta_max")
+    assert f"#define XT_COLS {cols}" in src and all(k in src for k in kernels)
+    assert compiles(m)
+
+
+def test_row_programs_beyond_a_cta_are_refused_loudly():
+    # two live rows of 32768 columns exceed a CTA's registers (1024 threads,
+    # 32 values each) and their tiles exceed 192 KiB of shared memory: the
+    # planner refuses the program with both reasons
+    F = xt.float32
+    m = xt.convert(row_stats, args=(A((64, 32768), F), A((64, 1), F), A((64, 32768), F), 2, 32768), grid=(32, 1, 1))
+    with pytest.raises(RuntimeError, match="exceed a CTA's registers"):
+        m.plan()
+
+
+def test_wide_softmax_runs_a_generated_kernel():
+    @xt.kernel
+    def softmax_rows(inp, out, trow, col):
+        i = xt.bid(0)
+        x = xt.load(inp, index=(i, 0), shape=(trow, col))
+        x = x - xt.max(x, axis=-1)
+        x = xt.exp(x)
+        xt.store(out, index=(i, 0), tile=x / xt.sum(x, axis=-1))
+
+    F = xt.float32
+    m = xt.convert(softmax_rows, args=(A((64, 32768), F), A((64, 32768), F), 1, 32768), grid=(64, 1, 1))
+    assert m.plan()["family"] == "rows"
+    src = generated(m)
+    assert "#define XT_TPR 1024" in src and "xt_cta_sum" in src
     assert compiles(m)
 
 

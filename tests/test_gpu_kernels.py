@@ -235,6 +235,40 @@ def test_row_program_generated(rows, cols):
     np.testing.assert_allclose(host(mx), ref[2], rtol=1e-5)
 
 
+@pytest.mark.parametrize("rows,cols", [(40, 3000), (24, 8192), (10, 6000), (9, 4097)])
+def test_row_program_wide_rows_one_cta_per_row(rows, cols):
+    # rows wider than 2048 columns run one CTA per row (128 to 1024 threads,
+    # block reductions through shared memory); 3000 and 6000 columns: a
+    # partial last chunk; 4097: element accesses.  (This program keeps three
+    # rows live: 8192 columns is the widest a CTA holds.)
+    x = torch.randn(rows, cols, generator=gen(5)) + 3
+    y = torch.empty(rows, cols, device=DEV)
+    mx = torch.empty(rows, 1, device=DEV)
+    m = xt.run(row_stats, args=(x.to(DEV), y, mx, 8, cols), grid=((rows + 7) // 8, 1, 1))
+    assert m.plan()["family"] == "rows"
+    ref = oracle(m, [x, torch.zeros(rows, cols), torch.zeros(rows, 1)])
+    np.testing.assert_array_equal(host(y), ref[1])
+    np.testing.assert_allclose(host(mx), ref[2], rtol=1e-5)
+    assert xt.device_error() == 0
+
+
+@pytest.mark.parametrize("rows,cols", [(16, 8192), (6, 32768), (12, 5001)])
+def test_softmax_wide_rows_and_shards(rows, cols):
+    # kernels/softmax.py's program on rows wider than the dedicated kernel
+    # takes (2048): the generated one-CTA-per-row kernel; a bid0 split into
+    # two launches gives the same rows
+    got, ref = softmax_case(rows, cols, 1, 7)
+    assert np.max(np.abs(got - ref) / ref) <= 1e-5
+    x = torch.randn(rows, cols, generator=gen(7)) * 4
+    y2 = torch.full((rows, cols), float("nan"), device=DEV)
+    m = xt.convert(softmax_rows, args=(xt.Array((rows, cols), xt.float32), xt.Array((rows, cols), xt.float32), 1, cols),
+                   grid=(rows, 1, 1))
+    assert m.plan()["family"] == "rows"
+    for lo, hi in [(0, rows // 2), (rows // 2, rows)]:
+        xt.launch(m, x.to(DEV), y2, bid0_range=(lo, hi))
+    np.testing.assert_array_equal(host(y2), got)
+
+
 # ---------------------------------------------------------------- matmul
 @xt.kernel
 def matmul_kloop(lhs, rhs, out, tm, tn, tk, ksteps):

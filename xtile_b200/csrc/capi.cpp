@@ -646,8 +646,8 @@ int xt_generated_source(const xt_module* module, const char* func, char** out_te
     std::string text;
     if (p->family == xt::Family::Ew)
       text = xt::jit::ew_source(ew_args_of(p->ew, nullptr));
-    else if (p->family == xt::Family::Rows && !p->rows.softmax)
-      text = xt::jit::rows_source(row_args_of(p->rows, nullptr));
+    else if (p->family == xt::Family::Rows && (!p->rows.softmax || p->rows.cols > 2048 || p->rows.cols % 4 != 0))
+      text = xt::jit::rows_kernel_source(row_args_of(p->rows, nullptr));
     else if (p->family == xt::Family::Tile) {
       const xt::dev::TileArgs a = tile_args_of(*p, nullptr);
       text = xt::jit::tile_source(a, xt::jit::tile_threads(a));

@@ -233,8 +233,10 @@ namespace {
 int64_t rows_pl4(int64_t cols) { return ((cols + 3) / 4 + 31) / 32; }
 int64_t rows_pls(int64_t cols) { return (cols + 31) / 32; }
 
-// the rows program; ``vec``: float4 chunks (cols % 4 == 0), else elements
-void rows_body(std::ostringstream& s, const dev::RowArgs& a, bool vec) {
+// the rows program; ``vec``: float4 chunks (cols % 4 == 0), else elements;
+// ``cta``: the row spread over the CTA's XT_TPR threads (block reductions),
+// else over a warp
+void rows_body(std::ostringstream& s, const dev::RowArgs& a, bool vec, bool cta) {
   const int n_v = std::max(a.n_vregs, 1);
   const char* T = vec ? "float4" : "float";
   const char* N = vec ? "XT_PL4" : "XT_PLS";
@@ -253,8 +255,9 @@ void rows_body(std::ostringstream& s, const dev::RowArgs& a, bool vec) {
     s << ";\n";
   }
   // index of chunk / element j of this lane, and whether it lies in the row
-  const std::string idx = vec ? "const int c = j * 32 + lane; const bool in = c < XT_C4;"
-                              : "const int c = j * 32 + lane; const bool in = c < XT_COLS;";
+  const std::string width = cta ? "XT_TPR" : "32";
+  const std::string idx = vec ? "const int c = j * " + width + " + lane; const bool in = c < XT_C4;"
+                              : "const int c = j * " + width + " + lane; const bool in = c < XT_COLS;";
   for (int pc = 0; pc < a.n_code; ++pc) {
     const Instr& in = a.code[pc];
     const uint8_t op = in.op & 0x7f;
@@ -293,7 +296,8 @@ void rows_body(std::ostringstream& s, const dev::RowArgs& a, bool vec) {
       else
         s << "#pragma unroll\n    for (int j = 0; j < XT_PLS; ++j) { " << idx << " if (in) acc = "
           << (mx ? "fmaxf(acc, v" + x + "[j])" : "__fadd_rn(acc, v" + x + "[j])") << "; }\n";
-      s << "    s" << d << " = " << (mx ? "xt_warp_max" : "xt_warp_sum") << "(acc);\n  }\n";
+      s << "    s" << d << " = " << (mx ? (cta ? "xt_cta_max" : "xt_warp_max") : (cta ? "xt_cta_sum" : "xt_warp_sum"))
+        << "(acc);\n  }\n";
     } else if (scalar) {
       if (binary_fn(op) && is_binary(op))
         s << "  s" << d << " = " << binary_fn(op) << "(s" << x << ", s" << y << ");\n";
@@ -319,9 +323,54 @@ void rows_body(std::ostringstream& s, const dev::RowArgs& a, bool vec) {
 }  // namespace
 
 bool rows_fit(const dev::RowArgs& a) {
-  // values a lane holds for the program's row registers
+  // rows of at most 2048 columns whose live rows a lane holds in at most 160 values
   const int64_t n_v = std::max(a.n_vregs, 1);
-  return n_v * 4 * rows_pl4(a.cols) <= 160 && n_v * rows_pls(a.cols) <= 160;
+  return a.cols <= 2048 && n_v * 4 * rows_pl4(a.cols) <= 160 && n_v * rows_pls(a.cols) <= 160;
+}
+
+std::string rows_cta_source(const dev::RowArgs& a, int tpr) {
+  if (a.n_code <= 0 || a.n_code > kMaxInstr) fail("row program length");
+  if (a.cols <= 0) fail("row length");
+  if (tpr < 128 || tpr > 1024 || (tpr & (tpr - 1))) fail("threads per row");
+  std::ostringstream s;
+  s << kOpMath << kHelpers;
+  s << "#define XT_COLS " << a.cols << "\n#define XT_C4 " << (a.cols + 3) / 4 << "\n#define XT_TPR " << tpr
+    << "\n#define XT_PL4 " << ((a.cols + 3) / 4 + tpr - 1) / tpr << "\n#define XT_PLS " << (a.cols + tpr - 1) / tpr
+    << "\n";
+  s << "struct XtRowArgs { const float* in[" << kMaxSlots << "]; float* out[" << kMaxSlots
+    << "]; xt_i64 row_begin, row_end; };\n";
+  // block reductions: warp trees, then the warps' results in a fixed order;
+  // the first barrier keeps the previous reduction's readers ahead of the
+  // writes, the second publishes them
+  s << "__device__ __forceinline__ float xt_cta_reduce(float v, bool mx) {\n"
+       "  __shared__ float red[XT_TPR / 32];\n"
+       "  v = mx ? xt_warp_max(v) : xt_warp_sum(v);\n"
+       "  __syncthreads();\n"
+       "  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;\n"
+       "  __syncthreads();\n"
+       "  float r = red[0];\n"
+       "#pragma unroll\n"
+       "  for (int w = 1; w < XT_TPR / 32; ++w) r = mx ? fmaxf(r, red[w]) : __fadd_rn(r, red[w]);\n"
+       "  return r;\n}\n"
+       "__device__ __forceinline__ float xt_cta_max(float v) { return xt_cta_reduce(v, true); }\n"
+       "__device__ __forceinline__ float xt_cta_sum(float v) { return xt_cta_reduce(v, false); }\n";
+  for (int vec = 1; vec >= 0; --vec) {
+    s << "extern \"C\" __global__ void __launch_bounds__(" << tpr << ") " << (vec ? "xt_rows_cv" : "xt_rows_cs")
+      << "(const XtRowArgs p) {\n"
+         "  const int lane = threadIdx.x;\n"
+         "  const xt_i64 row = p.row_begin + static_cast<xt_i64>(blockIdx.x);\n"
+         "  xt_pdl_launch();\n  if (row >= p.row_end) return;\n  xt_pdl_wait();\n";
+    rows_body(s, a, vec == 1, true);
+    s << "}\n";
+  }
+  return s.str();
+}
+
+std::string rows_kernel_source(const dev::RowArgs& a) {
+  if (rows_fit(a)) return rows_source(a);
+  const int tpr = row_cta_threads(a.cols, std::max(a.n_vregs, 1));
+  if (!tpr) fail("the row program's live rows exceed a CTA's registers");
+  return rows_cta_source(a, tpr);
 }
 
 std::string rows_source(const dev::RowArgs& a) {
@@ -340,7 +389,7 @@ std::string rows_source(const dev::RowArgs& a) {
          "  const int lane = threadIdx.x & 31;\n"
          "  const xt_i64 row = p.row_begin + static_cast<xt_i64>(blockIdx.x) * XT_ROWS_PER_CTA + (threadIdx.x >> 5);\n"
          "  xt_pdl_launch();\n  if (row >= p.row_end) return;\n  xt_pdl_wait();\n";
-    rows_body(s, a, vec == 1);
+    rows_body(s, a, vec == 1, false);
     s << "}\n";
   }
   return s.str();

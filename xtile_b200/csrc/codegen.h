@@ -26,9 +26,14 @@ std::string ew_source(const dev::EwArgs& a);
 // columns: ``xt_rows_v`` (float4 accesses, cols % 4 == 0 on 16-byte aligned
 // rows) and ``xt_rows_s`` (element accesses).
 std::string rows_source(const dev::RowArgs& a);
-// Whether a rows program fits the generated kernels' registers (wider ones
-// run the shared-memory interpreter).
+// Whether a rows program runs the one-warp-per-row kernels: rows of at most
+// 2048 columns whose live rows a lane holds in at most 160 values.  Others
+// run ``xt_rows_cv`` / ``xt_rows_cs`` (rows_cta_source): one CTA of
+// ``tpr`` threads per row (row_cta_threads in plan.h), block reductions.
 bool rows_fit(const dev::RowArgs& a);
+std::string rows_cta_source(const dev::RowArgs& a, int tpr);
+// The source a launch of the rows program compiles (one of the two above).
+std::string rows_kernel_source(const dev::RowArgs& a);
 
 // CUDA source of the tile-program kernels for ``a`` run by ``threads``
 // threads per CTA: ``xt_tile_v`` (accesses whose rows are whole 4-element

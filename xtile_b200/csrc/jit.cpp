@@ -321,7 +321,10 @@ cudaError_t launch_rows(const dev::RowArgs& a, cudaStream_t stream) {
     extra += static_cast<char>(a.in_scalar[k]);
     extra += static_cast<char>(a.out_scalar[k]);
   }
-  const std::string key = key_of('r', a.code, a.n_code, extra);
+  const bool warp = rows_fit(a);
+  const int tpr = warp ? 32 : row_cta_threads(a.cols, std::max(a.n_vregs, 1));
+  if (!tpr) throw Error(kUnsupported, "the row program's live rows exceed a CTA's registers");
+  const std::string key = key_of(warp ? 'r' : 'R', a.code, a.n_code, extra);
   bool vec = a.cols % 4 == 0;
   for (int k = 0; k < kMaxSlots && vec; ++k) {
     if (a.in[k] && !a.in_scalar[k]) vec = (reinterpret_cast<uintptr_t>(a.in[k]) & 15) == 0;
@@ -334,6 +337,10 @@ cudaError_t launch_rows(const dev::RowArgs& a, cudaStream_t stream) {
   }
   p.row_begin = a.row_begin;
   p.row_end = a.row_end;
+  if (!warp) {
+    CUfunction f = function(key, [&] { return rows_cta_source(a, tpr); }, vec ? "xt_rows_cv" : "xt_rows_cs");
+    return launch(f, dim3(grid_of(rows, 1)), tpr, stream, &p);
+  }
   CUfunction f = function(key, [&] { return rows_source(a); }, vec ? "xt_rows_v" : "xt_rows_s");
   return launch(f, dim3(grid_of(rows, kRowsPerCta)), 32 * kRowsPerCta, stream, &p);
 }

@@ -1,7 +1,7 @@
-// Scalar element operations of the compiled rows interpreter (the rows
-// programs too wide for the generated kernels): the xt unary and binary ops
-// on f32 values, dispatched on an opcode.  The arithmetic itself is
-// op_math.cuh's, shared with the kernels generated per program at run time.
+// Scalar element operations of the compiled kernels (the dedicated f32
+// add/sub/mul kernel): the xt unary and binary ops on f32 values, dispatched
+// on an opcode.  The arithmetic itself is op_math.cuh's, shared with the
+// kernels generated per program at run time.
 #pragma once
 
 #include <cuda_bf16.h>

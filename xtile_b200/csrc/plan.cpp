@@ -667,7 +667,6 @@ class Classifier {
     for (auto& kv : loads_) { bool s; check(kv.second, &s); }
     for (auto& s : stores_) { bool sc; check(s, &sc); }
     if (C < 0) unsupported("the program has no full-row tile");
-    if (C > 2048) unsupported("rows longer than 2048 elements are not supported");
     p.rows = std::min(grid_[axis] * tr, R);
     p.cols = C;
     p.tile_rows = tr;
@@ -772,6 +771,8 @@ class Classifier {
       unsupported("'" + n + "' is not supported in row programs");
     }
     if (p.code.size() > static_cast<size_t>(kMaxInstr)) unsupported("the program is too long");
+    if (row_cta_threads(C, std::max(p.n_vregs, 1)) == 0)
+      unsupported("the program's live rows of " + std::to_string(C) + " elements exceed a CTA's registers");
     p.softmax = is_softmax_chain(p);
     return p;
   }

@@ -106,6 +106,17 @@ struct ConvPlan {
   int n_axis = 0;                            // bid axis of the batch tile
 };
 
+// Threads per row of the generated one-CTA-per-row kernel for rows of
+// ``cols`` columns with ``n_v`` live rows: the fewest (128 to 1024, powers of
+// two) with which a thread holds at most 8 four-element groups (or 32
+// elements) of each live row; 0 when no CTA holds them.  The planner takes a
+// row program only when this is not 0.
+inline int row_cta_threads(int64_t cols, int n_v) {
+  for (int t = 128; t <= 1024; t *= 2)
+    if (n_v * ((cols + 4 * t - 1) / (4 * t)) <= 8 && n_v * ((cols + t - 1) / t) <= 32) return t;
+  return 0;
+}
+
 // --- tile -----------------------------------------------------------------------
 // Shapes are padded with leading 1s to rank 4 (tile and array rank agree).
 enum TileOpKind : uint8_t {
