@@ -19,6 +19,8 @@ Workloads are the BASELINE configurations (synthetic, seeded inputs):
                   kernels/matmul.py program (scale, bias, int8 out) at 8192^3
   col_sums        not a BASELINE configuration: a generated tile kernel
                   (column sums of 64 x 32 tiles of a 128 MiB f32 array)
+  softmax_wide    not a BASELINE configuration: kernels/softmax.py's program on
+                  [4096, 8192] (a generated kernel, one CTA per row)
   col_bias        not a BASELINE configuration: a generated tile kernel whose
                   elementwise ops run as one pass (sigmoid(t * c - c), c a
                   column broadcast over 32 x 64 tiles)
@@ -87,6 +89,7 @@ NCU_TRAFFIC_BYTES: dict[str, float] = {
     "row_center": 134_223_360 + 78_821_120,
     "col_sums": 134_223_360 + 4_445_056,
     "col_bias": 134_317_056 + 81_739_648,
+    "softmax_wide": 134_230_784 + 77_903_104,
 }
 
 
@@ -119,7 +122,7 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
                     unit="GB/s", dtype="f32", work=3 * 2048 * 2048 * 4,
                     config={"workload": "add", "shape": [2048, 2048], "block_tile": [32, 64],
                             "grid": [64, 32, 1]})
-    if name == "softmax":
+    if name in ("softmax", "softmax_wide"):
         @xt.kernel
         def softmax_rows(inp, out, trow, col):
             i = xt.bid(0)
@@ -128,6 +131,18 @@ def build_workload(name: str, xt, torch, world: int, rank: int):
             x = xt.exp(x)
             xt.store(out, index=(i, 0), tile=x / xt.sum(x, axis=-1))
 
+        if name == "softmax_wide":
+            # not a BASELINE configuration: the same program on rows wider
+            # than the dedicated kernel takes (a generated kernel, one CTA
+            # per row)
+            R, C = 4096, 8192
+            x = torch.randn(R, C, generator=g(12)) * 4
+            F = xt.float32
+            text = xt.trace_text(softmax_rows, args=(A((R, C), F), A((R, C), F), 1, C), grid=(R, 1, 1),
+                                 double_buffering=True)
+            return dict(text=text, inputs=[x], out_shape=(R, C), out_dtype=torch.float32, unit="GB/s", dtype="f32",
+                        work=2 * R * C * 4, tolerance="softmax",
+                        config={"workload": name, "shape": [R, C], "block_tile": [1, C], "grid": [R, 1, 1]})
         x = torch.randn(8192, 1024, generator=g(1)) * 4
         text = xt.trace_text(softmax_rows, args=(A((8192, 1024), xt.float32), A((8192, 1024), xt.float32),
                                                  1, 1024), grid=(8192, 1, 1), double_buffering=True)
@@ -857,7 +872,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="sharded_matmul",
                     choices=["add", "softmax", "matmul", "conv2d", "sharded_matmul", "transpose", "silu",
-                             "row_center", "row_bias", "matmul_i8", "col_sums", "col_bias"])
+                             "row_center", "row_bias", "matmul_i8", "col_sums", "col_bias", "softmax_wide"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference", "torch"],
                     help="b200: this backend; reference: the reference's CPU path; torch: the vendor library "
                          "(cuBLAS, cuDNN) through PyTorch on one GPU, for context")
@@ -1378,7 +1393,7 @@ def run_torch_library(args, torch) -> None:
     if name == "add":
         lib = "torch.add (out=)"
         fn = lambda i: torch.add(*sets[i % n_sets], out=outs[i % n_sets])  # noqa: E731
-    elif name == "softmax":
+    elif name in ("softmax", "softmax_wide"):
         lib = "torch.softmax"
         fn = lambda i: torch.softmax(sets[i % n_sets][0], -1)  # noqa: E731
     elif name in ("matmul", "sharded_matmul"):

@@ -80,13 +80,14 @@ def test_extra_workloads_plan_onto_their_families():
     import torch
     import xtile as xt
     fams = {name: xt.parse(bench.build_workload(name, bench.load_dsl(), torch, 1, 0)["text"]).plan()["family"]
-            for name in ("silu", "row_center", "row_bias", "transpose", "matmul_i8", "col_sums", "col_bias")}
+            for name in ("silu", "row_center", "row_bias", "transpose", "matmul_i8", "col_sums", "col_bias",
+                         "softmax_wide")}
     assert fams == {"silu": "ew", "row_center": "rows", "row_bias": "ew", "transpose": "tile", "matmul_i8": "gemm",
-                    "col_sums": "tile", "col_bias": "tile"}
+                    "col_sums": "tile", "col_bias": "tile", "softmax_wide": "rows"}
 
 
 @pytest.mark.parametrize("name", ["add", "softmax", "matmul", "conv2d", "sharded_matmul", "transpose", "silu",
-                                  "row_center", "row_bias", "matmul_i8", "col_sums", "col_bias"])
+                                  "row_center", "row_bias", "matmul_i8", "col_sums", "col_bias", "softmax_wide"])
 def test_configuration_work_matches_the_plan(name):
     # the reference arm takes the work from the configuration's formula; the
     # planner must count the same bytes / FLOP for the GPU arm
