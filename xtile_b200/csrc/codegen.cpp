@@ -322,11 +322,7 @@ void rows_body(std::ostringstream& s, const dev::RowArgs& a, bool vec, bool cta)
 
 }  // namespace
 
-bool rows_fit(const dev::RowArgs& a) {
-  // rows of at most 2048 columns whose live rows a lane holds in at most 160 values
-  const int64_t n_v = std::max(a.n_vregs, 1);
-  return a.cols <= 2048 && n_v * 4 * rows_pl4(a.cols) <= 160 && n_v * rows_pls(a.cols) <= 160;
-}
+bool rows_fit(const dev::RowArgs& a) { return row_warp_fits(a.cols, std::max(a.n_vregs, 1)); }
 
 std::string rows_cta_source(const dev::RowArgs& a, int tpr) {
   if (a.n_code <= 0 || a.n_code > kMaxInstr) fail("row program length");

@@ -1080,7 +1080,7 @@ std::string describe_plan(const Plan& p, int stage) {
     os << "\n";
   }
   if (stage >= 3 && (p.family == Family::Ew || p.family == Family::Rows)) {
-    // the register program the ew / rows kernels interpret
+    // the register program the ew / rows kernels are generated from
     static const char* kNames[] = {"?", "load", "store", "add", "sub", "mul", "exp", "cos", "sin",
                                    "recip", "rsqrt", "sigmoid", "tanh", "silu", "itof", "ftoi",
                                    "bcast_add", "bcast_sub", "bcast_mul", "rowmax", "rowsum",
@@ -1118,23 +1118,53 @@ std::string describe_plan(const Plan& p, int stage) {
       }
     }
   }
+  // rows: one warp per row up to 2048 columns while a lane holds the live
+  // rows in 160 values (the generated kernels' rule), else one CTA per row
+  const int n_v = std::max(p.rows.n_vregs, 1);
+  const int row_cta = p.family == Family::Rows && !row_warp_fits(p.rows.cols, n_v)
+                          ? row_cta_threads(p.rows.cols, n_v)
+                          : 0;
   if (stage >= 4) {
-    const char* threads = p.family == Family::Gemm || p.family == Family::Conv
-                              ? "warp 0 TMA producer, warp 1 tcgen05.mma issuer, warps 4-7 TMEM epilogue"
-                              : p.family == Family::Rows ? "one warp per row, 8 warps per CTA"
-                                                         : "grid-stride, 4 elements per thread per step";
+    std::string threads;
+    switch (p.family) {
+      case Family::Gemm:
+      case Family::Conv:
+        threads = "warp 0 TMA producer, MMA issuer warp(s), TMEM epilogue warps";
+        break;
+      case Family::Rows:
+        threads = row_cta ? "one CTA of " + std::to_string(row_cta) + " threads per row" : "one warp per row";
+        break;
+      case Family::Tile:
+        threads = "one CTA per Block, loops of its threads over each op's tile";
+        break;
+      default:
+        threads = "grid-stride, 8 elements per thread per step";
+    }
     os << "  //   nova_threading -> " << threads << "\n";
   }
   if (stage >= 5) {
     const char* sync = p.family == Family::Gemm || p.family == Family::Conv
                            ? "mbarrier ring (full/empty per stage) + TMEM full/empty, bounded waits"
-                           : "none (blocks are independent)";
+                       : p.family == Family::Tile ? "CTA barriers between ops that share shared memory"
+                       : row_cta ? "CTA barriers in the row reductions"
+                                 : "none (blocks are independent)";
     os << "  //   nova_barrier -> " << sync << "\n";
   }
   if (stage >= 6) {
-    const char* mem = p.family == Family::Gemm ? "4 smem stages of A 128x64 + B 64x256 (192 KiB), TMEM 512 columns"
-                      : p.family == Family::Conv ? "smem ring of shifted input tiles + resident filter, TMEM accumulator"
-                                                 : "registers only";
+    std::string mem;
+    switch (p.family) {
+      case Family::Gemm:
+        mem = "4 smem stages of A 128x64 + B 64x256 (192 KiB), TMEM 512 columns";
+        break;
+      case Family::Conv:
+        mem = "smem ring of shifted input tiles + resident filter, TMEM accumulator";
+        break;
+      case Family::Tile:
+        mem = "tile slots in " + std::to_string((p.tile.smem_floats * 4 + 1023) / 1024) + " KiB of shared memory";
+        break;
+      default:
+        mem = "registers only";
+    }
     os << "  //   nova_allocate -> " << mem << "\n";
   }
   if (stage >= 7) os << "  //   nova_to_x1 -> launch via xt_launch (sm_100a)\n";

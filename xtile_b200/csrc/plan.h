@@ -106,6 +106,13 @@ struct ConvPlan {
   int n_axis = 0;                            // bid axis of the batch tile
 };
 
+// Whether a row program runs the generated one-warp-per-row kernel: rows of
+// at most 2048 columns whose ``n_v`` live rows a lane holds in at most 160
+// values (float4 groups, or elements when the rows are not whole groups).
+inline bool row_warp_fits(int64_t cols, int n_v) {
+  return cols <= 2048 && n_v * 4 * (((cols + 3) / 4 + 31) / 32) <= 160 && n_v * ((cols + 31) / 32) <= 160;
+}
+
 // Threads per row of the generated one-CTA-per-row kernel for rows of
 // ``cols`` columns with ``n_v`` live rows: the fewest (128 to 1024, powers of
 // two) with which a thread holds at most 8 four-element groups (or 32
