@@ -33,6 +33,11 @@ the result copied out inside the timed region.  ``--impl reference`` times the
 reference path on the host CPU instead: the reference (sjjeong94/xtile)
 executes nothing, so its arm is the CPU oracle restating its semantics
 (``oracle/xt_oracle.py``) on a bounded sample of the workload.
+
+On one GPU the default line also carries ``per_config`` (BASELINE
+configurations 1-4) and ``generated`` (one workload of each kind of kernel
+generated per program: silu, row_center, softmax_wide, col_bias), each timed,
+put against its roofline and checked against the oracle on sampled Blocks.
 """
 from __future__ import annotations
 
@@ -743,12 +748,15 @@ def gpu_id_of(dev, torch) -> str:
 
 
 PER_CONFIG = ("add", "softmax", "matmul", "conv2d")
+# kernels generated per program (not BASELINE configurations), one of each
+# kind: elementwise, rows (a CTA per row), tile (a fused elementwise run)
+GENERATED = ("silu", "row_center", "softmax_wide", "col_bias")
 
 
 def run_per_config(xt, torch, dev, peaks: dict, peak_kind: str, steps: int = 50, warmup: int = 5,
-                   region_ms: float = 60.0) -> dict:
-    """BASELINE configurations 1-4 on one GPU, each timed like the headline's
-    graph mode (K launches in a CUDA graph over rotating buffer sets, events
+                   region_ms: float = 60.0, names=PER_CONFIG) -> dict:
+    """BASELINE configurations 1-4 (or the workloads ``names``) on one GPU,
+    each timed like the headline's graph mode (K launches in a CUDA graph over rotating buffer sets, events
     inside the graph), replayed for about ``region_ms`` with the clocks
     sampled, then checked on a seeded sample of Blocks against the oracle.
 
@@ -757,7 +765,7 @@ def run_per_config(xt, torch, dev, peaks: dict, peak_kind: str, steps: int = 50,
     milliseconds of the 4096^3 GEMM already meets the 1000 W cap (measured:
     1432 MHz median SM clock over 300 ms, 0.89 of the sustained GEMM peak)."""
     out = {}
-    for name in PER_CONFIG:
+    for name in names:
         w = build_workload(name, load_dsl(), torch, 1, 0)
         mod = xt.parse(w["text"])
         plan = mod.plan()
@@ -889,7 +897,8 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-per-config", action="store_true",
-                    help="skip configurations 1-4 beside the default (sharded_matmul) line on one GPU")
+                    help="skip configurations 1-4 and the generated-kernel workloads beside the default "
+                         "(sharded_matmul) line on one GPU")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -1361,8 +1370,10 @@ def main() -> None:
                        "ms_per_step": round(e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                        "pipelining": e_note}
     if world == 1 and args.workload == "sharded_matmul" and not args.no_per_config:
-        # BASELINE configurations 1-4, one GPU each, beside the headline
+        # BASELINE configurations 1-4, one GPU each, beside the headline; then
+        # one workload of each kind of generated kernel
         line["per_config"] = run_per_config(xt, torch, dev, peaks, peak_kind)
+        line["generated"] = run_per_config(xt, torch, dev, peaks, peak_kind, names=GENERATED)
     if not args.no_cpu and world == 1:  # the host-core baseline is a 1-GPU figure
         line["cpu_baseline"] = cpu_baseline(w, torch)
     print(json.dumps(line), flush=True)
