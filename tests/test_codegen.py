@@ -25,9 +25,9 @@ def compiles(mod):
     return native.compile_generated(generated(mod)) > 0
 
 
-@pytest.mark.parametrize("seed", range(36))
-def test_random_program_compiles(seed):
-    prog, R, C, tm, tn = random_program(seed)
+@pytest.mark.parametrize("seed,wide", [(s, False) for s in range(36)] + [(s, True) for s in range(24)])
+def test_random_program_compiles(seed, wide):
+    prog, R, C, tm, tn = random_program(seed, wide)
     F = xt.float32
     m = xt.convert(prog, args=(A((R, C), F), A((R, C), F), A((1, C), F), A((R, C), F), A((R, C), F), tm, tn),
                    grid=(-(-R // tm), C // tn, 1), double_buffering=True)
