@@ -849,10 +849,8 @@ std::string tile_source(const dev::TileArgs& a, int th) {
   s << "#define xt_red_f64 reinterpret_cast<double*>(xt_sm + " << red_offset(a) << ")\n"
     << "#define xt_red_f32 (xt_sm + " << red_offset(a) << ")\n";
   const std::vector<bool> compact = compact_values(a);
-  auto tile_geom = [&](const TileVal& v) {
-    const int idx = static_cast<int>(&v - a.vals);
-    return xt::jit::tile_geom(v, compact[idx]);
-  };
+  // a value's layout (its planned slot, rows unpadded when compact)
+  auto value_geom = [&](int v) { return tile_geom(a.vals[v], compact[v]); };
   s << "template <bool V>\n__device__ __forceinline__ void xt_tile_body(const XtTileArgs& p) {\n"
        "  const int t = threadIdx.x;\n"
        "  const xt_i64 b0 = p.bid0_begin + blockIdx.x, b1 = blockIdx.y, b2 = blockIdx.z;\n"
@@ -885,7 +883,7 @@ std::string tile_source(const dev::TileArgs& a, int th) {
   };
   std::vector<Span> rd, wr;
   auto span = [&](int v) {
-    const TileGeom g = tile_geom(a.vals[v]);
+    const TileGeom g = value_geom(v);
     return Span{g.off, g.off + g.rows() * g.st[2]};
   };
   const Span scratch{red_offset(a), red_offset(a) + 2 * th};
@@ -941,7 +939,7 @@ std::string tile_source(const dev::TileArgs& a, int th) {
     s << "  {  // op " << o << "\n";
     switch (op.kind) {
       case kTLoad: {
-        const TileGeom v = tile_geom(a.vals[op.dst]);
+        const TileGeom v = value_geom(op.dst);
         const Access g = access_of(a, op, v, o);
         s << g.decl << "    const xt_i64 gb = " << g.base << ";\n";
         if (g.vec) {
@@ -954,11 +952,11 @@ std::string tile_source(const dev::TileArgs& a, int th) {
         break;
       }
       case kTStore: {
-        const TileGeom v = tile_geom(a.vals[op.a]);
+        const TileGeom v = value_geom(op.a);
         const Access g = access_of(a, op, v, o);
         int64_t rd[kTileRank], rd_off;
         if (op.code == 1) {
-          const TileGeom src = tile_geom(a.vals[op.b]);
+          const TileGeom src = value_geom(op.b);
           rd_off = src.off;
           for (int d = 0; d < kTileRank; ++d) rd[d] = src.st[op.perm[d]];
         } else {
@@ -976,7 +974,7 @@ std::string tile_source(const dev::TileArgs& a, int th) {
         break;
       }
       case kTReduce: {
-        const TileGeom d = tile_geom(a.vals[op.dst]), x = tile_geom(a.vals[op.a]);
+        const TileGeom d = value_geom(op.dst), x = value_geom(op.a);
         if (op.axis >= kTileRank) fail("reduction axis");
         const int64_t n = x.s[op.axis], step = x.st[op.axis], outs = d.rows() * d.s[3];
         const bool sum = op.code != 0;
@@ -1044,7 +1042,7 @@ std::string tile_source(const dev::TileArgs& a, int th) {
         break;
       }
       case kTReshape: {
-        const TileGeom d = tile_geom(a.vals[op.dst]), x = tile_geom(a.vals[op.a]);
+        const TileGeom d = value_geom(op.dst), x = value_geom(op.a);
         std::ostringstream b;
         b << "        const int e = q * " << d.s[3] << " + cv;\n"
           << "        xt_sm[" << d.off << " + q * " << d.st[2] << " + cv] = xt_sm[" << x.off << " + e / " << x.s[3]
@@ -1053,7 +1051,7 @@ std::string tile_source(const dev::TileArgs& a, int th) {
         break;
       }
       case kTPermute: {
-        const TileGeom d = tile_geom(a.vals[op.dst]), x = tile_geom(a.vals[op.a]);
+        const TileGeom d = value_geom(op.dst), x = value_geom(op.a);
         // dst dim k is src dim perm[k]
         int64_t ss[kTileRank];
         for (int k = 0; k < kTileRank; ++k) ss[k] = x.st[op.perm[k]];
