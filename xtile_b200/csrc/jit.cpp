@@ -9,9 +9,14 @@
 // (with the reason); there is no fallback.
 #include <cuda.h>
 #include <dlfcn.h>
+#include <sys/stat.h>
+#include <unistd.h>
 
+#include <cerrno>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <fstream>
 #include <map>
 #include <memory>
 #include <mutex>
@@ -33,6 +38,7 @@ typedef int (*SizeFn)(void*, size_t*);
 typedef int (*GetFn)(void*, char*);
 typedef int (*DestroyFn)(void**);
 typedef const char* (*ErrStrFn)(int);
+typedef int (*VersionFn)(int*, int*);
 
 struct Nvrtc {
   CreateFn create = nullptr;
@@ -41,6 +47,7 @@ struct Nvrtc {
   GetFn cubin = nullptr, log = nullptr;
   DestroyFn destroy = nullptr;
   ErrStrFn err = nullptr;
+  VersionFn version = nullptr;
   std::string why;  // empty when loaded
 };
 
@@ -67,6 +74,7 @@ const Nvrtc& nvrtc() {
     r.log = reinterpret_cast<GetFn>(dlsym(h, "nvrtcGetProgramLog"));
     r.destroy = reinterpret_cast<DestroyFn>(dlsym(h, "nvrtcDestroyProgram"));
     r.err = reinterpret_cast<ErrStrFn>(dlsym(h, "nvrtcGetErrorString"));
+    r.version = reinterpret_cast<VersionFn>(dlsym(h, "nvrtcVersion"));
     if (!r.create || !r.compile || !r.cubin_size || !r.cubin || !r.log_size || !r.log || !r.destroy || !r.err)
       r.why = "NVRTC is missing an entry point";
     return r;
@@ -109,6 +117,48 @@ std::string cu_error(CUresult r) {
   return s ? s : ("CUresult " + std::to_string(static_cast<int>(r)));
 }
 
+// ------------------------------------------------------------------ disk cache
+// Compiled cubins persist across processes in a directory: XT_JIT_CACHE_DIR,
+// else $XDG_CACHE_HOME/xtile_b200, else ~/.cache/xtile_b200; XT_JIT_CACHE=0
+// turns the cache off.  A file is named by two independent 64-bit hashes of
+// the source, the NVRTC version and the compile options, and starts with the
+// lengths of that key and of the cubin, which a read checks; it is written,
+// checked, to a temporary name
+// and renamed, so processes that compile the same program at once (ranks)
+// each see a whole file.  Any failure to read or write the cache only means
+// a compile.
+std::string cache_dir() {
+  static const std::string dir = [] {
+    const char* off = std::getenv("XT_JIT_CACHE");
+    if (off && std::strcmp(off, "0") == 0) return std::string();
+    if (const char* d = std::getenv("XT_JIT_CACHE_DIR")) return std::string(d);
+    if (const char* x = std::getenv("XDG_CACHE_HOME")) return std::string(x) + "/xtile_b200";
+    if (const char* h = std::getenv("HOME")) return std::string(h) + "/.cache/xtile_b200";
+    return std::string();
+  }();
+  return dir;
+}
+
+// FNV-1a over ``s`` from ``h``
+uint64_t fnv1a(const std::string& s, uint64_t h) {
+  for (unsigned char c : s) {
+    h ^= c;
+    h *= 1099511628211ull;
+  }
+  return h;
+}
+
+bool make_dirs(const std::string& dir) {
+  for (size_t i = 1; i <= dir.size(); ++i)
+    if (i == dir.size() || dir[i] == '/') {
+      const std::string part = dir.substr(0, i);
+      if (mkdir(part.c_str(), 0755) != 0 && errno != EEXIST) return false;
+    }
+  return true;
+}
+
+std::string cached_compile(const std::string& source);
+
 // ------------------------------------------------------------------ cache
 struct Program {
   std::string cubin;
@@ -142,7 +192,7 @@ CUfunction function(const std::string& key, Make make, const char* name, int sme
   auto it = g_programs.find(key);
   if (it == g_programs.end()) {
     auto p = std::make_unique<Program>();
-    p->cubin = compile(make());
+    p->cubin = cached_compile(make());
     it = g_programs.emplace(key, std::move(p)).first;
   }
   Program& p = *it->second;
@@ -277,6 +327,48 @@ std::string compile(const std::string& source) {
   n.destroy(&prog);
   return cubin;
 }
+
+namespace {
+
+std::string cached_compile(const std::string& source) {
+  const std::string dir = cache_dir();
+  if (dir.empty()) return compile(source);
+  const Nvrtc& n = nvrtc();
+  int major = 0, minor = 0;
+  if (n.version) n.version(&major, &minor);
+  const std::string key = source + "\n// nvrtc " + std::to_string(major) + "." + std::to_string(minor) +
+                          " -arch=sm_100a -std=c++17 -lineinfo";
+  char name[48];
+  std::snprintf(name, sizeof name, "%016llx%016llx.cubin",
+                static_cast<unsigned long long>(fnv1a(key, 14695981039346656037ull)),
+                static_cast<unsigned long long>(fnv1a(key, 0x9e3779b97f4a7c15ull)));
+  const std::string path = dir + "/" + name;
+  {
+    std::ifstream in(path, std::ios::binary);
+    uint64_t len[2] = {0, 0};
+    if (in && in.read(reinterpret_cast<char*>(len), sizeof len) && len[0] == key.size() && len[1] > 0) {
+      std::string cubin((std::istreambuf_iterator<char>(in)), std::istreambuf_iterator<char>());
+      if (cubin.size() == len[1]) return cubin;
+    }
+  }
+  std::string cubin = compile(source);
+  if (make_dirs(dir)) {
+    const std::string tmp = path + ".tmp." + std::to_string(getpid());
+    bool ok = false;
+    {
+      std::ofstream out(tmp, std::ios::binary | std::ios::trunc);
+      const uint64_t len[2] = {key.size(), cubin.size()};
+      out.write(reinterpret_cast<const char*>(len), sizeof len);
+      out.write(cubin.data(), static_cast<std::streamsize>(cubin.size()));
+      out.flush();
+      ok = out.good();
+    }
+    if (!ok || std::rename(tmp.c_str(), path.c_str()) != 0) std::remove(tmp.c_str());
+  }
+  return cubin;
+}
+
+}  // namespace
 
 cudaError_t launch_ew(const dev::EwArgs& a, cudaStream_t stream) {
   const int64_t n = a.end - a.begin;
