@@ -88,7 +88,7 @@ NCU_TRAFFIC_BYTES: dict[str, float] = {
     "add": 33_561_088 + 10_496,
     "softmax": 33_566_464 + 343_552,
     "sharded_matmul": 6_210_000_000 + 1_060_000_000,
-    "transpose": 134_227_712 + 88_921_088,
+    "transpose": 134_243_200 + 82_835_968,
     "matmul_i8": 215_210_496 + 55_281_408,
     "silu": 134_240_512 + 84_709_376,
     "row_center": 134_223_360 + 78_821_120,

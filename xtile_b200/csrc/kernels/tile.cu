@@ -29,7 +29,10 @@ namespace xt {
 namespace dev {
 namespace {
 
-constexpr int kTileThreads = 256;
+// Data-movement CTA width: the transpose of [8, 2048, 2048] f32 in 32 x 64
+// tiles measured 5250 GB/s with 64 threads, 6048 with 128 and 5090 with 256
+// (128: four 16-byte loads in flight per thread and up to 16 CTAs per SM).
+constexpr int kTileThreads = 128;
 
 // ---------------------------------------------------------------------------
 // Pure data movement: the program is one row-tile load and one store of that
